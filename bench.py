@@ -1,0 +1,328 @@
+"""Benchmark of the fused DeltaNet decode layer (one token per sequence).
+
+Workload: a Gated DeltaNet layer with hidden 4096, 16 k-heads, 32 v-heads,
+head_dim 128, Q4_K in-projection 4096 -> 12352 and out-projection 4096 ->
+4096, width-4 causal conv, fp32 recurrent state [B, 32, 128, 128]; B
+independent sequences per GPU (default 64). A step is one decode step of the
+layer for the B sequences: li_launch_deltanet_layer_decode (in-projection +
+conv, recurrence + gated RMSNorm, out-projection). Inputs are seeded
+synthetic (random-code Q4_K weights, see leaninfer_b200/synth.py).
+
+Multi-GPU: one process per GPU (torchrun); sequences shard across ranks with
+no data-path communication (weak scaling: B sequences per rank); the time is
+the max over ranks of the CUDA-event time.
+
+L2 hygiene: steps rotate over several independent layer instances (weights
+and states) so that consecutive uses of one instance are separated by more
+than 3x the L2 capacity of traffic.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+HIDDEN, HK, HV, D = 4096, 16, 32, 128
+CONV_CH = 2 * HK * D + HV * D
+N_IN = CONV_CH + HV * D + 2 * HV
+METRIC = "fused-layer decode tokens/s"
+UNIT = "tokens/s"
+
+
+def algorithmic_bytes(batch: int) -> int:
+    """Bytes a step must move at least once: both weight matrices (Q4_K), the
+    conv weights, and per sequence the recurrent state and conv state read
+    and written plus x in and y out."""
+    w_in = N_IN * (HIDDEN // 256) * 144
+    w_out = HIDDEN * (HV * D // 256) * 144
+    conv_w = CONV_CH * 4 * 4
+    small = (2 * HV + D) * 4
+    per_seq = HV * D * D * 4 * 2 + CONV_CH * 3 * 4 * 2 + HIDDEN * 4 * 2
+    return w_in + w_out + conv_w + small + batch * per_seq
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+# --------------------------------------------------------------------------
+# clocks sampled during the timed region
+# --------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows: list[tuple[float, list[str]]] = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append((time.time(), [c.strip() for c in line.split(",")]))
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self, t0: float, t1: float) -> dict:
+        rows = [r for t, r in self.rows if t0 <= t <= t1] or [r for _, r in self.rows]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[3:7]) if v.lower().startswith("active")})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------
+# our arm
+# --------------------------------------------------------------------------
+def build_instances(dev, batch: int, n_inst: int, seed: int):
+    import torch
+    from leaninfer_b200 import ops, synth
+    insts = []
+    for i in range(n_inst):
+        r = np.random.Generator(np.random.PCG64(seed * 1000 + i))
+        w = synth.deltanet_layer(r, hidden=HIDDEN, n_k_heads=HK, n_v_heads=HV, head_dim=D, wtype=synth.Q4_K)
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+        layer = ops.DeltaNetLayerDecode(hidden=HIDDEN, n_k_heads=HK, n_v_heads=HV, head_dim=D, w_in=t(w["w_in"]),
+                                        conv_w=t(w["conv_w"]), a_log=t(w["a_log"]), dt_bias=t(w["dt_bias"]),
+                                        norm_w=t(w["norm_w"]), w_out=t(w["w_out"]))
+        inp = synth.deltanet_inputs(r, batch, w)
+        state = torch.empty(batch, HV, D, D, device=dev)
+        # state ~ N(0, 0.02), drawn on the device (268 MB per instance at B=64)
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed * 1000 + i)
+        state.normal_(0.0, 0.02, generator=g)
+        insts.append(dict(layer=layer, x=t(inp["x"]), y=torch.empty(batch, HIDDEN, device=dev),
+                          conv_state=t(inp["conv_state"]), state=state,
+                          ws=torch.empty(layer.workspace_bytes(batch), device=dev, dtype=torch.uint8)))
+    return insts
+
+
+def run_ours(args, rank: int, world: int, dist) -> dict | None:
+    import torch
+    from leaninfer_b200 import ops
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    B = args.batch
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    per_inst = algorithmic_bytes(B)
+    n_inst = max(2, math.ceil(3 * l2 / per_inst) + 1)
+    insts = build_instances(dev, B, n_inst, seed=rank + 1)
+    stream = torch.cuda.current_stream()
+
+    def step(i: int):
+        it = insts[i % n_inst]
+        it["layer"].step(it["x"], it["y"], it["conv_state"], it["state"], workspace=it["ws"])
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    sampler = ClockSampler(dev.index)
+    sampler.start()
+    time.sleep(0.3)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t_wall0 = time.time()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    if dist:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    sampler.stop()
+    clocks = sampler.summary(t_wall0, t_wall1)
+    status = ops.device_status()
+    if status:
+        raise RuntimeError(f"device status {status} after the timed region")
+
+    # e2e through the public entry with host buffers: pinned x in, y out each step
+    hx = [torch.empty(B, HIDDEN, pin_memory=True) for _ in range(n_inst)]
+    hy = [torch.empty(B, HIDDEN, pin_memory=True) for _ in range(n_inst)]
+    for i in range(n_inst):
+        hx[i].copy_(insts[i]["x"].cpu())
+    e_steps = max(1, min(args.steps, 200))
+
+    def e2e_step(i: int):
+        it = insts[i % n_inst]
+        it["x"].copy_(hx[i % n_inst], non_blocking=True)
+        it["layer"].step(it["x"], it["y"], it["conv_state"], it["state"], workspace=it["ws"])
+        hy[i % n_inst].copy_(it["y"], non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0.record(stream)
+    for i in range(e_steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if dist:
+        dist.barrier()
+
+    times = torch.tensor([ms, e2e_ms], device=dev, dtype=torch.float64)
+    if dist:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = float(times[0]), float(times[1])
+    if rank != 0:
+        return None
+
+    peaks = measured_peaks()
+    step_s = ms / 1e3 / args.steps
+    achieved = algorithmic_bytes(B) / step_s / 1e9
+    value = world * B * args.steps / (ms / 1e3)
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (Q4_K weights)", "data": "synthetic",
+        "config": {"workload": "deltanet_layer_decode_q4k", "batch_per_gpu": B, "global_batch": B * world,
+                   "hidden": HIDDEN, "k_heads": HK, "v_heads": HV, "head_dim": D, "weights": "Q4_K",
+                   "parallelism": f"sequence-sharded x{world}, no collectives",
+                   "l2": f"inputs larger than L2: rotating {n_inst} layer instances of {per_inst / 1e6:.1f} MB"},
+        "roofline": {"bound": "hbm", "kernel": "deltanet layer decode (3 PDL-chained kernels per step)",
+                     "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
+                     "algorithmic_bytes_per_step": algorithmic_bytes(B), "traffic": args.traffic},
+        "e2e": {"value": round(world * B * e_steps / (e2e_ms / 1e3), 1), "unit": UNIT,
+                "h2d_bytes_per_step": B * HIDDEN * 4, "d2h_bytes_per_step": B * HIDDEN * 4},
+        "gpu_launches": 3 * args.steps,
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(B, args.cpu_steps)
+    return line
+
+
+# --------------------------------------------------------------------------
+# CPU legs: the oracle (the C restatement of the path) on the host cores
+# --------------------------------------------------------------------------
+def cpu_baseline(batch: int, steps: int) -> dict:
+    from leaninfer_b200 import synth
+    from oracle import oracle
+    r = np.random.Generator(np.random.PCG64(7))
+    w = synth.deltanet_layer(r, hidden=HIDDEN, n_k_heads=HK, n_v_heads=HV, head_dim=D, wtype=synth.Q4_K)
+    L, keep = oracle.make_layer(w)
+    inp = synth.deltanet_inputs(r, batch, w)
+    cs, st = inp["conv_state"], inp["state"]
+    oracle.deltanet_layer_decode(L, keep, inp["x"], cs, st)        # warm-up
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        oracle.deltanet_layer_decode(L, keep, inp["x"], cs, st)
+    dt = time.perf_counter() - t0
+    return {"value": round(batch * steps / dt, 2), "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"{steps} decode steps of the same layer at batch {batch} (oracle/li_oracle.c, "
+                      f"double accumulation, {oracle.num_threads()} host threads)",
+            "seconds": round(dt, 3)}
+
+
+def run_reference(args, rank: int) -> dict | None:
+    if rank != 0:
+        return None
+    cb = cpu_baseline(args.batch, max(1, args.steps if args.steps <= 8 else 8))
+    return {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": 0,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64 accumulation (Q4_K weights)", "data": "synthetic",
+            "config": {"workload": "deltanet_layer_decode_q4k", "batch_per_gpu": args.batch, "hidden": HIDDEN,
+                       "k_heads": HK, "v_heads": HV, "head_dim": D, "weights": "Q4_K",
+                       "note": "the reference's ggml CPU ops are not vendored; its CPU path is the C oracle port"},
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-steps", type=int, default=4)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--traffic", type=float, default=None, help="ncu DRAM bytes per step, if captured")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        line = run_reference(args, rank)
+        if line:
+            print(json.dumps(line), flush=True)
+        return
+
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as tdist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist = tdist
+    from leaninfer_b200 import _lib, build
+    if not _lib.LIB_PATH.exists():
+        if rank == 0:
+            build.build()
+        if dist:
+            dist.barrier()
+    _lib.load()
+    try:
+        line = run_ours(args, rank, world, dist)
+    finally:
+        if dist:
+            dist.destroy_process_group()
+    if line:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,274 @@
+#pragma once
+
+/*
+ * LeanInfer fused-kernel C ABI, B200 (sm_100a) implementation.
+ *
+ * Drop-in for the reference header cuda/leaninfer-cuda.h: the five reference
+ * entry points keep their exact names, argument lists and `void` returns, and
+ * the header keeps the reference's dual shape (real declarations only when
+ * GGML_USE_CUDA or GGML_USE_CUBLAS is defined, static no-op stubs otherwise;
+ * reference cuda/leaninfer-cuda.h:16 and :54-76).
+ *
+ * Everything below the "additive entries" line is new. New entries return an
+ * int status: 0 on success, a cudaError_t value for a CUDA failure, or one of
+ * the LI_ERR_* codes for an argument the kernels do not accept.
+ *
+ * Conventions shared by all entries:
+ *   - every pointer is device memory owned by the caller (ggml tensors);
+ *     no entry allocates or frees device memory;
+ *   - every launch is stream-ordered on `stream` (a cudaStream_t passed as
+ *     void*, as in the reference), performs no synchronisation and no host
+ *     allocation, and may be captured into a CUDA graph;
+ *   - quantized weights are raw ggml blocks, one matrix row after another
+ *     (row r of a [N, K] matrix starts at r * li_row_bytes(type, K));
+ *   - activations are fp32, row-major [n_rows, K].
+ */
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ggml type ids, so a ggml dispatch can pass src0->type unchanged. */
+enum li_wtype {
+    LI_WTYPE_F32  = 0,
+    LI_WTYPE_F16  = 1,
+    LI_WTYPE_Q8_0 = 8,   /* 32 values per 34-byte block: fp16 d, 32 x int8   */
+    LI_WTYPE_Q4_K = 12   /* 256 values per 144-byte block: fp16 d, fp16 dmin,
+                            12 bytes of 6-bit scales/mins, 128 bytes of nibbles */
+};
+
+/* Status codes of the new entries (above every cudaError_t value). */
+#define LI_OK                 0
+#define LI_ERR_BAD_ARG        2001  /* null pointer, non-positive size      */
+#define LI_ERR_BAD_SHAPE      2002  /* K not a multiple of the block size,
+                                       or a size beyond what a kernel takes */
+#define LI_ERR_UNSUPPORTED    2003  /* weight type / head_dim not built     */
+#define LI_ERR_WORKSPACE      2004  /* workspace missing or too small       */
+#define LI_ERR_MISALIGNED     2005  /* pointer not 16-byte aligned          */
+#define LI_ERR_TIMEOUT        2006  /* a bounded device-side wait gave up   */
+#define LI_ERR_NO_CUDA        2007  /* built without CUDA (stub branch)     */
+
+/*
+ * Recurrent DeltaNet layer for the fused decode entry. One layer's weights
+ * and shapes; the per-sequence states live in caller buffers passed at launch.
+ *
+ * In-projection rows, in order (n_rows_in = 2*Hk*D + 2*Hv*D + 2*Hv):
+ *   q [Hk*D] | k [Hk*D] | v [Hv*D] | z [Hv*D] | beta [Hv] | alpha [Hv]
+ * Per step and sequence:
+ *   p      = W_in . rmsnorm?(x)                (rmsnorm only if in_norm_w)
+ *   c      = silu(causal_conv1d(p[q|k|v], conv_state, conv_w))  width 4
+ *   q, k   = l2norm(c_q), l2norm(c_k) per k-head; q *= head_dim^-1/2
+ *   beta   = sigmoid(p_beta)
+ *   g      = -exp(a_log) * softplus(p_alpha + dt_bias)     (decay = e^g)
+ *   S, o   = gated delta rule on S [D(k), D(v)] per v-head (see
+ *            li_launch_deltanet_recurrent_f32)
+ *   y      = W_out . ( silu(z) * rmsnorm(o) * norm_w )  per v-head rows
+ */
+typedef struct li_deltanet_layer {
+    int   hidden;        /* model width K of W_in, rows of W_out        */
+    int   n_k_heads;     /* Hk                                          */
+    int   n_v_heads;     /* Hv, a multiple of Hk                        */
+    int   head_dim;      /* D; 128 is the only built size               */
+    int   conv_kernel;   /* 4 is the only built size                    */
+    int   repeat_type;   /* 0: v-head h uses k-head h/(Hv/Hk);
+                            1: v-head h uses k-head h % Hk               */
+    int   w_in_type;     /* LI_WTYPE_Q4_K or LI_WTYPE_Q8_0              */
+    int   w_out_type;    /* LI_WTYPE_Q4_K or LI_WTYPE_Q8_0              */
+    float in_norm_eps;   /* eps of the optional input RMSNorm           */
+    float norm_eps;      /* eps of the gated RMSNorm                    */
+    float l2_eps;        /* eps of the q/k L2 normalisation             */
+    const float *in_norm_w; /* [hidden] or NULL: no input RMSNorm       */
+    const void  *w_in;      /* [n_rows_in, hidden] quantized rows        */
+    const float *conv_w;    /* [2*Hk*D + Hv*D, conv_kernel]; tap
+                               conv_kernel-1 multiplies the new input    */
+    const float *a_log;     /* [Hv]                                      */
+    const float *dt_bias;   /* [Hv]                                      */
+    const float *norm_w;    /* [D] gamma of the gated RMSNorm            */
+    const void  *w_out;     /* [hidden, Hv*D] quantized rows             */
+} li_deltanet_layer;
+
+#if defined(GGML_USE_CUDA) || defined(GGML_USE_CUBLAS)
+
+/* ======================================================================
+ * Reference entries (reference cuda/leaninfer-cuda.h:19-52), unchanged
+ * signatures. Errors are recorded for li_get_last_error().
+ * ====================================================================== */
+
+/* dst[r][n] = sum_k rmsnorm(x[r])[k] * W[n][k], fp32 W [N, K].
+ * Replaces reference cuda/leaninfer-fused-ffn.cu:259-268 (one row of x). */
+void li_launch_fused_rms_norm_matmul_f32(
+        const float * x, const float * gamma, const float * W,
+        float * dst, int K, int N, float eps, void * stream);
+
+/* hidden[n] = silu(<x_norm, W_gate[n]>) * <x_norm, W_up[n]>, fp32 weights.
+ * Replaces reference cuda/leaninfer-fused-ffn.cu:270-280. */
+void li_launch_fused_rms_norm_swiglu_f32(
+        const float * x, const float * gamma,
+        const float * W_gate, const float * W_up,
+        float * hidden, int K, int N, float eps, void * stream);
+
+/* Same with fp16 weights (const void* = half[N*K]); x_norm is rounded to
+ * fp16 before the dot, as in reference cuda/leaninfer-fused-ffn.cu:230.
+ * Replaces reference cuda/leaninfer-fused-ffn.cu:282-292. */
+void li_launch_fused_rms_norm_swiglu_f16(
+        const float * x, const float * gamma,
+        const void  * W_gate, const void  * W_up,
+        float * hidden, int K, int N, float eps, void * stream);
+
+/* dst[r][k] = silu(z[r][k]) * output[r][k] * gamma[k] * rsqrt(mean(output[r]^2)+eps).
+ * Replaces reference cuda/leaninfer-fused-gate.cu:92-99. */
+void li_launch_fused_rms_norm_silu_gate_f32(
+        const float * output, const float * z, const float * gamma,
+        float * dst, int K, int n_rows, float eps, void * stream);
+
+/* Gated delta-rule recurrence over n_tokens with the reference layouts
+ * (reference cuda/leaninfer-fused-deltanet.cu:331-366):
+ *   q, k  [n_seqs][n_heads/gqa][n_tokens][D]; v addressed with element
+ *   strides vnb1 (token), vnb2 (head), vnb3 (seq); g, beta [n_seqs][n_tokens][n_heads];
+ *   state_in [n_seqs][n_heads][D(k)][D(v)];
+ *   dst = per-head outputs [n_seqs][n_tokens][n_heads][D], followed by the
+ *   final state in the state_in layout.
+ * proj_out [hidden_dim][n_tokens] receives sum over seqs and heads of
+ * W_out[d][h*D + j] * o[h][j] (W_out fp32 [hidden_dim, n_heads*D]); it is
+ * zeroed first. head_dim 128 and 64 are built; any other value records
+ * LI_ERR_UNSUPPORTED. */
+void li_launch_fused_deltanet_recurrent_out_f32(
+        const float * q, const float * k, const float * v,
+        const float * g, const float * beta, const float * state_in,
+        const float * W_out,
+        float * dst, float * proj_out,
+        int64_t head_dim, int64_t n_tokens, int64_t n_heads,
+        int64_t gqa_ratio, int repeat_type, int64_t n_seqs,
+        int64_t hidden_dim,
+        size_t vnb1, size_t vnb2, size_t vnb3,
+        void * stream);
+
+/* RMSNorm + three fp32 projections sharing one normalised x:
+ * dst_ptrs[i][n] = <rmsnorm(x), W_ptrs[i][n]>, i = 0..2, each W [N_OUT, K].
+ * W_ptrs and dst_ptrs are HOST arrays of three device pointers (read at
+ * launch, so the launch can be graph-captured). The reference exports this
+ * symbol as a stub (reference cuda/leaninfer-fused-deltanet.cu:306-327). */
+void li_launch_fused_rms_norm_qkv_f32(
+        const float * x, const float * gamma,
+        const float * const * W_ptrs,
+        float * const * dst_ptrs,
+        int K, int N_OUT, float eps, void * stream);
+
+/* Status of the last reference-entry launch on the calling host thread
+ * (0 = success). Reading it clears it. */
+int li_get_last_error(void);
+
+/* ======================================================================
+ * Additive entries (no reference counterpart unless cited).
+ * ====================================================================== */
+
+/* Synchronises the current device and returns (and clears) the status of
+ * the bounded device-side waits of earlier launches: LI_ERR_TIMEOUT if one
+ * gave up, a cudaError_t value if the synchronisation failed, else 0.
+ * Synchronous: not for use inside graph capture. */
+int li_device_status(void);
+
+/* Bytes of one row of k values of type wtype (0 if k is not a multiple of
+ * the block size or the type is unknown). */
+size_t li_row_bytes(int wtype, int64_t k);
+
+/* Block decode to fp32 (ggml to_float, as called from reference
+ * metal/leaninfer-metal.mm:187-193). Bit-exact with gguf-py's dequantize for
+ * Q8_0 and Q4_K. n = number of values (a multiple of the block size). */
+int li_launch_dequantize(int wtype, const void * src, float * dst, int64_t n,
+                         void * stream);
+
+/* dst[r][n] = <rmsnorm(x[r]) or x[r], W[n]> over n_rows rows of x.
+ * gamma == NULL skips the RMSNorm (plain quantized matmul, e.g. the FFN
+ * down projection). Quantized counterpart of
+ * reference cuda/leaninfer-fused-ffn.cu:41-97. */
+int li_launch_rms_norm_matmul_q(int wtype,
+        const float * x, const float * gamma, const void * W, float * dst,
+        int K, int N, int n_rows, float eps, void * stream);
+
+/* RMSNorm + Q/K/V projections with one shared normalised x (the reference's
+ * intended li_fused_rms_norm_multi_proj_f32<3>,
+ * reference cuda/leaninfer-fused-deltanet.cu:46-110). */
+int li_launch_fused_rms_norm_qkv_q(int wtype,
+        const float * x, const float * gamma,
+        const void * Wq, const void * Wk, const void * Wv,
+        float * q, float * k, float * v,
+        int K, int Nq, int Nk, int Nv, int n_rows, float eps, void * stream);
+
+/* RMSNorm + SwiGLU gate/up (quantized counterpart of
+ * reference cuda/leaninfer-fused-ffn.cu:116-180):
+ * h[r][n] = silu(<x_norm, Wg[n]>) * <x_norm, Wu[n]>. */
+int li_launch_fused_rms_norm_swiglu_q(int wtype,
+        const float * x, const float * gamma,
+        const void * Wg, const void * Wu, float * h,
+        int K, int N, int n_rows, float eps, void * stream);
+
+/* Whole SwiGLU FFN: y = Wd . (silu(Wg.xn) * (Wu.xn)), xn = rmsnorm(x).
+ * Wg, Wu [N, K]; Wd [K, N]. The intermediate h lives in the workspace. */
+size_t li_fused_ffn_workspace_size(int N, int n_rows);
+int li_launch_fused_ffn_q(int wtype,
+        const float * x, const float * gamma,
+        const void * Wg, const void * Wu, const void * Wd, float * y,
+        int K, int N, int n_rows, float eps,
+        void * workspace, size_t workspace_bytes, void * stream);
+
+/* Gated delta-rule recurrence with the reference's arithmetic and layouts
+ * (same argument meaning as li_launch_fused_deltanet_recurrent_out_f32,
+ * without the projection): writes per-head outputs to `out`
+ * [n_seqs][n_tokens][n_heads][D] and the final state to state_out
+ * (state_out == state_in is allowed: each head's state is read fully before
+ * it is written, by the same thread block). Recurrence per token
+ * (reference cuda/leaninfer-fused-deltanet.cu:217-288):
+ *   q~ = q * D^-1/2, beta = sigmoid(beta_in), a = exp(min(g, 50)),
+ *   u = S^T k, w = S^T q~, v' = beta (v - a u), o = a w + v' (k . q~),
+ *   S <- clamp(a S + k v'^T, -1e6, 1e6). */
+int li_launch_deltanet_recurrent_f32(
+        const float * q, const float * k, const float * v,
+        const float * g, const float * beta, const float * state_in,
+        float * out, float * state_out,
+        int64_t head_dim, int64_t n_tokens, int64_t n_heads,
+        int64_t gqa_ratio, int repeat_type, int64_t n_seqs,
+        size_t vnb1, size_t vnb2, size_t vnb3, void * stream);
+
+/* One decode step (one token per sequence) of a whole DeltaNet layer, as
+ * described at li_deltanet_layer. x, y [n_seqs, hidden]; conv_state
+ * [n_seqs][2*Hk*D + Hv*D][conv_kernel-1] (oldest input first) and
+ * state [n_seqs][Hv][D(k)][D(v)] are updated in place. */
+size_t li_deltanet_layer_workspace_size(const li_deltanet_layer * L, int n_seqs);
+int li_launch_deltanet_layer_decode(const li_deltanet_layer * L,
+        const float * x, float * y, float * conv_state, float * state,
+        int n_seqs, void * workspace, size_t workspace_bytes, void * stream);
+
+#else  /* no CUDA: the reference's no-op stubs, plus stubs for the new entries */
+
+static inline void li_launch_fused_rms_norm_silu_gate_f32(
+        const float*o,const float*z,const float*g,float*d,int K,int nr,float e,void*s)
+        {(void)o;(void)z;(void)g;(void)d;(void)K;(void)nr;(void)e;(void)s;}
+static inline void li_launch_fused_rms_norm_matmul_f32(
+        const float*x,const float*g,const float*W,float*d,int K,int N,float e,void*s)
+        {(void)x;(void)g;(void)W;(void)d;(void)K;(void)N;(void)e;(void)s;}
+static inline void li_launch_fused_rms_norm_swiglu_f32(
+        const float*x,const float*g,const float*wg,const float*wu,float*h,int K,int N,float e,void*s)
+        {(void)x;(void)g;(void)wg;(void)wu;(void)h;(void)K;(void)N;(void)e;(void)s;}
+static inline void li_launch_fused_rms_norm_swiglu_f16(
+        const float*x,const float*g,const void*wg,const void*wu,float*h,int K,int N,float e,void*s)
+        {(void)x;(void)g;(void)wg;(void)wu;(void)h;(void)K;(void)N;(void)e;(void)s;}
+static inline void li_launch_fused_deltanet_recurrent_out_f32(
+        const float*q,const float*k,const float*v,const float*g,const float*b,const float*s,
+        const float*w,float*d,float*p,int64_t hd,int64_t nt,int64_t nh,int64_t gr,int rt,
+        int64_t ns,int64_t hid,size_t v1,size_t v2,size_t v3,void*st)
+        {(void)q;(void)k;(void)v;(void)g;(void)b;(void)s;(void)w;(void)d;(void)p;
+         (void)hd;(void)nt;(void)nh;(void)gr;(void)rt;(void)ns;(void)hid;(void)v1;(void)v2;(void)v3;(void)st;}
+static inline void li_launch_fused_rms_norm_qkv_f32(
+        const float*x,const float*g,const float*const*W,float*const*d,int K,int N,float e,void*s)
+        {(void)x;(void)g;(void)W;(void)d;(void)K;(void)N;(void)e;(void)s;}
+static inline int li_get_last_error(void) { return LI_ERR_NO_CUDA; }
+
+#endif
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,390 @@
+// Gated DeltaNet recurrence and the fused decode layer.
+//
+// Entries:
+//   li_launch_fused_deltanet_recurrent_out_f32  (reference
+//       cuda/leaninfer-fused-deltanet.cu:331-366, same arguments)
+//   li_launch_deltanet_recurrent_f32             (recurrence only, in-place state)
+//   li_launch_deltanet_layer_decode              (whole layer, one token/sequence)
+//
+// Recurrence kernel: one CTA per (sequence, v-head), 256 threads = 8 warps.
+// The head's fp32 state S[D(k)][D(v)] lives in registers for all tokens:
+// lane l owns value rows 4l..4l+3 (D=128; 2l..2l+1 for D=64) and warp w owns
+// key columns w, w+8, ..., so every state load/store is a warp-wide
+// contiguous 512-byte (256-byte) column segment, issued all at once. Per
+// token: u = S^T k and w = S^T q~ as per-thread partials over the thread's
+// columns, an 8-way cross-warp sum in shared memory, v' and o on D threads,
+// then the rank-1 update in registers. Arithmetic follows the reference
+// kernel (cuda/leaninfer-fused-deltanet.cu:217-288): q~ = q*D^-1/2,
+// beta = sigmoid, decay = exp(min(g,50)), clamp to +-1e6.
+//
+// Layer decode = three stream-ordered kernels, the 2nd and 3rd launched as
+// programmatic dependents so they start while their predecessor drains:
+//   1. in-projection GEMV (li_qgemv.cu) with the causal-conv1d + SiLU
+//      epilogue that also shifts the conv state;
+//   2. this file's recurrence in layer mode: q/k L2 norm, beta, g from the
+//      projected alpha, the recurrence, and the gated RMSNorm of the head
+//      (reference cuda/leaninfer-fused-gate.cu:39-85) into the workspace;
+//   3. out-projection GEMV (li_qgemv.cu) of the gated heads.
+// Kernel 2 reads its state before griddepcontrol.wait; this is safe because
+// kernel 1 is launched without the programmatic attribute, so by the time
+// kernel 2 runs the previous step's kernels have all completed.
+#include "li_common.cuh"
+#include "li_qgemv.cuh"
+
+LI_DEFINE_TU_STATUS(deltanet)
+
+namespace li {
+namespace {
+
+constexpr int kRecThreads = 256;
+constexpr int kRecWarps = 8;
+
+struct RecArgs {
+    // reference layouts (legacy mode)
+    const float *q, *k, *v, *g, *beta;
+    const float *state_in;
+    float *out, *state_out;
+    int64_t n_tokens, n_heads, gqa, n_seqs;
+    int repeat_type;
+    size_t vnb1, vnb2, vnb3;
+    // layer mode
+    const float *proj;      // [B][NI]: act(q|k|v) | z | beta | alpha
+    int NI, Hk, C;
+    const float *a_log, *dt_bias, *norm_w;
+    float l2_eps, norm_eps;
+    float *o_gated;         // [B][Hv*D]
+};
+
+template <int D>
+struct RecLayout {
+    static constexpr int RPL = D / 32;            // rows per lane
+    static constexpr int CPW = D / kRecWarps;     // columns per warp
+};
+
+template <int RPL>
+struct VecT;
+template <>
+struct VecT<4> { using T = float4; };
+template <>
+struct VecT<2> { using T = float2; };
+
+template <int RPL>
+__device__ __forceinline__ void vload(float *dst, const float *src) {
+    typename VecT<RPL>::T v = *reinterpret_cast<const typename VecT<RPL>::T *>(src);
+    const float *pv = reinterpret_cast<const float *>(&v);
+#pragma unroll
+    for (int r = 0; r < RPL; ++r) dst[r] = pv[r];
+}
+
+template <int RPL>
+__device__ __forceinline__ void vstore(float *dst, const float *src) {
+    typename VecT<RPL>::T v;
+    float *pv = reinterpret_cast<float *>(&v);
+#pragma unroll
+    for (int r = 0; r < RPL; ++r) pv[r] = src[r];
+    *reinterpret_cast<typename VecT<RPL>::T *>(dst) = v;
+}
+
+template <int D, bool LAYER>
+__global__ void __launch_bounds__(kRecThreads)
+recurrent_kernel(RecArgs a) {
+    constexpr int RPL = RecLayout<D>::RPL;
+    constexpr int CPW = RecLayout<D>::CPW;
+    __shared__ __align__(16) float s_q[D];
+    __shared__ __align__(16) float s_k[D];
+    __shared__ __align__(16) float s_vp[D];
+    __shared__ __align__(16) float s_red[kRecWarps][2][D];
+    __shared__ float s_scal[8];
+
+    const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+    const int64_t seq = blockIdx.x / a.n_heads;
+    const int64_t h = blockIdx.x % a.n_heads;
+    const int64_t nkq = a.n_heads / a.gqa;
+    const int64_t hk = a.repeat_type == 0 ? h / a.gqa : h % nkq;   // ref :165-167
+    const float scale = rsqrtf((float)D);
+
+    // ---- state -> registers (independent of the previous kernel) ----
+    const float *Sin = a.state_in + ((size_t)seq * a.n_heads + h) * D * D;
+    float S[CPW][RPL];
+#pragma unroll
+    for (int j = 0; j < CPW; ++j) vload<RPL>(S[j], Sin + (size_t)(warp + kRecWarps * j) * D + RPL * lane);
+
+    if (LAYER) {
+        grid_dep_launch_dependents();
+        grid_dep_wait();
+    }
+
+    for (int64_t t = 0; t < a.n_tokens; ++t) {
+        float beta_s, decay;
+        if (!LAYER) {
+            const float *qp = a.q + ((seq * nkq + hk) * a.n_tokens + t) * D;
+            const float *kp = a.k + ((seq * nkq + hk) * a.n_tokens + t) * D;
+            for (int i = threadIdx.x; i < D; i += kRecThreads) {
+                s_q[i] = qp[i] * scale;
+                s_k[i] = kp[i];
+            }
+            const float gb = a.g[(seq * a.n_tokens + t) * a.n_heads + h];
+            const float bb = a.beta[(seq * a.n_tokens + t) * a.n_heads + h];
+            beta_s = 1.0f / (1.0f + expf(-bb));
+            decay = expf(fminf(gb, 50.0f));
+        } else {
+            const float *pr = a.proj + (size_t)seq * a.NI;
+            const int Hv = (int)a.n_heads;
+            // q, k of k-head hk, L2-normalised (warp 0: q, warp 1: k)
+            if (warp < 2) {
+                const float *src = pr + (warp == 0 ? 0 : a.Hk * D) + hk * D;
+                float vals[RPL];
+                float sq = 0.f;
+#pragma unroll
+                for (int r = 0; r < RPL; ++r) {
+                    vals[r] = src[RPL * lane + r];
+                    sq = fmaf(vals[r], vals[r], sq);
+                }
+                const float inv = rsqrtf(warp_sum(sq) + (warp == 0 ? a.l2_eps : a.l2_eps));
+                float *dst = warp == 0 ? s_q : s_k;
+#pragma unroll
+                for (int r = 0; r < RPL; ++r) dst[RPL * lane + r] = vals[r] * inv * (warp == 0 ? scale : 1.0f);
+            }
+            const float braw = pr[a.C + Hv * D + h];
+            const float araw = pr[a.C + Hv * D + Hv + h];
+            beta_s = sigmoid(braw);
+            const float gval = -expf(a.a_log[h]) * softplus(araw + a.dt_bias[h]);
+            decay = expf(fminf(gval, 50.0f));
+        }
+        __syncthreads();
+
+        // k . q~ (every warp computes it; no extra barrier)
+        float kq = 0.f;
+#pragma unroll
+        for (int i = 0; i < D / kWarp; ++i) kq = fmaf(s_k[lane + kWarp * i], s_q[lane + kWarp * i], kq);
+        const float attn = warp_sum(kq);
+
+        // partial u = S^T k, w = S^T q~ over this thread's columns
+        float pu[RPL], pw[RPL];
+#pragma unroll
+        for (int r = 0; r < RPL; ++r) pu[r] = pw[r] = 0.f;
+#pragma unroll
+        for (int j = 0; j < CPW; ++j) {
+            const int c = warp + kRecWarps * j;
+            const float kc = s_k[c], qc = s_q[c];
+#pragma unroll
+            for (int r = 0; r < RPL; ++r) {
+                pu[r] = fmaf(S[j][r], kc, pu[r]);
+                pw[r] = fmaf(S[j][r], qc, pw[r]);
+            }
+        }
+        vstore<RPL>(&s_red[warp][0][RPL * lane], pu);
+        vstore<RPL>(&s_red[warp][1][RPL * lane], pw);
+        __syncthreads();
+
+        if (threadIdx.x < D) {
+            const int r = threadIdx.x;
+            float u = 0.f, w = 0.f;
+#pragma unroll
+            for (int ww = 0; ww < kRecWarps; ++ww) {
+                u += s_red[ww][0][r];
+                w += s_red[ww][1][r];
+            }
+            float vv;
+            if (!LAYER)
+                vv = a.v[seq * a.vnb3 + h * a.vnb2 + t * a.vnb1 + r];
+            else
+                vv = a.proj[(size_t)seq * a.NI + 2 * a.Hk * D + h * D + r];
+            const float vn = beta_s * (vv - u * decay);
+            const float o = w * decay + vn * attn;
+            s_vp[r] = vn;
+            if (!LAYER) {
+                a.out[((seq * a.n_tokens + t) * a.n_heads + h) * D + r] = o;
+            } else {
+                // gated RMSNorm of this head (threads 0..D-1 are whole warps)
+                const float sq = warp_sum(o * o);
+                if ((r % kWarp) == 0) s_scal[r / kWarp] = sq;
+                asm volatile("bar.sync 1, %0;" ::"r"(D));
+                float tot = 0.f;
+#pragma unroll
+                for (int i = 0; i < D / kWarp; ++i) tot += s_scal[i];
+                const float rs = rsqrtf(tot / (float)D + a.norm_eps);
+                const float z = a.proj[(size_t)seq * a.NI + a.C + h * D + r];
+                a.o_gated[((size_t)seq * a.n_heads + h) * D + r] = silu(z) * (o * a.norm_w[r] * rs);
+            }
+        }
+        __syncthreads();
+
+        // S <- clamp(decay*S + k v'^T)
+        float vp[RPL];
+        vload<RPL>(vp, &s_vp[RPL * lane]);
+#pragma unroll
+        for (int j = 0; j < CPW; ++j) {
+            const float kc = s_k[warp + kRecWarps * j];
+#pragma unroll
+            for (int r = 0; r < RPL; ++r)
+                S[j][r] = fminf(fmaxf(fmaf(decay, S[j][r], vp[r] * kc), -1e6f), 1e6f);
+        }
+        __syncthreads();   // s_q/s_k/s_vp/s_red reused by the next token
+    }
+
+    float *Sout = a.state_out + ((size_t)seq * a.n_heads + h) * D * D;
+#pragma unroll
+    for (int j = 0; j < CPW; ++j) vstore<RPL>(Sout + (size_t)(warp + kRecWarps * j) * D + RPL * lane, S[j]);
+}
+
+// proj[d][t] = sum_s sum_j W[d][j] * o[s][t][j], o [n_seqs][n_tok][HD]
+// (the reference's intended out-projection, cuda/leaninfer-fused-deltanet.cu:260-279).
+__global__ void __launch_bounds__(256)
+proj_f32_kernel(const float *__restrict__ W, const float *__restrict__ o, float *__restrict__ proj,
+                int64_t hidden, int64_t n_tok, int64_t n_seqs, int64_t HD) {
+    const int64_t d = (int64_t)blockIdx.x * 8 + threadIdx.x / kWarp;
+    const int lane = threadIdx.x % kWarp;
+    if (d >= hidden) return;
+    const float *wr = W + d * HD;
+    for (int64_t t = 0; t < n_tok; ++t) {
+        float acc = 0.f;
+        for (int64_t j = lane; j < HD; j += kWarp) {
+            float os = 0.f;
+            for (int64_t s = 0; s < n_seqs; ++s) os += o[(s * n_tok + t) * HD + j];
+            acc = fmaf(wr[j], os, acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) proj[d * n_tok + t] = acc;
+    }
+}
+
+int check_rec(const float *q, const float *k, const float *v, const float *g, const float *beta,
+              const float *state_in, int64_t head_dim, int64_t n_tokens, int64_t n_heads,
+              int64_t gqa, int64_t n_seqs) {
+    if (!q || !k || !v || !g || !beta || !state_in) return LI_ERR_BAD_ARG;
+    if (n_tokens < 0 || n_heads <= 0 || gqa <= 0 || n_seqs < 0) return LI_ERR_BAD_ARG;
+    if (n_heads % gqa) return LI_ERR_BAD_SHAPE;
+    if (head_dim != 128 && head_dim != 64) return LI_ERR_UNSUPPORTED;
+    if (n_seqs * n_heads > 0x7fffffffLL) return LI_ERR_BAD_SHAPE;
+    return 0;
+}
+
+int launch_rec(const RecArgs &a, int64_t head_dim, cudaStream_t stream) {
+    const unsigned grid = (unsigned)(a.n_seqs * a.n_heads);
+    if (grid == 0) return 0;
+    if (head_dim == 128)
+        recurrent_kernel<128, false><<<grid, kRecThreads, 0, stream>>>(a);
+    else
+        recurrent_kernel<64, false><<<grid, kRecThreads, 0, stream>>>(a);
+    return launch_status();
+}
+
+}  // namespace
+}  // namespace li
+
+using namespace li;
+
+extern "C" {
+
+int li_launch_deltanet_recurrent_f32(const float *q, const float *k, const float *v,
+                                     const float *g, const float *beta, const float *state_in,
+                                     float *out, float *state_out, int64_t head_dim,
+                                     int64_t n_tokens, int64_t n_heads, int64_t gqa_ratio,
+                                     int repeat_type, int64_t n_seqs, size_t vnb1, size_t vnb2,
+                                     size_t vnb3, void *stream) {
+    int rc = check_rec(q, k, v, g, beta, state_in, head_dim, n_tokens, n_heads, gqa_ratio, n_seqs);
+    if (rc) return rc;
+    if (!out || !state_out) return LI_ERR_BAD_ARG;
+    if (!aligned16(state_in) || !aligned16(state_out)) return LI_ERR_MISALIGNED;
+    RecArgs a = {};
+    a.q = q; a.k = k; a.v = v; a.g = g; a.beta = beta;
+    a.state_in = state_in; a.out = out; a.state_out = state_out;
+    a.n_tokens = n_tokens; a.n_heads = n_heads; a.gqa = gqa_ratio; a.n_seqs = n_seqs;
+    a.repeat_type = repeat_type; a.vnb1 = vnb1; a.vnb2 = vnb2; a.vnb3 = vnb3;
+    return launch_rec(a, head_dim, (cudaStream_t)stream);
+}
+
+void li_launch_fused_deltanet_recurrent_out_f32(const float *q, const float *k, const float *v,
+                                                const float *g, const float *beta,
+                                                const float *state_in, const float *W_out,
+                                                float *dst, float *proj_out, int64_t head_dim,
+                                                int64_t n_tokens, int64_t n_heads,
+                                                int64_t gqa_ratio, int repeat_type, int64_t n_seqs,
+                                                int64_t hidden_dim, size_t vnb1, size_t vnb2,
+                                                size_t vnb3, void *stream) {
+    int rc = check_rec(q, k, v, g, beta, state_in, head_dim, n_tokens, n_heads, gqa_ratio, n_seqs);
+    if (!rc && !dst) rc = LI_ERR_BAD_ARG;
+    if (!rc && (!aligned16(state_in) || !aligned16(dst))) rc = LI_ERR_MISALIGNED;
+    const cudaStream_t s = (cudaStream_t)stream;
+    const int64_t out_elems = head_dim * n_tokens * n_heads * n_seqs;   // ref :342
+    if (!rc && (out_elems * 4) % 16) rc = LI_ERR_MISALIGNED;           // state after outputs
+    if (!rc) {
+        RecArgs a = {};
+        a.q = q; a.k = k; a.v = v; a.g = g; a.beta = beta;
+        a.state_in = state_in; a.out = dst; a.state_out = dst + out_elems;
+        a.n_tokens = n_tokens; a.n_heads = n_heads; a.gqa = gqa_ratio; a.n_seqs = n_seqs;
+        a.repeat_type = repeat_type; a.vnb1 = vnb1; a.vnb2 = vnb2; a.vnb3 = vnb3;
+        rc = launch_rec(a, head_dim, s);
+    }
+    if (!rc && proj_out && W_out && hidden_dim > 0 && n_tokens > 0) {
+        const unsigned grid = (unsigned)((hidden_dim + 7) / 8);
+        proj_f32_kernel<<<grid, 256, 0, s>>>(W_out, dst, proj_out, hidden_dim, n_tokens, n_seqs,
+                                             n_heads * head_dim);
+        rc = launch_status();
+    }
+    set_last_error(rc);
+}
+
+size_t li_deltanet_layer_workspace_size(const li_deltanet_layer *L, int n_seqs) {
+    if (!L || n_seqs <= 0) return 0;
+    const size_t D = L->head_dim, Hk = L->n_k_heads, Hv = L->n_v_heads;
+    const size_t NI = 2 * Hk * D + 2 * Hv * D + 2 * Hv;
+    const size_t a = (NI * n_seqs * 4 + 255) / 256 * 256;
+    const size_t b = (Hv * D * n_seqs * 4 + 255) / 256 * 256;
+    return a + b;
+}
+
+int li_launch_deltanet_layer_decode(const li_deltanet_layer *L, const float *x, float *y,
+                                    float *conv_state, float *state, int n_seqs, void *workspace,
+                                    size_t workspace_bytes, void *stream) {
+    if (!L || !x || !y || !conv_state || !state || n_seqs < 0) return LI_ERR_BAD_ARG;
+    if (n_seqs == 0) return 0;
+    if (!L->w_in || !L->conv_w || !L->a_log || !L->dt_bias || !L->norm_w || !L->w_out)
+        return LI_ERR_BAD_ARG;
+    if (L->head_dim != 128 || L->conv_kernel != 4) return LI_ERR_UNSUPPORTED;
+    if (L->n_k_heads <= 0 || L->n_v_heads <= 0 || L->n_v_heads % L->n_k_heads) return LI_ERR_BAD_SHAPE;
+    if (!aligned16(state) || !aligned16(L->conv_w)) return LI_ERR_MISALIGNED;
+    if (!workspace || workspace_bytes < li_deltanet_layer_workspace_size(L, n_seqs))
+        return LI_ERR_WORKSPACE;
+    const int D = L->head_dim, Hk = L->n_k_heads, Hv = L->n_v_heads;
+    const int C = 2 * Hk * D + Hv * D;
+    const int NI = C + Hv * D + 2 * Hv;
+    float *proj = (float *)workspace;
+    float *og = (float *)((char *)workspace + ((size_t)NI * n_seqs * 4 + 255) / 256 * 256);
+    const cudaStream_t s = (cudaStream_t)stream;
+
+    // 1. in-projection + conv1d/SiLU epilogue (not a dependent launch)
+    QGemvArgs in = {};
+    in.wtype = L->w_in_type; in.epi = kEpiConv;
+    int rc = qgemv_plan(L->w_in_type, L->hidden, NI, kEpiConv, &in.plan);
+    if (rc) return rc;
+    in.x = x; in.x_stride = L->hidden; in.gamma = L->in_norm_w; in.K = L->hidden;
+    in.eps = L->in_norm_eps; in.n_seg = 1; in.W[0] = L->w_in; in.seg_rows[0] = NI;
+    in.dst[0] = proj; in.dst_stride[0] = NI;
+    in.conv_w = L->conv_w; in.conv_state = conv_state; in.conv_channels = C;
+    if ((rc = qgemv_launch(in, n_seqs, s, false))) return rc;
+
+    // 2. recurrence + L2 norm + gated RMSNorm (dependent launch)
+    RecArgs a = {};
+    a.state_in = state; a.state_out = state;
+    a.n_tokens = 1; a.n_heads = Hv; a.gqa = Hv / Hk; a.n_seqs = n_seqs;
+    a.repeat_type = L->repeat_type;
+    a.proj = proj; a.NI = NI; a.Hk = Hk; a.C = C;
+    a.a_log = L->a_log; a.dt_bias = L->dt_bias; a.norm_w = L->norm_w;
+    a.l2_eps = L->l2_eps; a.norm_eps = L->norm_eps; a.o_gated = og;
+    rc = (int)launch_pdl(recurrent_kernel<128, true>, dim3((unsigned)(n_seqs * Hv)),
+                         dim3(kRecThreads), 0, s, true, a);
+    if (rc) return rc;
+
+    // 3. out-projection (dependent launch)
+    QGemvArgs out = {};
+    out.wtype = L->w_out_type; out.epi = kEpiStore;
+    if ((rc = qgemv_plan(L->w_out_type, Hv * D, L->hidden, kEpiStore, &out.plan))) return rc;
+    out.x = og; out.x_stride = Hv * D; out.gamma = nullptr; out.K = Hv * D; out.eps = 0.f;
+    out.n_seg = 1; out.W[0] = L->w_out; out.seg_rows[0] = L->hidden;
+    out.dst[0] = y; out.dst_stride[0] = L->hidden;
+    return qgemv_launch(out, n_seqs, s, true);
+}
+
+}  // extern "C"
