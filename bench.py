@@ -149,9 +149,28 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
     insts = build_instances(dev, B, n_inst, seed=rank + 1)
     stream = torch.cuda.current_stream()
 
-    def step(i: int):
-        it = insts[i % n_inst]
+    def launch(it):
         it["layer"].step(it["x"], it["y"], it["conv_state"], it["state"], workspace=it["ws"])
+
+    # One CUDA graph per instance holds the step's three launches (the ABI is
+    # capture-safe: no allocation, no synchronisation); one eager call per
+    # instance first fills the library's launch-attribute caches.
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for it in insts:
+            launch(it)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    for it in insts:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            launch(it)
+        it["graph"] = g
+    torch.cuda.synchronize()
+
+    def step(i: int):
+        insts[i % n_inst]["graph"].replay()
 
     for i in range(args.warmup):
         step(i)
@@ -191,7 +210,7 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
     def e2e_step(i: int):
         it = insts[i % n_inst]
         it["x"].copy_(hx[i % n_inst], non_blocking=True)
-        it["layer"].step(it["x"], it["y"], it["conv_state"], it["state"], workspace=it["ws"])
+        it["graph"].replay()
         hy[i % n_inst].copy_(it["y"], non_blocking=True)
 
     for i in range(3):

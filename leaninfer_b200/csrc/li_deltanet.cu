@@ -6,14 +6,18 @@
 //   li_launch_deltanet_recurrent_f32             (recurrence only, in-place state)
 //   li_launch_deltanet_layer_decode              (whole layer, one token/sequence)
 //
-// Recurrence kernel: one CTA per (sequence, v-head), 256 threads = 8 warps.
-// The head's fp32 state S[D(k)][D(v)] lives in registers for all tokens:
-// lane l owns value rows 4l..4l+3 (D=128; 2l..2l+1 for D=64) and warp w owns
-// key columns w, w+8, ..., so every state load/store is a warp-wide
-// contiguous 512-byte (256-byte) column segment, issued all at once. Per
-// token: u = S^T k and w = S^T q~ as per-thread partials over the thread's
-// columns, an 8-way cross-warp sum in shared memory, v' and o on D threads,
-// then the rank-1 update in registers. Arithmetic follows the reference
+// Recurrence kernel: one CTA per (sequence, v-head, block of RB value rows),
+// 256 threads = 8 warps; RB = 128, 64 or 32 picks 1, 2 or 4 CTAs per head so
+// small batches still spread over the SMs. The CTA's slice of the fp32 state
+// S[D(k)][D(v)] lives in registers for all tokens: lane l owns value rows
+// row0 + (RB/32)*l .. and warp w owns key columns w, w+8, ..., so every
+// state load/store is a warp-wide contiguous RB*4-byte column segment, all
+// issued before the first use. Per token: u = S^T k and w = S^T q~ as
+// per-thread partials over the thread's columns, an 8-way cross-warp sum in
+// shared memory, v' and o on RB threads, then the rank-1 update in
+// registers. In layer mode the CTAs of one head form a thread-block cluster
+// and combine the gated RMSNorm's sum of squares through distributed shared
+// memory. Arithmetic follows the reference
 // kernel (cuda/leaninfer-fused-deltanet.cu:217-288): q~ = q*D^-1/2,
 // beta = sigmoid, decay = exp(min(g,50)), clamp to +-1e6.
 //
@@ -30,6 +34,10 @@
 // kernel 2 runs the previous step's kernels have all completed.
 #include "li_common.cuh"
 #include "li_qgemv.cuh"
+
+#include <cooperative_groups.h>
+
+namespace cg = cooperative_groups;
 
 LI_DEFINE_TU_STATUS(deltanet)
 
@@ -67,6 +75,8 @@ template <>
 struct VecT<4> { using T = float4; };
 template <>
 struct VecT<2> { using T = float2; };
+template <>
+struct VecT<1> { using T = float; };
 
 template <int RPL>
 __device__ __forceinline__ void vload(float *dst, const float *src) {
@@ -85,26 +95,31 @@ __device__ __forceinline__ void vstore(float *dst, const float *src) {
     *reinterpret_cast<typename VecT<RPL>::T *>(dst) = v;
 }
 
-template <int D, bool LAYER>
+template <int D, bool LAYER, int RB>
 __global__ void __launch_bounds__(kRecThreads)
 recurrent_kernel(RecArgs a) {
-    constexpr int RPL = RecLayout<D>::RPL;
-    constexpr int CPW = RecLayout<D>::CPW;
+    constexpr int RPL = RB / 32;                 // value rows per lane
+    constexpr int CPW = D / kRecWarps;           // key columns per warp
+    constexpr int CS = D / RB;                   // CTAs per head
     __shared__ __align__(16) float s_q[D];
     __shared__ __align__(16) float s_k[D];
-    __shared__ __align__(16) float s_vp[D];
-    __shared__ __align__(16) float s_red[kRecWarps][2][D];
+    __shared__ __align__(16) float s_vp[RB];
+    __shared__ __align__(16) float s_red[kRecWarps][2][RB];
     __shared__ float s_scal[8];
+    __shared__ float s_part;                     // this CTA's sum of o^2 (cluster-visible)
 
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
-    const int64_t seq = blockIdx.x / a.n_heads;
-    const int64_t h = blockIdx.x % a.n_heads;
+    const int rank = CS == 1 ? 0 : (int)(blockIdx.x % CS);
+    const int64_t hblk = blockIdx.x / CS;
+    const int64_t seq = hblk / a.n_heads;
+    const int64_t h = hblk % a.n_heads;
     const int64_t nkq = a.n_heads / a.gqa;
     const int64_t hk = a.repeat_type == 0 ? h / a.gqa : h % nkq;   // ref :165-167
+    const int row0 = rank * RB;
     const float scale = rsqrtf((float)D);
 
-    // ---- state -> registers (independent of the previous kernel) ----
-    const float *Sin = a.state_in + ((size_t)seq * a.n_heads + h) * D * D;
+    // ---- state slice -> registers (independent of the previous kernel) ----
+    const float *Sin = a.state_in + ((size_t)seq * a.n_heads + h) * D * D + row0;
     float S[CPW][RPL];
 #pragma unroll
     for (int j = 0; j < CPW; ++j) vload<RPL>(S[j], Sin + (size_t)(warp + kRecWarps * j) * D + RPL * lane);
@@ -132,18 +147,20 @@ recurrent_kernel(RecArgs a) {
             const int Hv = (int)a.n_heads;
             // q, k of k-head hk, L2-normalised (warp 0: q, warp 1: k)
             if (warp < 2) {
+                constexpr int E = D / 32;
                 const float *src = pr + (warp == 0 ? 0 : a.Hk * D) + hk * D;
-                float vals[RPL];
+                float vals[E];
                 float sq = 0.f;
 #pragma unroll
-                for (int r = 0; r < RPL; ++r) {
-                    vals[r] = src[RPL * lane + r];
+                for (int r = 0; r < E; ++r) {
+                    vals[r] = src[E * lane + r];
                     sq = fmaf(vals[r], vals[r], sq);
                 }
-                const float inv = rsqrtf(warp_sum(sq) + (warp == 0 ? a.l2_eps : a.l2_eps));
+                const float inv = rsqrtf(warp_sum(sq) + a.l2_eps);
                 float *dst = warp == 0 ? s_q : s_k;
+                const float f = warp == 0 ? inv * scale : inv;
 #pragma unroll
-                for (int r = 0; r < RPL; ++r) dst[RPL * lane + r] = vals[r] * inv * (warp == 0 ? scale : 1.0f);
+                for (int r = 0; r < E; ++r) dst[E * lane + r] = vals[r] * f;
             }
             const float braw = pr[a.C + Hv * D + h];
             const float araw = pr[a.C + Hv * D + Hv + h];
@@ -177,7 +194,8 @@ recurrent_kernel(RecArgs a) {
         vstore<RPL>(&s_red[warp][1][RPL * lane], pw);
         __syncthreads();
 
-        if (threadIdx.x < D) {
+        float o = 0.f;
+        if (threadIdx.x < RB) {
             const int r = threadIdx.x;
             float u = 0.f, w = 0.f;
 #pragma unroll
@@ -187,28 +205,48 @@ recurrent_kernel(RecArgs a) {
             }
             float vv;
             if (!LAYER)
-                vv = a.v[seq * a.vnb3 + h * a.vnb2 + t * a.vnb1 + r];
+                vv = a.v[seq * a.vnb3 + h * a.vnb2 + t * a.vnb1 + row0 + r];
             else
-                vv = a.proj[(size_t)seq * a.NI + 2 * a.Hk * D + h * D + r];
+                vv = a.proj[(size_t)seq * a.NI + 2 * a.Hk * D + h * D + row0 + r];
             const float vn = beta_s * (vv - u * decay);
-            const float o = w * decay + vn * attn;
+            o = w * decay + vn * attn;
             s_vp[r] = vn;
             if (!LAYER) {
-                a.out[((seq * a.n_tokens + t) * a.n_heads + h) * D + r] = o;
+                a.out[((seq * a.n_tokens + t) * a.n_heads + h) * D + row0 + r] = o;
             } else {
-                // gated RMSNorm of this head (threads 0..D-1 are whole warps)
                 const float sq = warp_sum(o * o);
                 if ((r % kWarp) == 0) s_scal[r / kWarp] = sq;
-                asm volatile("bar.sync 1, %0;" ::"r"(D));
-                float tot = 0.f;
-#pragma unroll
-                for (int i = 0; i < D / kWarp; ++i) tot += s_scal[i];
-                const float rs = rsqrtf(tot / (float)D + a.norm_eps);
-                const float z = a.proj[(size_t)seq * a.NI + a.C + h * D + r];
-                a.o_gated[((size_t)seq * a.n_heads + h) * D + r] = silu(z) * (o * a.norm_w[r] * rs);
             }
         }
         __syncthreads();
+        if (LAYER) {
+            // gated RMSNorm of the head (reference cuda/leaninfer-fused-gate.cu:39-85):
+            // sum o^2 over the CS CTAs of the cluster
+            if (threadIdx.x == 0) {
+                float p = 0.f;
+#pragma unroll
+                for (int i = 0; i < RB / kWarp; ++i) p += s_scal[i];
+                s_part = p;
+            }
+            float tot;
+            if (CS == 1) {
+                __syncthreads();
+                tot = s_part;
+            } else {
+                cg::cluster_group cluster = cg::this_cluster();
+                cluster.sync();
+                tot = 0.f;
+#pragma unroll
+                for (int i = 0; i < CS; ++i) tot += *cluster.map_shared_rank(&s_part, i);
+            }
+            if (threadIdx.x < RB) {
+                const int r = threadIdx.x;
+                const float rs = rsqrtf(tot / (float)D + a.norm_eps);
+                const float z = a.proj[(size_t)seq * a.NI + a.C + h * D + row0 + r];
+                a.o_gated[((size_t)seq * a.n_heads + h) * D + row0 + r] =
+                    silu(z) * (o * a.norm_w[row0 + r] * rs);
+            }
+        }
 
         // S <- clamp(decay*S + k v'^T)
         float vp[RPL];
@@ -223,9 +261,15 @@ recurrent_kernel(RecArgs a) {
         __syncthreads();   // s_q/s_k/s_vp/s_red reused by the next token
     }
 
-    float *Sout = a.state_out + ((size_t)seq * a.n_heads + h) * D * D;
+    float *Sout = a.state_out + ((size_t)seq * a.n_heads + h) * D * D + row0;
 #pragma unroll
     for (int j = 0; j < CPW; ++j) vstore<RPL>(Sout + (size_t)(warp + kRecWarps * j) * D + RPL * lane, S[j]);
+    if (LAYER && CS > 1) {
+        // No CTA leaves while a cluster peer may still read its s_part. Only
+        // shared-memory lifetime is at stake, so the arrive is relaxed: it
+        // does not wait for this thread's global stores to become visible.
+        asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+    }
 }
 
 // proj[d][t] = sum_s sum_j W[d][j] * o[s][t][j], o [n_seqs][n_tok][HD]
@@ -260,14 +304,47 @@ int check_rec(const float *q, const float *k, const float *v, const float *g, co
     return 0;
 }
 
+// Value rows per CTA: enough CTAs to cover the SMs at small batch.
+int pick_rows(int64_t heads_total, int64_t head_dim) {
+    if (head_dim == 64) return heads_total <= 128 ? 32 : 64;
+    return heads_total <= 64 ? 32 : (heads_total <= 512 ? 64 : 128);
+}
+
 int launch_rec(const RecArgs &a, int64_t head_dim, cudaStream_t stream) {
-    const unsigned grid = (unsigned)(a.n_seqs * a.n_heads);
-    if (grid == 0) return 0;
-    if (head_dim == 128)
-        recurrent_kernel<128, false><<<grid, kRecThreads, 0, stream>>>(a);
-    else
-        recurrent_kernel<64, false><<<grid, kRecThreads, 0, stream>>>(a);
+    const int64_t heads = a.n_seqs * a.n_heads;
+    if (heads == 0) return 0;
+    const int rb = pick_rows(heads, head_dim);
+    const unsigned grid = (unsigned)(heads * (head_dim / rb));
+    if (head_dim == 128) {
+        if (rb == 32) recurrent_kernel<128, false, 32><<<grid, kRecThreads, 0, stream>>>(a);
+        else if (rb == 64) recurrent_kernel<128, false, 64><<<grid, kRecThreads, 0, stream>>>(a);
+        else recurrent_kernel<128, false, 128><<<grid, kRecThreads, 0, stream>>>(a);
+    } else {
+        if (rb == 32) recurrent_kernel<64, false, 32><<<grid, kRecThreads, 0, stream>>>(a);
+        else recurrent_kernel<64, false, 64><<<grid, kRecThreads, 0, stream>>>(a);
+    }
     return launch_status();
+}
+
+// Layer-mode launch: a cluster of D/RB CTAs per head, programmatic dependent.
+template <int RB>
+int launch_layer_rec(const RecArgs &a, cudaStream_t stream) {
+    const int64_t heads = a.n_seqs * a.n_heads;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(heads * (128 / RB)));
+    cfg.blockDim = dim3(kRecThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 128 / RB;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return (int)cudaLaunchKernelEx(&cfg, recurrent_kernel<128, true, RB>, a);
 }
 
 }  // namespace
@@ -344,7 +421,8 @@ int li_launch_deltanet_layer_decode(const li_deltanet_layer *L, const float *x, 
         return LI_ERR_BAD_ARG;
     if (L->head_dim != 128 || L->conv_kernel != 4) return LI_ERR_UNSUPPORTED;
     if (L->n_k_heads <= 0 || L->n_v_heads <= 0 || L->n_v_heads % L->n_k_heads) return LI_ERR_BAD_SHAPE;
-    if (!aligned16(state) || !aligned16(L->conv_w)) return LI_ERR_MISALIGNED;
+    if (!aligned16(state) || !aligned16(L->conv_w) || !aligned16(x)) return LI_ERR_MISALIGNED;
+    if (L->in_norm_w && !aligned16(L->in_norm_w)) return LI_ERR_MISALIGNED;
     if (!workspace || workspace_bytes < li_deltanet_layer_workspace_size(L, n_seqs))
         return LI_ERR_WORKSPACE;
     const int D = L->head_dim, Hk = L->n_k_heads, Hv = L->n_v_heads;
@@ -373,8 +451,8 @@ int li_launch_deltanet_layer_decode(const li_deltanet_layer *L, const float *x, 
     a.proj = proj; a.NI = NI; a.Hk = Hk; a.C = C;
     a.a_log = L->a_log; a.dt_bias = L->dt_bias; a.norm_w = L->norm_w;
     a.l2_eps = L->l2_eps; a.norm_eps = L->norm_eps; a.o_gated = og;
-    rc = (int)launch_pdl(recurrent_kernel<128, true>, dim3((unsigned)(n_seqs * Hv)),
-                         dim3(kRecThreads), 0, s, true, a);
+    const int rb = pick_rows((int64_t)n_seqs * Hv, 128);
+    rc = rb == 32 ? launch_layer_rec<32>(a, s) : rb == 64 ? launch_layer_rec<64>(a, s) : launch_layer_rec<128>(a, s);
     if (rc) return rc;
 
     // 3. out-projection (dependent launch)

@@ -5,29 +5,39 @@
 // li_launch_dequantize; and the in-/out-projection stages of the DeltaNet
 // layer decode (li_deltanet.cu) through qgemv_launch().
 //
-// Design (SIMT path, one x row per pass):
-//   * A "unit" is 32 weights of one row: one Q8_0 block, or one 16-byte
-//     nibble chunk of a Q4_K super-block (16 low nibbles of sub-block 2i and
-//     the 16 high nibbles of sub-block 2i+1). A row has U = K/32 units.
-//   * A CTA has RP "row slots" of U (rounded to 32) threads. Thread u of a
-//     slot owns unit u of every row the CTA visits, so it keeps the 32 x_norm
-//     values of that unit in registers for the whole kernel: x is read once
-//     per CTA, never from shared memory in the inner loop.
+// Design (SIMT path, one x row per CTA row):
+//   * A "unit" is a fixed slice of a row: one Q8_0 block (32 weights) or one
+//     Q4_K sub-block pair (64 weights: the 32 nibble bytes of pair i hold
+//     sub-block 2i in their low and 2i+1 in their high nibbles). A row has U
+//     units. A CTA has RP "row slots" of U (rounded up to 32) threads; thread
+//     u of a slot owns unit u of every row the CTA visits and keeps that
+//     unit's x_norm values in registers for the whole kernel.
 //   * Weight rows are staged into shared memory by the TMA engine
 //     (cp.async.bulk, 1-D) in a ring of S stages of SR rows each, completion
-//     tracked by mbarriers (bounded waits). Rows are contiguous in ggml
-//     layout, so one stage is one to three bulk copies.
-//   * Each thread decodes its unit in registers (byte permutes into float
-//     magic numbers; Q4_K scales unpacked per sub-block, the min term folded
-//     as dmin*m*sum(x)), reduces with xor-shuffles, and the slot's warps
-//     combine through shared memory into an epilogue: plain store, SwiGLU,
-//     or the DeltaNet in-projection epilogue (causal conv1d + SiLU with the
-//     conv-state shift, so each conv channel has exactly one writer).
+//     tracked by mbarriers with bounded waits. Rows are contiguous in ggml
+//     layout, so a stage is one to three bulk copies.
+//   * Integer dot products: each thread quantizes its (fixed) x slice once,
+//     per 32-value sub-block, to int16 with scale max|x|/32767 (error at
+//     most 1.5e-5 of the sub-block's max |x|), and multiplies it against the
+//     codes with dp2a (two int16 x int8 products per instruction, exact
+//     int32 sums). Q8_0 code words feed dp2a as they are; Q4_K needs one mask
+//     and one shift per 8 nibbles. The unit's partial is rescaled in fp32 by
+//     the block scale(s) and the x scale; the Q4_K min term uses the fp32
+//     sum of x.
+//   * Each thread reduces its R rows with a butterfly transpose over the
+//     warp (R-1 + log2(32/R) shuffles for R rows), warps of a slot combine
+//     through double-buffered shared memory, one barrier per stage, into an
+//     epilogue: plain store, SwiGLU, or the DeltaNet in-projection epilogue
+//     (causal conv1d + SiLU with the conv-state shift, one writer per
+//     channel).
 //   * The grid is persistent (SM count x resident CTAs); CTAs stride over
-//     stages. A launch may be a programmatic dependent launch: weight
-//     stages are requested before griddepcontrol.wait, x after it.
+//     stages. A launch may be a programmatic dependent launch: weight stages
+//     are requested before griddepcontrol.wait, x after it.
 #include "li_common.cuh"
 #include "li_qgemv.cuh"
+
+#include <mutex>
+#include <vector>
 
 LI_DEFINE_TU_STATUS(qgemv)
 
@@ -35,100 +45,155 @@ namespace li {
 
 namespace {
 
-constexpr int kRowsPerThread = 4;     // rows of a stage per row slot
-constexpr int kMaxThreads = 1024;
-constexpr int kSmemBudget = 100 * 1024;
+constexpr int kMaxThreads = 512;      // 64-weight units: K <= 16384 (Q8_0), 32768 (Q4_K)
+constexpr int kStageTarget = 40 * 1024;   // bytes of weight rows per stage
+constexpr int kSmemBudget = 112 * 1024;   // stages per CTA (two CTAs per SM)
 
-// ---------------------------------------------------------------------------
-// Unit dot products. xr[0..31] are the unit's x values in decode order.
-// ---------------------------------------------------------------------------
+// Weights per unit.
+__host__ __device__ constexpr int unit_weights(int wt) { return wt == LI_WTYPE_Q8_0 ? 32 : 64; }
 
-// Q8_0 block b of a row whose shared-memory copy starts at `srow` (4-byte
-// aligned). Reads 9 aligned words; even blocks start on a 4-byte boundary
-// (scale in the low half of word 0), odd blocks 2 bytes past one.
-__device__ __forceinline__ float dot_q8_0(const uint8_t *srow, int b, const float *xr) {
-    const uint32_t off = 34u * (uint32_t)b;
+// Q8_0 block u of a row whose shared-memory copy starts at `srow` (4-byte
+// aligned); xq[k] = int16 pair (x[2k], x[2k+1]) of the block, xscale its
+// quantization step. Reads 9 aligned words: even blocks start on a 4-byte
+// boundary (scale in the low half of word 0), odd blocks 2 bytes past one.
+__device__ __forceinline__ float dot_q8_0(const uint8_t *srow, int u, const int *xq, float xscale) {
+    const uint32_t off = 34u * (uint32_t)u;
     const uint32_t *w = reinterpret_cast<const uint32_t *>(srow + (off & ~3u));
     uint32_t v[9];
 #pragma unroll
     for (int i = 0; i < 9; ++i) v[i] = w[i];
-    const uint32_t sh = (off & 2u) ? 32u : 16u;      // odd block: quants start at word 1
-    const float d = half_bits_to_float((off & 2u) ? (v[0] >> 16) : v[0]);
-    float acc = 0.f;
+    const bool odd = (off & 2u) != 0;                  // odd block: quants start at word 1
+    const uint32_t sh = odd ? 32u : 16u;
+    const float d = half_bits_to_float(odd ? (v[0] >> 16) : v[0]);
+    int acc = 0;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-        const uint32_t q = __funnelshift_rc(v[j], v[j + 1], sh) ^ 0x80808080u;
-#pragma unroll
-        for (int bb = 0; bb < 4; ++bb) {
-            const float f = __uint_as_float(__byte_perm(q, 0x4B000000u, 0x7540u | bb)) - 8388736.0f;
-            acc = fmaf(xr[4 * j + bb], f, acc);
-        }
+        const int q = (int)__funnelshift_rc(v[j], v[j + 1], sh);
+        acc = __dp2a_lo(xq[2 * j], q, acc);
+        acc = __dp2a_hi(xq[2 * j + 1], q, acc);
     }
-    return d * acc;
+    return d * xscale * (float)acc;
 }
 
-// Q4_K unit: header word h (d | dmin<<16, then three scale words) and the
-// 16-byte nibble chunk q of pair i = c/2. xsum = {sum(xr[0..15]), sum(xr[16..31])}.
-__device__ __forceinline__ float dot_q4_k(uint4 h, uint4 q, int c, const float *xr,
-                                          float xsum_lo, float xsum_hi) {
-    const int i = c >> 1;
-    float sc0, m0, sc1, m1;
-    q4k_scale_min(h.y, h.z, h.w, 2 * i, sc0, m0);
-    q4k_scale_min(h.y, h.z, h.w, 2 * i + 1, sc1, m1);
+// Q4_K sub-block pair i of a super-block: header h = {d | dmin<<16, scale
+// bytes 0-3, 4-7, 8-11}, nibble bytes q0 (0-15) and q1 (16-31) of the pair.
+// xq0/xq1 = int16 pairs of sub-blocks 2i / 2i+1, xs0/xs1 their steps,
+// sum0/sum1 their fp32 sums of x.
+__device__ __forceinline__ float dot_q4_k(uint4 h, uint4 q0, uint4 q1, int i, const int *xq0,
+                                          const int *xq1, float xs0, float xs1, float sum0,
+                                          float sum1) {
+    const uint32_t bsh = 16u * (uint32_t)(i & 1);
+    const uint32_t a0 = h.y >> bsh, a1 = h.z >> bsh, a2 = h.w >> bsh;
+    uint32_t sc0, sc1, m0, m1;
+    if (i < 2) {
+        sc0 = a0 & 63u; sc1 = (a0 >> 8) & 63u; m0 = a1 & 63u; m1 = (a1 >> 8) & 63u;
+    } else {
+        sc0 = (a2 & 15u) | ((a0 >> 2) & 48u);
+        sc1 = ((a2 >> 8) & 15u) | ((a0 >> 10) & 48u);
+        m0 = ((a2 >> 4) & 15u) | ((a1 >> 2) & 48u);
+        m1 = ((a2 >> 12) & 15u) | ((a1 >> 10) & 48u);
+    }
+    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    int acc0 = 0, acc1 = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int lo = (int)(w[j] & 0x0f0f0f0fu);          // sub-block 2i, positions 4j..4j+3
+        const int hi = (int)((w[j] >> 4) & 0x0f0f0f0fu);   // sub-block 2i+1
+        acc0 = __dp2a_lo(xq0[2 * j], lo, acc0);
+        acc0 = __dp2a_hi(xq0[2 * j + 1], lo, acc0);
+        acc1 = __dp2a_lo(xq1[2 * j], hi, acc1);
+        acc1 = __dp2a_hi(xq1[2 * j + 1], hi, acc1);
+    }
     const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-    float lo = 0.f, hi = 0.f;
+    return d * fmaf((float)sc0 * xs0, (float)acc0, (float)sc1 * xs1 * (float)acc1) -
+           dmin * fmaf((float)m0, sum0, (float)m1 * sum1);
+}
+
+// Quantize 32 fp32 values to int16 pairs with step max|v|/32767; returns
+// the step (0 for an all-zero slice).
+__device__ __forceinline__ float quantize32_s16(const float *v, int *xq) {
+    float mx = 0.f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const uint32_t L = w[j] & 0x0f0f0f0fu;
-        const uint32_t H = (w[j] >> 4) & 0x0f0f0f0fu;
+    for (int k = 0; k < 32; ++k) mx = fmaxf(mx, fabsf(v[k]));
+    const float step = mx / 32767.0f;
+    const float inv = mx > 0.f ? 32767.0f / mx : 0.f;
 #pragma unroll
-        for (int bb = 0; bb < 4; ++bb) {
-            lo = fmaf(xr[4 * j + bb], byte_to_float(L, bb), lo);
-            hi = fmaf(xr[16 + 4 * j + bb], byte_to_float(H, bb), hi);
-        }
+    for (int k = 0; k < 16; ++k) {
+        const int a = __float2int_rn(v[2 * k] * inv);
+        const int b = __float2int_rn(v[2 * k + 1] * inv);
+        xq[k] = (a & 0xffff) | (b << 16);
     }
-    return d * (sc0 * lo + sc1 * hi) - dmin * (m0 * xsum_lo + m1 * xsum_hi);
+    return step;
 }
 
-// x offsets (elements) of decode position p (0..31) of unit u.
-__device__ __forceinline__ int unit_x_index(int wt, int u, int p) {
-    if (wt == LI_WTYPE_Q8_0) return 32 * u + p;
-    const int sb = u >> 3, c = u & 7, i = c >> 1, h = c & 1;
-    return 256 * sb + 64 * i + 16 * h + (p < 16 ? p : 32 + (p - 16));
+// Butterfly transpose-reduction of V values per lane over the warp: after
+// it, lane l holds the warp sum of value index (l >> (5 - log2 V)) & (V-1).
+template <int V>
+__device__ __forceinline__ float warp_transpose_reduce(float (&v)[V], int lane) {
+    int cur = V;
+#pragma unroll
+    for (int o = 16; cur > 1; o >>= 1) {
+        const bool upper = (lane & o) != 0;
+        const int half = cur >> 1;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const float send = upper ? v[i] : v[i + half];
+            const float keep = upper ? v[i + half] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+        cur = half;
+    }
+    float r = v[0];
+    constexpr int lv = V == 1 ? 0 : V == 2 ? 1 : V == 4 ? 2 : V == 8 ? 3 : 4;
+#pragma unroll
+    for (int o = 16 >> lv; o > 0; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+    return r;
 }
 
 // ---------------------------------------------------------------------------
-// The kernel.
+// The kernel. R = rows per slot per stage, NW = weight streams (2: SwiGLU).
 // ---------------------------------------------------------------------------
-template <int WT, int EPI, int LB>
+template <int WT, int EPI, int LB, int R>
 __global__ void __launch_bounds__(LB)
 qgemv_kernel(QGemvArgs a) {
+    constexpr int NW = EPI == kEpiSwiGLU ? 2 : 1;
+    constexpr int V = NW * R;                         // values per thread per stage
+    constexpr int UW = unit_weights(WT);              // weights per unit
     extern __shared__ __align__(16) uint8_t smem[];
     const QGemvPlan &p = a.plan;
-    const int t = threadIdx.x;
+    const int t = threadIdx.x, lane = t % kWarp;
     const int slot = t / p.UP, u = t % p.UP;
     const bool active = u < p.U;
-    const int nw = EPI == kEpiSwiGLU ? 2 : 1;
     const size_t rb = p.row_bytes;
-    const uint32_t stage_bytes = (uint32_t)(nw * p.SR * rb);
+    const uint32_t stage_bytes = (uint32_t)(NW * p.SR * rb);
+    const int wps = p.UP / kWarp;                     // warps per slot
+    const int XB = p.XB;                              // buffers that first stage x
 
     uint8_t *stages = smem;
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem + (size_t)p.S * stage_bytes);
-    float *red = reinterpret_cast<float *>(bar + p.S);          // [SR][warps per slot][2]
-    int *abort_flag = reinterpret_cast<int *>(red + p.SR * (p.UP / kWarp) * 2);
+    float *red = reinterpret_cast<float *>(bar + p.S);   // [2][SR][wps][NW]
+    int *abort_flag = reinterpret_cast<int *>(red + 2 * p.SR * wps * NW);
+    __shared__ float sred[kMaxThreads / kWarp];
 
-    const int wps = p.UP / kWarp;                                // warps per slot
-    const int b = blockIdx.y;                                    // x row (batch)
+    const int b = blockIdx.y;                         // x row (batch)
     const int n_stages = (p.total_rows + p.SR - 1) / p.SR;
 
-    // -- issue a stage: rows [r0, r0+SR) of the concatenated row space --
-    auto issue = [&](int st, int buf) {
+    // Pipeline slots: virtual iteration v uses buffer v % S and, for v >= XB,
+    // holds weight stage stage_of(v). Virtual iterations 0..XB-1 are not
+    // weight stages: their buffers stage x while weight stages XB..S-1 are
+    // already in flight. Buffer v % S has completed (v / S) - (v % S < XB)
+    // bulk-copy phases before the copy of iteration v.
+    auto stage_of = [&](int v) { return (int)blockIdx.x + (v - XB) * (int)gridDim.x; };
+    auto parity_of = [&](int v) { return (uint32_t)(((v / p.S) - ((v % p.S) < XB ? 1 : 0)) & 1); };
+
+    auto issue = [&](int v) {
+        const int st = stage_of(v);
+        const int buf = v % p.S;
         const int r0 = st * p.SR;
         const int r1 = min(r0 + p.SR, p.total_rows);
         uint8_t *dst = stages + (size_t)buf * stage_bytes;
-        mbar_arrive_expect_tx(&bar[buf], (uint32_t)((size_t)nw * (r1 - r0) * rb));
-        for (int w = 0; w < nw; ++w) {
+        mbar_arrive_expect_tx(&bar[buf], (uint32_t)((size_t)NW * (r1 - r0) * rb));
+        for (int w = 0; w < NW; ++w) {
             int r = r0;
             while (r < r1) {
                 int m = 0, lr = r;
@@ -150,104 +215,117 @@ qgemv_kernel(QGemvArgs a) {
     }
     __syncthreads();
     if (t == 0) {
-        for (int s = 0; s < p.S; ++s) {
-            const int st = blockIdx.x + s * gridDim.x;
-            if (st < n_stages) issue(st, s);
-        }
+        for (int v = XB; v < p.S; ++v)
+            if (stage_of(v) < n_stages) issue(v);
     }
     // Let a dependent launch start its own weight-independent prologue.
     grid_dep_launch_dependents();
-
     // x depends on the previous kernel in the stream; weights do not.
     grid_dep_wait();
 
-    // -- x_norm of this thread's unit into registers --
-    float xr[32];
-    float xs_lo = 0.f, xs_hi = 0.f;
+    // -- x (times gamma) into buffers 0..XB-1, coalesced, padded by one
+    //    float per unit so the per-unit reads below are conflict free --
+    float *xs = reinterpret_cast<float *>(stages);
+    float rnorm = 1.0f;
     {
-        const float *xrow = a.x + (size_t)b * a.x_stride;
+        const float4 *x4 = reinterpret_cast<const float4 *>(a.x + (size_t)b * a.x_stride);
+        const float4 *g4 = reinterpret_cast<const float4 *>(a.gamma);
         float sq = 0.f;
-#pragma unroll
-        for (int q = 0; q < 32; ++q) {
-            const float v = active ? xrow[unit_x_index(WT, u, q)] : 0.f;
-            xr[q] = v;
-            sq = fmaf(v, v, sq);
+        for (int i = t; i < a.K / 4; i += blockDim.x) {
+            float4 v = x4[i];
+            sq = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, sq))));
+            if (a.gamma) {
+                const float4 g = g4[i];
+                v.x *= g.x; v.y *= g.y; v.z *= g.z; v.w *= g.w;
+            }
+            const int k = 4 * i, kp = k + k / UW;
+            xs[kp] = v.x; xs[kp + 1] = v.y; xs[kp + 2] = v.z; xs[kp + 3] = v.w;
         }
+        sq = warp_sum(sq);
+        if (lane == 0) sred[t / kWarp] = sq;
+        __syncthreads();
         if (a.gamma) {
-            sq = warp_sum(slot == 0 ? sq : 0.f);
-            __shared__ float sred[kMaxThreads / kWarp];
-            if ((t % kWarp) == 0) sred[t / kWarp] = sq;
-            __syncthreads();
             float tot = 0.f;
-            for (int w = 0; w < wps; ++w) tot += sred[w];
-            const float r = rsqrtf(tot / (float)a.K + a.eps);
-#pragma unroll
-            for (int q = 0; q < 32; ++q)
-                xr[q] = active ? xr[q] * a.gamma[unit_x_index(WT, u, q)] * r : 0.f;
-        }
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-            xs_lo += xr[q];
-            xs_hi += xr[16 + q];
+            for (int w = 0; w < (int)(blockDim.x / kWarp); ++w) tot += sred[w];
+            rnorm = rsqrtf(tot / (float)a.K + a.eps);
         }
     }
 
-    int it = 0;
-    for (;; ++it) {
-        const int st = blockIdx.x + it * gridDim.x;
+    // -- this thread's unit: x_norm quantized to int16 per 32-value sub-block --
+    constexpr int NSUB = UW / 32;                     // sub-blocks per unit
+    int xq[NSUB][16];
+    float xstep[NSUB], xsum[NSUB];
+    {
+        const float *xu = xs + (size_t)(active ? u : 0) * (UW + 1);
+#pragma unroll
+        for (int sb = 0; sb < NSUB; ++sb) {
+            float v[32];
+            float sm = 0.f;
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+                v[k] = active ? xu[32 * sb + k] * rnorm : 0.f;
+                sm += v[k];
+            }
+            xsum[sb] = sm;
+            xstep[sb] = quantize32_s16(v, xq[sb]);
+        }
+    }
+    __syncthreads();                     // x buffers free
+    if (t == 0) {
+        for (int v = p.S; v < p.S + XB; ++v)
+            if (stage_of(v) < n_stages) issue(v);
+    }
+
+    int v = XB;
+    for (;; ++v) {
+        const int st = stage_of(v);
         if (st >= n_stages) break;
-        const int buf = it % p.S;
-        if (!mbar_wait(&bar[buf], (uint32_t)((it / p.S) & 1))) atomicExch(abort_flag, 1);
+        const int buf = v % p.S;
+        if (!mbar_wait(&bar[buf], parity_of(v))) atomicExch(abort_flag, 1);
         const uint8_t *sbuf = stages + (size_t)buf * stage_bytes;
         const int r0 = st * p.SR;
 
-        // partial dot products of this thread's unit over its rows
-        float part[kRowsPerThread][2];
+        float part[V];
 #pragma unroll
-        for (int j = 0; j < kRowsPerThread; ++j) {
+        for (int j = 0; j < R; ++j) {
             const int lr = slot + p.RP * j;
+            const bool ok = active && r0 + lr < p.total_rows;
 #pragma unroll
-            for (int w = 0; w < 2; ++w) {
-                part[j][w] = 0.f;
-                if (w < nw && active && lr < p.SR && r0 + lr < p.total_rows && !*abort_flag) {
+            for (int w = 0; w < NW; ++w) {
+                float val = 0.f;
+                if (ok) {
                     const uint8_t *srow = sbuf + ((size_t)w * p.SR + lr) * rb;
                     if (WT == LI_WTYPE_Q8_0) {
-                        part[j][w] = dot_q8_0(srow, u, xr);
+                        val = dot_q8_0(srow, u, xq[0], xstep[0]);
                     } else {
-                        const int sb = u >> 3, c = u & 7;
-                        const uint4 h = *reinterpret_cast<const uint4 *>(srow + 144 * sb);
-                        const uint4 q = *reinterpret_cast<const uint4 *>(srow + 144 * sb + 16 + 16 * c);
-                        part[j][w] = dot_q4_k(h, q, c, xr, xs_lo, xs_hi);
+                        const uint8_t *blk = srow + 144 * (u >> 2);
+                        const uint4 h = *reinterpret_cast<const uint4 *>(blk);
+                        const uint4 q0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * (u & 3));
+                        const uint4 q1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * (u & 3));
+                        val = dot_q4_k(h, q0, q1, u & 3, xq[0], xq[NSUB - 1], xstep[0], xstep[NSUB - 1],
+                                       xsum[0], xsum[NSUB - 1]);
                     }
                 }
+                part[w * R + j] = val;
             }
         }
-#pragma unroll
-        for (int j = 0; j < kRowsPerThread; ++j)
-#pragma unroll
-            for (int w = 0; w < 2; ++w) part[j][w] = warp_sum(part[j][w]);
-        if ((t % kWarp) == 0) {
-            const int wi = u / kWarp;
-#pragma unroll
-            for (int j = 0; j < kRowsPerThread; ++j) {
-                const int lr = slot + p.RP * j;
-                if (lr < p.SR) {
-                    red[(lr * wps + wi) * 2 + 0] = part[j][0];
-                    red[(lr * wps + wi) * 2 + 1] = part[j][1];
-                }
-            }
+        const float sum = warp_transpose_reduce<V>(part, lane);
+        float *rb2 = red + (size_t)(v & 1) * p.SR * wps * NW;
+        constexpr int lv = V == 1 ? 0 : V == 2 ? 1 : V == 4 ? 2 : V == 8 ? 3 : 4;
+        if ((lane & ((32 >> lv) - 1)) == 0) {
+            const int vi = (lane >> (5 - lv)) & (V - 1);
+            const int w = vi / R, j = vi % R;
+            const int lr = slot + p.RP * j;
+            rb2[(lr * wps + u / kWarp) * NW + w] = sum;
         }
         __syncthreads();                 // stage buffer free, partials visible
         if (*abort_flag) break;
-        if (t == 0) {
-            const int nst = blockIdx.x + (it + p.S) * gridDim.x;
-            if (nst < n_stages) issue(nst, buf);
-        }
+        if (t == 0 && stage_of(v + p.S) < n_stages) issue(v + p.S);
         if (t < p.SR && r0 + t < p.total_rows) {
             float s0 = 0.f, s1 = 0.f;
             for (int w = 0; w < wps; ++w) {
-                s0 += red[(t * wps + w) * 2 + 0];
-                s1 += red[(t * wps + w) * 2 + 1];
+                s0 += rb2[(t * wps + w) * NW];
+                if (NW == 2) s1 += rb2[(t * wps + w) * NW + 1];
             }
             const int row = r0 + t;
             if (EPI == kEpiSwiGLU) {
@@ -255,7 +333,9 @@ qgemv_kernel(QGemvArgs a) {
             } else if (EPI == kEpiStore) {
                 int m = 0, lr = row;
                 while (m < a.n_seg - 1 && lr >= a.seg_rows[m]) lr -= a.seg_rows[m++];
-                a.dst[m][(size_t)b * a.dst_stride[m] + lr] = s0;
+                float *d = m == 0 ? a.dst[0] : (m == 1 ? a.dst[1] : a.dst[2]);
+                const int ds = m == 0 ? a.dst_stride[0] : (m == 1 ? a.dst_stride[1] : a.dst_stride[2]);
+                d[(size_t)b * ds + lr] = s0;
             } else {  // kEpiConv: DeltaNet in-projection epilogue
                 float out = s0;
                 if (row < a.conv_channels) {
@@ -271,14 +351,13 @@ qgemv_kernel(QGemvArgs a) {
                 a.dst[0][(size_t)b * a.dst_stride[0] + row] = out;
             }
         }
-        __syncthreads();                 // red reused next iteration
     }
     if (*abort_flag && t == 0) {
-        // A wait gave up at iteration `it`: stages it .. it+S-1 were issued
-        // and not consumed. Drain them (bounded) before the CTA's shared
-        // memory is released.
-        for (int j = it; j < it + p.S; ++j)
-            if (blockIdx.x + j * gridDim.x < n_stages) mbar_wait(&bar[j % p.S], (uint32_t)((j / p.S) & 1));
+        // A wait gave up at virtual iteration v: iterations v .. v+S-1 were
+        // issued and not consumed. Drain them (bounded) before the CTA's
+        // shared memory is released.
+        for (int j = v; j < v + p.S; ++j)
+            if (stage_of(j) < n_stages) mbar_wait(&bar[j % p.S], parity_of(j));
     }
 }
 
@@ -291,39 +370,105 @@ int qgemv_plan(int wtype, int K, int total_rows, int epi, QGemvPlan *p) {
     if (wtype != LI_WTYPE_Q8_0 && wtype != LI_WTYPE_Q4_K) return LI_ERR_UNSUPPORTED;
     const size_t rb = li_row_bytes(wtype, K);
     if (!rb || K % 256) return LI_ERR_BAD_SHAPE;               // bulk copies need 16-byte rows
-    p->U = K / 32;
+    p->U = K / unit_weights(wtype);
     p->UP = (p->U + kWarp - 1) / kWarp * kWarp;
     if (p->UP > kMaxThreads) return LI_ERR_BAD_SHAPE;
     p->RP = p->UP >= 256 ? 1 : 256 / p->UP;
-    p->SR = p->RP * kRowsPerThread;
+    const int nw = epi == kEpiSwiGLU ? 2 : 1;
+    p->R = 8 / nw;
+    while (p->R > 1 && (size_t)nw * p->RP * p->R * rb > kStageTarget) p->R >>= 1;
+    p->SR = p->RP * p->R;
     p->row_bytes = rb;
     p->total_rows = total_rows;
-    const int nw = epi == kEpiSwiGLU ? 2 : 1;
-    size_t stage = (size_t)nw * p->SR * rb;
+    const size_t stage = (size_t)nw * p->SR * rb;
     p->S = (int)(kSmemBudget / stage);
     if (p->S > 4) p->S = 4;
     if (p->S < 2) p->S = 2;
     if (p->S * stage > 200 * 1024) return LI_ERR_BAD_SHAPE;
+    // x staging (K floats + one pad per unit) borrows the first XB buffers
+    const size_t xbytes = ((size_t)K + K / unit_weights(wtype)) * sizeof(float);
+    p->XB = (int)((xbytes + stage - 1) / stage);
+    if (p->S < p->XB + 1) p->S = p->XB + 1;
+    if (p->S * stage > 200 * 1024) return LI_ERR_BAD_SHAPE;
     p->threads = p->UP * p->RP;
-    p->smem = p->S * stage + p->S * sizeof(uint64_t) + (size_t)p->SR * (p->UP / kWarp) * 2 * 4 + 16;
+    p->smem = p->S * stage + p->S * sizeof(uint64_t) + 2 * (size_t)p->SR * (p->UP / kWarp) * nw * 4 + 16;
     return 0;
+}
+
+// Resident CTAs per SM of a kernel at (threads, smem). The kernel's dynamic
+// shared-memory limit is raised to the device maximum once per (device,
+// kernel), and the occupancy is cached per (device, kernel, threads, smem),
+// so a launch makes no attribute or occupancy query after the first one
+// (launches stay cheap and graph-capturable).
+static int resident_ctas(const void *kern, int threads, size_t smem) {
+    struct Entry { int dev; const void *k; int threads; size_t smem; int per_sm; };
+    static std::mutex mu;
+    static std::vector<Entry> cache;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    bool raised = false;
+    for (const Entry &e : cache) {
+        if (e.dev == dev && e.k == kern) {
+            raised = true;
+            if (e.threads == threads && e.smem == smem) return e.per_sm;
+        }
+    }
+    cudaError_t e;
+    if (!raised) {
+        int max_optin = 0;
+        e = cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        if (e != cudaSuccess) return -(int)e;
+        cudaFuncAttributes fa;
+        e = cudaFuncGetAttributes(&fa, kern);
+        if (e != cudaSuccess) return -(int)e;
+        // the limit covers dynamic shared memory only; static usage counts against the total
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 max_optin - (int)fa.sharedSizeBytes);
+        if (e != cudaSuccess) return -(int)e;
+    }
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem);
+    if (e != cudaSuccess) return -(int)e;
+    cache.push_back({dev, kern, threads, smem, per_sm});
+    return per_sm;
+}
+
+template <int WT, int EPI, int R>
+static const void *pick_kernel(int) {
+    return (const void *)qgemv_kernel<WT, EPI, kMaxThreads, R>;
 }
 
 template <int WT, int EPI>
 static int launch_t(const QGemvArgs &a, int n_rows, cudaStream_t stream, bool pdl) {
-    auto kern = a.plan.threads <= 512 ? qgemv_kernel<WT, EPI, 512> : qgemv_kernel<WT, EPI, 1024>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)a.plan.smem);
-    if (e != cudaSuccess) return (int)e;
-    int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, a.plan.threads, a.plan.smem);
-    if (e != cudaSuccess) return (int)e;
+    const void *kern;
+    switch (a.plan.R) {
+    case 1: kern = pick_kernel<WT, EPI, 1>(a.plan.threads); break;
+    case 2: kern = pick_kernel<WT, EPI, 2>(a.plan.threads); break;
+    case 4: kern = pick_kernel<WT, EPI, 4>(a.plan.threads); break;
+    default:
+        if (EPI == kEpiSwiGLU) return LI_ERR_BAD_SHAPE;
+        kern = pick_kernel<WT, EPI, EPI == kEpiSwiGLU ? 4 : 8>(a.plan.threads);
+        break;
+    }
+    const int per_sm = resident_ctas(kern, a.plan.threads, a.plan.smem);
+    if (per_sm < 0) return -per_sm;
     if (per_sm < 1) return LI_ERR_BAD_SHAPE;
     const int n_stages = (a.plan.total_rows + a.plan.SR - 1) / a.plan.SR;
     int grid = num_sms() * per_sm;
     if (grid > n_stages) grid = n_stages;
-    e = launch_pdl(kern, dim3(grid, n_rows), dim3(a.plan.threads), a.plan.smem, stream, pdl, a);
-    return (int)e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, n_rows);
+    cfg.blockDim = dim3(a.plan.threads);
+    cfg.dynamicSmemBytes = a.plan.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void *params[] = {const_cast<QGemvArgs *>(&a)};
+    return (int)cudaLaunchKernelExC(&cfg, kern, params);
 }
 
 int qgemv_launch(const QGemvArgs &a, int n_rows, cudaStream_t stream, bool pdl) {
@@ -389,7 +534,7 @@ static int common_q_checks(int wtype, const void *x, const void *W, const void *
                            int n_rows) {
     if (!x || !W || !dst || K <= 0 || N < 0 || n_rows < 0) return LI_ERR_BAD_ARG;
     if (wtype != LI_WTYPE_Q8_0 && wtype != LI_WTYPE_Q4_K) return LI_ERR_UNSUPPORTED;
-    if (!aligned16(W)) return LI_ERR_MISALIGNED;
+    if (!aligned16(W) || !aligned16(x)) return LI_ERR_MISALIGNED;   // x rows are read as float4
     return 0;
 }
 
@@ -417,6 +562,7 @@ int li_launch_rms_norm_matmul_q(int wtype, const float *x, const float *gamma, c
                                 float *dst, int K, int N, int n_rows, float eps, void *stream) {
     int rc = common_q_checks(wtype, x, W, dst, K, N, n_rows);
     if (rc) return rc;
+    if (gamma && !aligned16(gamma)) return LI_ERR_MISALIGNED;
     if (N == 0 || n_rows == 0) return 0;
     QGemvArgs a = {};
     a.wtype = wtype; a.epi = kEpiStore;
@@ -435,6 +581,7 @@ int li_launch_fused_rms_norm_qkv_q(int wtype, const float *x, const float *gamma
     if (!rc) rc = common_q_checks(wtype, x, Wv, v, K, Nv, n_rows);
     if (rc) return rc;
     if (!gamma) return LI_ERR_BAD_ARG;
+    if (!aligned16(gamma)) return LI_ERR_MISALIGNED;
     const int total = Nq + Nk + Nv;
     if (total == 0 || n_rows == 0) return 0;
     QGemvArgs a = {};

@@ -13,7 +13,7 @@ enum QEpilogue {
 };
 
 struct QGemvPlan {
-    int U, UP, RP, SR, S, threads;
+    int U, UP, RP, R, SR, S, XB, threads;
     int total_rows;
     size_t row_bytes, smem;
 };
