@@ -50,6 +50,13 @@ enum li_wtype {
 #define LI_ERR_MISALIGNED     2005  /* pointer not 16-byte aligned          */
 #define LI_ERR_TIMEOUT        2006  /* a bounded device-side wait gave up   */
 #define LI_ERR_NO_CUDA        2007  /* built without CUDA (stub branch)     */
+#define LI_ERR_SCRATCH_LIMIT  2008  /* the call needs more scratch than the
+                                       library's static scratch array holds */
+
+/* Size of the library's own device scratch used by
+ * li_launch_deltanet_layer_decode_noalloc (8 MiB: up to 127 sequences of a
+ * layer with hidden 4096, 16 k-heads, 32 v-heads, head_dim 128). */
+#define LI_DELTANET_STATIC_SCRATCH_BYTES (8u << 20)
 
 /*
  * Recurrent DeltaNet layer for the fused decode entry. One layer's weights
@@ -241,6 +248,23 @@ size_t li_deltanet_layer_workspace_size(const li_deltanet_layer * L, int n_seqs)
 int li_launch_deltanet_layer_decode(const li_deltanet_layer * L,
         const float * x, float * y, float * conv_state, float * state,
         int n_seqs, void * workspace, size_t workspace_bytes, void * stream);
+
+/* The same layer decode step for callers that cannot allocate device memory
+ * for a workspace (for example a ggml graph whose buffers were all planned
+ * before this op, or a host runtime that owns every device allocation and
+ * passes only tensors and a stream). This entry has no counterpart in the
+ * reference. Its scratch is a device array inside the library
+ * (LI_DELTANET_STATIC_SCRATCH_BYTES, held by every GPU that loads the
+ * library until the process exits); the call allocates nothing. A call whose
+ * workspace would exceed it returns LI_ERR_SCRATCH_LIMIT without launching.
+ * The first call on a device looks up the array's device address (with that
+ * device current), so make that first call before any stream capture. All
+ * calls share the one array: calls that overlap on the GPU (for example on
+ * two streams at once) race on it and must be serialised by the caller.
+ * Nothing in the scratch needs to start at zero. */
+int li_launch_deltanet_layer_decode_noalloc(const li_deltanet_layer * L,
+        const float * x, float * y, float * conv_state, float * state,
+        int n_seqs, void * stream);
 
 #else  /* no CUDA: the reference's no-op stubs, plus stubs for the new entries */
 

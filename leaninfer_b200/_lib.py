@@ -22,6 +22,7 @@ STATUS_NAMES = {
     2005: "LI_ERR_MISALIGNED",
     2006: "LI_ERR_TIMEOUT",
     2007: "LI_ERR_NO_CUDA",
+    2008: "LI_ERR_SCRATCH_LIMIT",
 }
 
 
@@ -79,6 +80,8 @@ _SIGS = {
     "li_launch_deltanet_layer_decode": (
         c_int, [POINTER(DeltaNetLayer), c_void_p, c_void_p, c_void_p, c_void_p, c_int,
                 c_void_p, c_size_t, c_void_p]),
+    "li_launch_deltanet_layer_decode_noalloc": (
+        c_int, [POINTER(DeltaNetLayer), c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
 }
 
 _lib = None

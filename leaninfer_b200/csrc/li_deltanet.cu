@@ -36,6 +36,7 @@
 #include "li_qgemv.cuh"
 
 #include <cooperative_groups.h>
+#include <mutex>
 
 namespace cg = cooperative_groups;
 
@@ -466,3 +467,53 @@ int li_launch_deltanet_layer_decode(const li_deltanet_layer *L, const float *x, 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Layer decode with scratch in this library's own device memory.
+//
+// Some callers cannot hand the layer a workspace: a ggml graph whose buffers
+// the graph allocator planned before this op existed, a host runtime that
+// owns all device memory and passes a plugin only tensors and a stream, or a
+// decode loop where an allocation call (which waits for the device) is not
+// acceptable. For them the scratch is a file-scope device array of
+// LI_DELTANET_STATIC_SCRATCH_BYTES, which every GPU that loads the library
+// holds until the process exits. Host code cannot use the array's name as a
+// device address, so its address is looked up with cudaGetSymbolAddress once
+// per device, with that device current, on the first call made on it.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_layer_scratch[LI_DELTANET_STATIC_SCRATCH_BYTES];
+
+static int layer_scratch_address(void **out) {
+    static std::mutex mu;
+    static void *addr[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= 64) return LI_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_layer_scratch);
+        if (e != cudaSuccess) return (int)e;
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return 0;
+}
+
+extern "C" int li_launch_deltanet_layer_decode_noalloc(const li_deltanet_layer *L, const float *x,
+                                                       float *y, float *conv_state, float *state,
+                                                       int n_seqs, void *stream) {
+    if (!L || n_seqs < 0) return LI_ERR_BAD_ARG;
+    if (n_seqs == 0) return 0;
+    // Every byte of the scratch that a launch reads is written earlier in the
+    // same launch, so nothing has to start at zero; the array keeps the last
+    // call's contents.
+    if (li_deltanet_layer_workspace_size(L, n_seqs) > (size_t)LI_DELTANET_STATIC_SCRATCH_BYTES)
+        return LI_ERR_SCRATCH_LIMIT;
+    void *ws = nullptr;
+    const int rc = layer_scratch_address(&ws);
+    if (rc) return rc;
+    return li_launch_deltanet_layer_decode(L, x, y, conv_state, state, n_seqs, ws,
+                                           (size_t)LI_DELTANET_STATIC_SCRATCH_BYTES, stream);
+}
