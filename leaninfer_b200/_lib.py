@@ -70,7 +70,7 @@ _SIGS = {
         c_int, [c_int] + [c_void_p] * 8 + [c_int] * 5 + [c_float, c_void_p]),
     "li_launch_fused_rms_norm_swiglu_q": (
         c_int, [c_int] + [c_void_p] * 5 + [c_int, c_int, c_int, c_float, c_void_p]),
-    "li_fused_ffn_workspace_size": (c_size_t, [c_int, c_int]),
+    "li_fused_ffn_workspace_size": (c_size_t, [c_int, c_int, c_int]),
     "li_launch_fused_ffn_q": (
         c_int, [c_int] + [c_void_p] * 6 + [c_int, c_int, c_int, c_float, c_void_p, c_size_t, c_void_p]),
     "li_launch_deltanet_recurrent_f32": (

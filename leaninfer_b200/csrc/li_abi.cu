@@ -6,6 +6,7 @@
 int li_tu_status_dense(int clear);
 int li_tu_status_qgemv(int clear);
 int li_tu_status_deltanet(int clear);
+int li_tu_status_tcgemm(int clear);
 
 namespace li {
 
@@ -66,6 +67,7 @@ int li_device_status(void) {
     if ((v = li_tu_status_dense(1)) && !s) s = v;
     if ((v = li_tu_status_qgemv(1)) && !s) s = v;
     if ((v = li_tu_status_deltanet(1)) && !s) s = v;
+    if ((v = li_tu_status_tcgemm(1)) && !s) s = v;
     return s;
 }
 

@@ -34,6 +34,7 @@
 // kernel 2 runs the previous step's kernels have all completed.
 #include "li_common.cuh"
 #include "li_qgemv.cuh"
+#include "li_tcgemm.cuh"
 
 #include <cooperative_groups.h>
 #include <mutex>
@@ -61,7 +62,8 @@ struct RecArgs {
     int NI, Hk, C;
     const float *a_log, *dt_bias, *norm_w;
     float l2_eps, norm_eps;
-    float *o_gated;         // [B][Hv*D]
+    float *o_gated;         // [B][Hv*D] fp32, or
+    __half *o_gated16;      // [B][Hv*D] f16 (the tensor-core out-projection's operand)
 };
 
 template <int D>
@@ -244,8 +246,10 @@ recurrent_kernel(RecArgs a) {
                 const int r = threadIdx.x;
                 const float rs = rsqrtf(tot / (float)D + a.norm_eps);
                 const float z = a.proj[(size_t)seq * a.NI + a.C + h * D + row0 + r];
-                a.o_gated[((size_t)seq * a.n_heads + h) * D + row0 + r] =
-                    silu(z) * (o * a.norm_w[row0 + r] * rs);
+                const float og = silu(z) * (o * a.norm_w[row0 + r] * rs);
+                const size_t oi = ((size_t)seq * a.n_heads + h) * D + row0 + r;
+                if (a.o_gated16) a.o_gated16[oi] = __float2half_rn(og);
+                else a.o_gated[oi] = og;
             }
         }
 
@@ -404,13 +408,18 @@ void li_launch_fused_deltanet_recurrent_out_f32(const float *q, const float *k, 
     set_last_error(rc);
 }
 
+// Workspace regions, each 256-byte aligned:
+//   SIMT path (n_seqs < kTcMinRows):   proj f32 [B][NI] | og f32 [B][Hv*D]
+//   tensor path (n_seqs >= kTcMinRows): proj f32 [B][NI] | x16 f16 [B][hidden] |
+//                                       xscale f32 [B] | og16 f16 [B][Hv*D]
+static size_t al256(size_t v) { return (v + 255) / 256 * 256; }
+
 size_t li_deltanet_layer_workspace_size(const li_deltanet_layer *L, int n_seqs) {
     if (!L || n_seqs <= 0) return 0;
-    const size_t D = L->head_dim, Hk = L->n_k_heads, Hv = L->n_v_heads;
+    const size_t D = L->head_dim, Hk = L->n_k_heads, Hv = L->n_v_heads, n = (size_t)n_seqs;
     const size_t NI = 2 * Hk * D + 2 * Hv * D + 2 * Hv;
-    const size_t a = (NI * n_seqs * 4 + 255) / 256 * 256;
-    const size_t b = (Hv * D * n_seqs * 4 + 255) / 256 * 256;
-    return a + b;
+    if (n_seqs < li::kTcMinRows) return al256(NI * n * 4) + al256(Hv * D * n * 4);
+    return al256(NI * n * 4) + al256((size_t)L->hidden * n * 2) + al256(n * 4) + al256(Hv * D * n * 2);
 }
 
 int li_launch_deltanet_layer_decode(const li_deltanet_layer *L, const float *x, float *y,
@@ -429,41 +438,72 @@ int li_launch_deltanet_layer_decode(const li_deltanet_layer *L, const float *x, 
     const int D = L->head_dim, Hk = L->n_k_heads, Hv = L->n_v_heads;
     const int C = 2 * Hk * D + Hv * D;
     const int NI = C + Hv * D + 2 * Hv;
-    float *proj = (float *)workspace;
-    float *og = (float *)((char *)workspace + ((size_t)NI * n_seqs * 4 + 255) / 256 * 256);
+    const size_t n = (size_t)n_seqs;
+    char *ws = (char *)workspace;
+    float *proj = (float *)ws;
     const cudaStream_t s = (cudaStream_t)stream;
+    const bool tc = n_seqs >= kTcMinRows;
+    int rc;
 
-    // 1. in-projection + conv1d/SiLU epilogue (not a dependent launch)
-    QGemvArgs in = {};
-    in.wtype = L->w_in_type; in.epi = kEpiConv;
-    int rc = qgemv_plan(L->w_in_type, L->hidden, NI, kEpiConv, &in.plan);
-    if (rc) return rc;
-    in.x = x; in.x_stride = L->hidden; in.gamma = L->in_norm_w; in.K = L->hidden;
-    in.eps = L->in_norm_eps; in.n_seg = 1; in.W[0] = L->w_in; in.seg_rows[0] = NI;
-    in.dst[0] = proj; in.dst_stride[0] = NI;
-    in.conv_w = L->conv_w; in.conv_state = conv_state; in.conv_channels = C;
-    if ((rc = qgemv_launch(in, n_seqs, s, false))) return rc;
-
-    // 2. recurrence + L2 norm + gated RMSNorm (dependent launch)
     RecArgs a = {};
     a.state_in = state; a.state_out = state;
     a.n_tokens = 1; a.n_heads = Hv; a.gqa = Hv / Hk; a.n_seqs = n_seqs;
     a.repeat_type = L->repeat_type;
     a.proj = proj; a.NI = NI; a.Hk = Hk; a.C = C;
     a.a_log = L->a_log; a.dt_bias = L->dt_bias; a.norm_w = L->norm_w;
-    a.l2_eps = L->l2_eps; a.norm_eps = L->norm_eps; a.o_gated = og;
+    a.l2_eps = L->l2_eps; a.norm_eps = L->norm_eps;
     const int rb = pick_rows((int64_t)n_seqs * Hv, 128);
+
+    if (!tc) {
+        float *og = (float *)(ws + al256((size_t)NI * n * 4));
+        // 1. in-projection + conv1d/SiLU epilogue (not a dependent launch)
+        QGemvArgs in = {};
+        in.wtype = L->w_in_type; in.epi = kEpiConv;
+        if ((rc = qgemv_plan(L->w_in_type, L->hidden, NI, kEpiConv, &in.plan))) return rc;
+        in.x = x; in.x_stride = L->hidden; in.gamma = L->in_norm_w; in.K = L->hidden;
+        in.eps = L->in_norm_eps; in.n_seg = 1; in.W[0] = L->w_in; in.seg_rows[0] = NI;
+        in.dst[0] = proj; in.dst_stride[0] = NI;
+        in.conv_w = L->conv_w; in.conv_state = conv_state; in.conv_channels = C;
+        if ((rc = qgemv_launch(in, n_seqs, s, false))) return rc;
+        // 2. recurrence + L2 norm + gated RMSNorm (dependent launch)
+        a.o_gated = og;
+        rc = rb == 32 ? launch_layer_rec<32>(a, s) : rb == 64 ? launch_layer_rec<64>(a, s) : launch_layer_rec<128>(a, s);
+        if (rc) return rc;
+        // 3. out-projection (dependent launch)
+        QGemvArgs out = {};
+        out.wtype = L->w_out_type; out.epi = kEpiStore;
+        if ((rc = qgemv_plan(L->w_out_type, Hv * D, L->hidden, kEpiStore, &out.plan))) return rc;
+        out.x = og; out.x_stride = Hv * D; out.gamma = nullptr; out.K = Hv * D; out.eps = 0.f;
+        out.n_seg = 1; out.W[0] = L->w_out; out.seg_rows[0] = L->hidden;
+        out.dst[0] = y; out.dst_stride[0] = L->hidden;
+        return qgemv_launch(out, n_seqs, s, true);
+    }
+
+    // tensor-core path: x -> f16, in-projection GEMM (+conv), recurrence
+    // (gated heads written as f16), out-projection GEMM
+    size_t off = al256((size_t)NI * n * 4);
+    __half *x16 = (__half *)(ws + off);
+    off += al256((size_t)L->hidden * n * 2);
+    float *xscale = (float *)(ws + off);
+    off += al256(n * 4);
+    __half *og16 = (__half *)(ws + off);
+    if ((rc = tc_prep_launch(x, L->hidden, L->in_norm_w, L->in_norm_eps, n_seqs, L->hidden, x16, xscale, s,
+                             false)))
+        return rc;
+    TcArgs in = {};
+    in.wtype = L->w_in_type; in.epi = kTcConv; in.K = L->hidden; in.total_rows = NI; in.B = n_seqs;
+    in.W[0] = L->w_in; in.n_seg = 1; in.seg_rows[0] = NI; in.dst[0] = proj; in.dst_stride[0] = NI;
+    in.X16 = x16; in.xscale = xscale;
+    in.conv_w = L->conv_w; in.conv_state = conv_state; in.conv_channels = C;
+    if ((rc = tc_gemm_launch(in, s, true))) return rc;
+    a.o_gated16 = og16;
     rc = rb == 32 ? launch_layer_rec<32>(a, s) : rb == 64 ? launch_layer_rec<64>(a, s) : launch_layer_rec<128>(a, s);
     if (rc) return rc;
-
-    // 3. out-projection (dependent launch)
-    QGemvArgs out = {};
-    out.wtype = L->w_out_type; out.epi = kEpiStore;
-    if ((rc = qgemv_plan(L->w_out_type, Hv * D, L->hidden, kEpiStore, &out.plan))) return rc;
-    out.x = og; out.x_stride = Hv * D; out.gamma = nullptr; out.K = Hv * D; out.eps = 0.f;
-    out.n_seg = 1; out.W[0] = L->w_out; out.seg_rows[0] = L->hidden;
-    out.dst[0] = y; out.dst_stride[0] = L->hidden;
-    return qgemv_launch(out, n_seqs, s, true);
+    TcArgs out = {};
+    out.wtype = L->w_out_type; out.epi = kTcStore; out.K = Hv * D; out.total_rows = L->hidden; out.B = n_seqs;
+    out.W[0] = L->w_out; out.n_seg = 1; out.seg_rows[0] = L->hidden; out.dst[0] = y;
+    out.dst_stride[0] = L->hidden; out.X16 = og16; out.xscale = nullptr;
+    return tc_gemm_launch(out, s, true);
 }
 
 }  // extern "C"

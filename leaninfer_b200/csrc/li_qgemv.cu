@@ -35,6 +35,7 @@
 //     are requested before griddepcontrol.wait, x after it.
 #include "li_common.cuh"
 #include "li_qgemv.cuh"
+#include "li_tcgemm.cuh"
 
 #include <mutex>
 #include <vector>
@@ -612,9 +613,17 @@ int li_launch_fused_rms_norm_swiglu_q(int wtype, const float *x, const float *ga
     return qgemv_launch(a, n_rows, (cudaStream_t)stream, false);
 }
 
-size_t li_fused_ffn_workspace_size(int N, int n_rows) {
-    if (N <= 0 || n_rows <= 0) return 0;
-    return ((size_t)N * n_rows * sizeof(float) + 255) / 256 * 256;
+// Workspace regions, 256-byte aligned: h f32 [n_rows][N]; and for
+// n_rows >= kTcMinRows (tensor-core path) also x16 f16 [n_rows][K],
+// xscale [n_rows], h16 f16 [n_rows][N], hscale [n_rows].
+static size_t al256(size_t v) { return (v + 255) / 256 * 256; }
+
+size_t li_fused_ffn_workspace_size(int K, int N, int n_rows) {
+    if (K <= 0 || N <= 0 || n_rows <= 0) return 0;
+    const size_t n = (size_t)n_rows;
+    size_t b = al256((size_t)N * n * 4);
+    if (n_rows >= kTcMinRows) b += al256((size_t)K * n * 2) + al256(n * 4) + al256((size_t)N * n * 2) + al256(n * 4);
+    return b;
 }
 
 int li_launch_fused_ffn_q(int wtype, const float *x, const float *gamma, const void *Wg,
@@ -625,22 +634,46 @@ int li_launch_fused_ffn_q(int wtype, const float *x, const float *gamma, const v
     if (!rc) rc = common_q_checks(wtype, x, Wd, y, N, K, n_rows);
     if (rc) return rc;
     if (N == 0 || n_rows == 0) return 0;
-    if (!workspace || workspace_bytes < li_fused_ffn_workspace_size(N, n_rows))
+    if (!workspace || workspace_bytes < li_fused_ffn_workspace_size(K, N, n_rows))
         return LI_ERR_WORKSPACE;
-    float *h = (float *)workspace;
+    if (gamma && !aligned16(gamma)) return LI_ERR_MISALIGNED;
+    const cudaStream_t s = (cudaStream_t)stream;
+    char *ws = (char *)workspace;
+    float *h = (float *)ws;
+    if (n_rows >= kTcMinRows && n_rows <= 256 && K % 256 == 0 && N % 256 == 0) {
+        // tensor-core path: x -> f16, gate/up GEMM + SwiGLU, h -> f16, down GEMM
+        const size_t n = (size_t)n_rows;
+        size_t off = al256((size_t)N * n * 4);
+        __half *x16 = (__half *)(ws + off); off += al256((size_t)K * n * 2);
+        float *xs = (float *)(ws + off);    off += al256(n * 4);
+        __half *h16 = (__half *)(ws + off); off += al256((size_t)N * n * 2);
+        float *hs = (float *)(ws + off);
+        if ((rc = tc_prep_launch(x, K, gamma, eps, n_rows, K, x16, xs, s, false))) return rc;
+        TcArgs g = {};
+        g.wtype = wtype; g.epi = kTcSwiGLU; g.K = K; g.total_rows = N; g.B = n_rows;
+        g.W[0] = Wg; g.W[1] = Wu; g.n_seg = 1; g.seg_rows[0] = N; g.dst[0] = h; g.dst_stride[0] = N;
+        g.X16 = x16; g.xscale = xs;
+        if ((rc = tc_gemm_launch(g, s, true))) return rc;
+        if ((rc = tc_prep_launch(h, N, nullptr, 0.f, n_rows, N, h16, hs, s, true))) return rc;
+        TcArgs d = {};
+        d.wtype = wtype; d.epi = kTcStore; d.K = N; d.total_rows = K; d.B = n_rows;
+        d.W[0] = Wd; d.n_seg = 1; d.seg_rows[0] = K; d.dst[0] = y; d.dst_stride[0] = K;
+        d.X16 = h16; d.xscale = hs;
+        return tc_gemm_launch(d, s, true);
+    }
     QGemvArgs a = {};
     a.wtype = wtype; a.epi = kEpiSwiGLU;
     if ((rc = qgemv_plan(wtype, K, N, kEpiSwiGLU, &a.plan))) return rc;
     a.x = x; a.x_stride = K; a.gamma = gamma; a.K = K; a.eps = eps;
     a.n_seg = 1; a.W[0] = Wg; a.W[1] = Wu; a.seg_rows[0] = N;
     a.dst[0] = h; a.dst_stride[0] = N;
-    if ((rc = qgemv_launch(a, n_rows, (cudaStream_t)stream, false))) return rc;
-    QGemvArgs d = {};
-    d.wtype = wtype; d.epi = kEpiStore;
-    if ((rc = qgemv_plan(wtype, N, K, kEpiStore, &d.plan))) return rc;
-    d.x = h; d.x_stride = N; d.gamma = nullptr; d.K = N; d.eps = 0.f;
-    d.n_seg = 1; d.W[0] = Wd; d.seg_rows[0] = K; d.dst[0] = y; d.dst_stride[0] = K;
-    return qgemv_launch(d, n_rows, (cudaStream_t)stream, true);
+    if ((rc = qgemv_launch(a, n_rows, s, false))) return rc;
+    QGemvArgs dn = {};
+    dn.wtype = wtype; dn.epi = kEpiStore;
+    if ((rc = qgemv_plan(wtype, N, K, kEpiStore, &dn.plan))) return rc;
+    dn.x = h; dn.x_stride = N; dn.gamma = nullptr; dn.K = N; dn.eps = 0.f;
+    dn.n_seg = 1; dn.W[0] = Wd; dn.seg_rows[0] = K; dn.dst[0] = y; dn.dst_stride[0] = K;
+    return qgemv_launch(dn, n_rows, s, true);
 }
 
 }  // extern "C"

@@ -157,7 +157,7 @@ def rms_norm_swiglu_q(wtype, x, gamma, Wg, Wu, N: int, eps: float = 1e-6):
 def ffn_q(wtype, x, gamma, Wg, Wu, Wd, N: int, eps: float = 1e-6, workspace=None, out=None):
     n_rows, K = x.shape
     lib = _lib.load()
-    ws_bytes = int(lib.li_fused_ffn_workspace_size(N, n_rows))
+    ws_bytes = int(lib.li_fused_ffn_workspace_size(K, N, n_rows))
     if workspace is None:
         workspace = torch.empty(ws_bytes, device=x.device, dtype=torch.uint8)
     y = out if out is not None else torch.empty(n_rows, K, device=x.device, dtype=torch.float32)

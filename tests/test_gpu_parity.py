@@ -140,12 +140,14 @@ def test_matmul_q_shapes(cuda, oracle_mod, wtype, n_rows):
 
 
 @pytest.mark.parametrize("wtype", [8, 12])
-def test_ffn_q(cuda, oracle_mod, wtype):
-    """RMSNorm + SwiGLU gate/up + down, reduced width (K=1024, N=3072)."""
+@pytest.mark.parametrize("n_rows", [2, 8, 32])
+def test_ffn_q(cuda, oracle_mod, wtype, n_rows):
+    """RMSNorm + SwiGLU gate/up + down, reduced width (K=1024, N=3072); from 8
+    rows on the gate/up and down contractions run on the tensor cores."""
     from leaninfer_b200 import ops, synth
-    r = rng(300 + wtype)
+    r = rng(300 + wtype + n_rows)
     K, N_ = 1024, 3072
-    x = r.standard_normal((2, K)).astype(np.float32)
+    x = r.standard_normal((n_rows, K)).astype(np.float32)
     gamma = r.uniform(0.5, 1.5, K).astype(np.float32)
     Wg, Wu = synth.random_weights(r, wtype, N_, K), synth.random_weights(r, wtype, N_, K)
     Wd = synth.random_weights(r, wtype, K, N_)
@@ -275,6 +277,9 @@ def _layer(cuda, w, repeat_type=0, in_norm_w=None):
     (12, 2, 1024, 4, 8, 0),
     (8, 3, 1024, 2, 8, 1),
     (12, 1, 4096, 16, 32, 0),      # the decode workload's layer shape
+    (12, 8, 1024, 4, 8, 0),        # tensor-core projections from here on
+    (8, 16, 1024, 2, 8, 1),
+    (12, 64, 4096, 16, 32, 0),     # the decode workload: layer shape and batch
 ])
 def test_layer_decode_steps(cuda, oracle_mod, wtype, B, hidden, Hk, Hv, repeat_type):
     import torch
