@@ -132,7 +132,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity), "r"(20000u)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(10000000u)
         : "memory");
     return ok != 0;
 }

@@ -64,6 +64,8 @@ struct RecArgs {
     float l2_eps, norm_eps;
     float *o_gated;         // [B][Hv*D] fp32, or
     __half *o_gated16;      // [B][Hv*D] f16 (the tensor-core out-projection's operand)
+    float *zero_out;        // layer output to clear for a K-split out-projection, or nullptr
+    int64_t zero_len;       // floats in zero_out
 };
 
 template <int D>
@@ -130,6 +132,13 @@ recurrent_kernel(RecArgs a) {
     if (LAYER) {
         grid_dep_launch_dependents();
         grid_dep_wait();
+        if (a.zero_out) {
+            // the out-projection that follows adds K-split partials into it
+            const int64_t per = (a.zero_len + gridDim.x - 1) / gridDim.x;
+            const int64_t z0 = (int64_t)blockIdx.x * per;
+            const int64_t z1 = z0 + per < a.zero_len ? z0 + per : a.zero_len;
+            for (int64_t i = z0 + threadIdx.x; i < z1; i += blockDim.x) a.zero_out[i] = 0.f;
+        }
     }
 
     for (int64_t t = 0; t < a.n_tokens; ++t) {
@@ -496,13 +505,17 @@ int li_launch_deltanet_layer_decode(const li_deltanet_layer *L, const float *x, 
     in.X16 = x16; in.xscale = xscale;
     in.conv_w = L->conv_w; in.conv_state = conv_state; in.conv_channels = C;
     if ((rc = tc_gemm_launch(in, s, true))) return rc;
-    a.o_gated16 = og16;
-    rc = rb == 32 ? launch_layer_rec<32>(a, s) : rb == 64 ? launch_layer_rec<64>(a, s) : launch_layer_rec<128>(a, s);
-    if (rc) return rc;
     TcArgs out = {};
     out.wtype = L->w_out_type; out.epi = kTcStore; out.K = Hv * D; out.total_rows = L->hidden; out.B = n_seqs;
     out.W[0] = L->w_out; out.n_seg = 1; out.seg_rows[0] = L->hidden; out.dst[0] = y;
     out.dst_stride[0] = L->hidden; out.X16 = og16; out.xscale = nullptr;
+    a.o_gated16 = og16;
+    if (tc_gemm_splits_k(out)) {
+        a.zero_out = y;
+        a.zero_len = (int64_t)n_seqs * L->hidden;
+    }
+    rc = rb == 32 ? launch_layer_rec<32>(a, s) : rb == 64 ? launch_layer_rec<64>(a, s) : launch_layer_rec<128>(a, s);
+    if (rc) return rc;
     return tc_gemm_launch(out, s, true);
 }
 

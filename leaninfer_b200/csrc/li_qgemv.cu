@@ -648,6 +648,14 @@ int li_launch_fused_ffn_q(int wtype, const float *x, const float *gamma, const v
         float *xs = (float *)(ws + off);    off += al256(n * 4);
         __half *h16 = (__half *)(ws + off); off += al256((size_t)N * n * 2);
         float *hs = (float *)(ws + off);
+        TcArgs d = {};
+        d.wtype = wtype; d.epi = kTcStore; d.K = N; d.total_rows = K; d.B = n_rows;
+        d.W[0] = Wd; d.n_seg = 1; d.seg_rows[0] = K; d.dst[0] = y; d.dst_stride[0] = K;
+        d.X16 = h16; d.xscale = hs;
+        if (tc_gemm_splits_k(d)) {   // the down projection adds K-split partials into y
+            const cudaError_t e = cudaMemsetAsync(y, 0, (size_t)n_rows * K * sizeof(float), s);
+            if (e != cudaSuccess) return (int)e;
+        }
         if ((rc = tc_prep_launch(x, K, gamma, eps, n_rows, K, x16, xs, s, false))) return rc;
         TcArgs g = {};
         g.wtype = wtype; g.epi = kTcSwiGLU; g.K = K; g.total_rows = N; g.B = n_rows;
@@ -655,10 +663,6 @@ int li_launch_fused_ffn_q(int wtype, const float *x, const float *gamma, const v
         g.X16 = x16; g.xscale = xs;
         if ((rc = tc_gemm_launch(g, s, true))) return rc;
         if ((rc = tc_prep_launch(h, N, nullptr, 0.f, n_rows, N, h16, hs, s, true))) return rc;
-        TcArgs d = {};
-        d.wtype = wtype; d.epi = kTcStore; d.K = N; d.total_rows = K; d.B = n_rows;
-        d.W[0] = Wd; d.n_seg = 1; d.seg_rows[0] = K; d.dst[0] = y; d.dst_stride[0] = K;
-        d.X16 = h16; d.xscale = hs;
         return tc_gemm_launch(d, s, true);
     }
     QGemvArgs a = {};

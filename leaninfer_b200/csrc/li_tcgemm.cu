@@ -5,16 +5,17 @@
 // per CTA tile), the batch is N (padded to a multiple of 32, up to 256).
 //
 // One CTA per 128-row weight tile, 10 warps:
-//   warp 8  producer: 2-D tiled TMA of raw weight blocks ([128 rows] x one
+//   warp 4G producer: 2-D tiled TMA of raw weight blocks ([128 rows] x one
 //           256-value column: 144 B Q4_K / 272 B Q8_0 per row) and of the f16
 //           X tile (64 k x N rows, 128-byte swizzle) into shared-memory rings;
-//   warps 0-7 dequant: raw blocks -> f16 weights written in the canonical
+//   warps 0..4G-1 dequant: raw blocks -> f16 weights written in the canonical
 //           K-major 128B-swizzled UMMA layout (one 16-byte granule per store,
-//           bank-conflict free); group 0 takes even, group 1 odd k-blocks;
-//   warp 9  MMA: allocates TMEM, issues tcgen05.mma kind::f16 (fp32
+//           bank-conflict free); group g (4 warps, one row each per
+//           thread) takes k-blocks g, g+G, ... into A slot g (G = 2 or 4);
+//   warp 4G+1 MMA: allocates TMEM, issues tcgen05.mma kind::f16 (fp32
 //           accumulators in TMEM, N columns per weight matrix), commits slot
 //           releases to mbarriers;
-//   warps 0-7 epilogue: tcgen05.ld 32x32b of their TMEM lane quarter, scale by
+//   warps 0..4G-1 epilogue: tcgen05.ld 32x32b of their TMEM lane quarter, scale by
 //           the X row scale, store / SwiGLU / DeltaNet conv epilogue.
 // Dequant: nibbles / bytes become f16 through the 0x6400 magic-exponent form
 // (one byte permute + one LOP3 per pair), then (q - 1024) * d*sc - dmin*m in
@@ -40,10 +41,12 @@ namespace li {
 namespace {
 
 constexpr int kBM = 128;                 // weight rows per tile
-constexpr int kDeqWarps = 8;
-constexpr int kThreads = (kDeqWarps + 2) * kWarp;
-constexpr int kProducerWarp = kDeqWarps;
-constexpr int kMmaWarp = kDeqWarps + 1;
+// Dequant groups of 4 warps (one tile row per thread). The group count G
+// equals the number of A slots (2 or 4): group g owns slot g and its
+// k-blocks g, g+G, ..., so each slot's successive phases are produced and
+// awaited by one group and no parity wait can run two phases ahead.
+constexpr int kMaxGroups = 4;
+constexpr int kMaxThreads = (4 * kMaxGroups + 2) * kWarp;
 constexpr int kMaxSmem = 227 * 1024;
 
 struct TcPlan {
@@ -55,6 +58,8 @@ struct TcPlan {
     int seg_tiles[3];
     int tmem_cols;
     int n_raw;       // raw stages (K / 256)
+    int ks;          // K splits (CTAs per tile); > 1 only for kTcStore, reduced with fp32 red.add
+    int raw_per_split;
     uint32_t off_a, off_x, off_raw, off_bar;
     size_t smem;
 };
@@ -118,6 +123,13 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
           "=r"(r[15])
         : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
@@ -233,7 +245,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, vo
 }
 
 template <int WT, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kMaxThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__ CUtensorMap tmW1,
                const __grid_constant__ CUtensorMap tmW2, const __grid_constant__ CUtensorMap tmX,
                TcArgs a, TcPlan p) {
@@ -242,6 +254,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
     uint8_t *smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     constexpr int NW = EPI == kTcSwiGLU ? 2 : 1;
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+    const int G = p.AS;                                   // dequant groups = A slots
+    const int deq_warps = 4 * G, producer_warp = deq_warps, mma_warp = deq_warps + 1;
 
     uint8_t *a_ring = smem + p.off_a;      // [AS][NW][16 KB]
     uint8_t *x_ring = smem + p.off_x;      // [XS][Npad*128]
@@ -254,33 +268,42 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(acc_full + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
-    // tile -> (segment, first row)
-    int seg = 0, tile = blockIdx.x;
-    while (seg < a.n_seg - 1 && tile >= p.seg_tiles[seg]) tile -= p.seg_tiles[seg++];
+    // CTA -> (segment, first row, K split)
+    const int split = (int)blockIdx.x % p.ks;
+    int tile = (int)blockIdx.x / p.ks, seg = 0;
+    if (a.n_seg > 1 && tile >= p.seg_tiles[0]) {
+        tile -= p.seg_tiles[0];
+        seg = 1;
+        if (a.n_seg > 2 && tile >= p.seg_tiles[1]) { tile -= p.seg_tiles[1]; seg = 2; }
+    }
     const int row0 = tile * kBM;
-    const int seg_rows = a.seg_rows[seg];
+    const int seg_rows = seg == 0 ? a.seg_rows[0] : (seg == 1 ? a.seg_rows[1] : a.seg_rows[2]);
+    float *const dseg = seg == 0 ? a.dst[0] : (seg == 1 ? a.dst[1] : a.dst[2]);
+    const int dstride = seg == 0 ? a.dst_stride[0] : (seg == 1 ? a.dst_stride[1] : a.dst_stride[2]);
     const CUtensorMap *tmA = seg == 0 ? &tmW0 : (seg == 1 ? &tmW1 : &tmW2);
     const CUtensorMap *tmB = &tmW1;                       // SwiGLU: up matrix
-    const int nkb = p.n_raw * 4;                          // 64-value k-blocks
+    const int r_base = split * p.raw_per_split;           // first raw stage (256 k) of this CTA
+    const int n_raw = p.raw_per_split;
+    const int nkb = n_raw * 4;                            // 64-value k-blocks
     const uint32_t raw_stage_bytes = (uint32_t)(kBM * p.RB);
     const uint32_t x_slot_bytes = (uint32_t)(p.Npad * 128);
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < p.RS; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], kDeqWarps); }
+        for (int i = 0; i < p.RS; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], deq_warps); }   // every dequant warp once per raw stage
         for (int i = 0; i < p.AS; ++i) { mbar_init(&a_full[i], kBM); mbar_init(&a_empty[i], 1); }
         for (int i = 0; i < p.XS; ++i) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 1); }
         mbar_init(acc_full, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
-    if (warp == kMmaWarp) tmem_alloc(tmem_holder, (uint32_t)p.tmem_cols);
+    if (warp == mma_warp) tmem_alloc(tmem_holder, (uint32_t)p.tmem_cols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
     grid_dep_launch_dependents();
 
-    if (warp == kProducerWarp) {
+    if (warp == producer_warp) {
         if (lane == 0) {
             int issued_raw = 0, issued_x = 0;
             auto issue_raw = [&](int r) {
@@ -289,13 +312,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
                     return false;
                 mbar_arrive_expect_tx(&raw_full[s], (uint32_t)NW * raw_stage_bytes);
                 uint8_t *dst = raw_ring + (size_t)s * NW * raw_stage_bytes;
-                tma_load_2d(dst, tmA, r * (p.RB / 2), row0, &raw_full[s]);
-                if (NW == 2) tma_load_2d(dst + raw_stage_bytes, tmB, r * (p.RB / 2), row0, &raw_full[s]);
+                tma_load_2d(dst, tmA, (r_base + r) * (p.RB / 2), row0, &raw_full[s]);
+                if (NW == 2) tma_load_2d(dst + raw_stage_bytes, tmB, (r_base + r) * (p.RB / 2), row0, &raw_full[s]);
                 issued_raw = r + 1;
                 return true;
             };
             // weights do not depend on the previous kernel: prefetch them first
-            const int pre = p.RS < p.n_raw ? p.RS : p.n_raw;
+            const int pre = p.RS < n_raw ? p.RS : n_raw;
             for (int r = 0; r < pre; ++r) issue_raw(r);
             grid_dep_wait();
             for (int kb = 0; kb < nkb && !*abort_flag; ++kb) {
@@ -303,11 +326,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
                 if (kb >= p.XS && !wait_or_abort(&x_empty[s], (uint32_t)(((kb / p.XS) - 1) & 1), abort_flag))
                     break;
                 mbar_arrive_expect_tx(&x_full[s], x_slot_bytes);
-                tma_load_2d(x_ring + (size_t)s * x_slot_bytes, &tmX, kb * 64, 0, &x_full[s]);
+                tma_load_2d(x_ring + (size_t)s * x_slot_bytes, &tmX, (r_base * 4 + kb) * 64, 0, &x_full[s]);
                 issued_x = kb + 1;
                 // keep the raw ring RS stages ahead of the X stream
                 const int want = kb / 4 + p.RS;
-                while (issued_raw < p.n_raw && issued_raw < want && !*abort_flag) issue_raw(issued_raw);
+                while (issued_raw < n_raw && issued_raw < want && !*abort_flag) issue_raw(issued_raw);
             }
             // drain: every copy this CTA issued has landed before it exits
             for (int r = issued_raw - p.RS < 0 ? 0 : issued_raw - p.RS; r < issued_raw; ++r)
@@ -315,7 +338,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
             for (int kb = issued_x - p.XS < 0 ? 0 : issued_x - p.XS; kb < issued_x; ++kb)
                 mbar_wait(&x_full[kb % p.XS], (uint32_t)((kb / p.XS) & 1));
         }
-    } else if (warp == kMmaWarp) {
+    } else if (warp == mma_warp) {
         if (lane == 0) {
             const uint32_t idesc = idesc_f16(p.Npad);
             for (int kb = 0; kb < nkb; ++kb) {
@@ -339,9 +362,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
         }
     } else {
         // ---------------- dequant warps ----------------
-        const int grp = warp / 4;                 // 0: even k-blocks, 1: odd
+        const int grp = warp / 4;                 // k-blocks grp, grp+G, ...
         const int m = threadIdx.x % kBM;          // tile row
-        for (int kb = grp; kb < nkb; kb += 2) {
+        for (int kb = grp; kb < nkb; kb += G) {
             const int r = kb / 4, sub = kb % 4;
             const int rs = r % p.RS, as = kb % p.AS;
             if (!wait_or_abort(&raw_full[rs], (uint32_t)((r / p.RS) & 1), abort_flag)) break;
@@ -357,7 +380,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
             }
             fence_proxy_async_shared();           // generic-proxy writes -> tensor core reads
             mbar_arrive(&a_full[as]);
-            if (sub == 2 + grp) {                 // this group's last k-block of the raw stage
+            if (sub + G >= 4) {                   // the group's last k-block of this raw stage
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&raw_empty[rs]);
             }
@@ -367,42 +390,52 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
         grid_dep_wait();                          // outputs may be read by the previous kernel
         const bool ok = wait_or_abort(acc_full, 0u, abort_flag);
         tc_fence_after();
-        const int q = warp & 3, half = warp >> 2;
+        const int q = warp & 3, part = warp >> 2;
         const int rloc = 32 * q + lane;           // tile row of this thread's TMEM lane
         const int row = row0 + rloc;
         const bool row_ok = ok && row < seg_rows;
         float4 cw = make_float4(0.f, 0.f, 0.f, 0.f);
         if (EPI == kTcConv && row_ok && row < a.conv_channels)
             cw = *reinterpret_cast<const float4 *>(a.conv_w + 4 * (size_t)row);
-        const int cols = p.Npad / 2;
-        for (int c0 = half * cols; c0 < (half + 1) * cols; c0 += 16) {
-            uint32_t acc[16], acc2[16];
+        const int cols = p.Npad / G;              // batch columns of this warp
+        const bool conv_row = EPI == kTcConv && row_ok && row < a.conv_channels;
+        for (int c0 = part * cols; c0 < (part + 1) * cols; c0 += 8) {
+            uint32_t acc[8], acc2[8];
             const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0;
             if (ok) {
-                tmem_ld16(taddr, acc);
-                if (NW == 2) tmem_ld16(taddr + (uint32_t)p.Npad, acc2);
+                tmem_ld8(taddr, acc);
+                if (NW == 2) tmem_ld8(taddr + (uint32_t)p.Npad, acc2);
+            }
+            if (!row_ok) continue;
+            // every load of the chunk is issued before the first use
+            float sc[8], cst[8][3];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int b = c0 + i;
+                sc[i] = (a.xscale && b < a.B) ? a.xscale[b] : 1.0f;
+                if (conv_row && b < a.B) {
+                    const float *cs = a.conv_state + ((size_t)b * a.conv_channels + row) * 3;
+                    cst[i][0] = cs[0]; cst[i][1] = cs[1]; cst[i][2] = cs[2];
+                }
             }
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
+            for (int i = 0; i < 8; ++i) {
                 const int b = c0 + i;
-                if (!row_ok || b >= a.B) continue;
-                const float s = a.xscale ? a.xscale[b] : 1.0f;
-                const float v = __uint_as_float(acc[i]) * s;
+                if (b >= a.B) continue;
+                const float v = __uint_as_float(acc[i]) * sc[i];
                 if (EPI == kTcSwiGLU) {
-                    const float u = __uint_as_float(acc2[i]) * s;
+                    const float u = __uint_as_float(acc2[i]) * sc[i];
                     a.dst[0][(size_t)b * a.dst_stride[0] + row] = silu(v) * u;
                 } else if (EPI == kTcStore) {
-                    float *d = seg == 0 ? a.dst[0] : (seg == 1 ? a.dst[1] : a.dst[2]);
-                    const int ds = seg == 0 ? a.dst_stride[0] : (seg == 1 ? a.dst_stride[1] : a.dst_stride[2]);
-                    d[(size_t)b * ds + row] = v;
+                    float *d = dseg + (size_t)b * dstride + row;
+                    if (p.ks > 1) atomicAdd(d, v); else *d = v;
                 } else {
                     float out = v;
-                    if (row < a.conv_channels) {
+                    if (conv_row) {
                         float *cs = a.conv_state + ((size_t)b * a.conv_channels + row) * 3;
-                        const float c0v = cs[0], c1 = cs[1], c2 = cs[2];
-                        const float accv = fmaf(cw.x, c0v, fmaf(cw.y, c1, fmaf(cw.z, c2, cw.w * v)));
-                        cs[0] = c1;
-                        cs[1] = c2;
+                        const float accv = fmaf(cw.x, cst[i][0], fmaf(cw.y, cst[i][1], fmaf(cw.z, cst[i][2], cw.w * v)));
+                        cs[0] = cst[i][1];
+                        cs[1] = cst[i][2];
                         cs[2] = v;
                         out = silu(accv);
                     }
@@ -415,7 +448,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
     if (*abort_flag && threadIdx.x == 0) atomicExch(&g_device_error, LI_ERR_TIMEOUT);
     tc_fence_before();
     __syncthreads();
-    if (warp == kMmaWarp) {
+    if (warp == mma_warp) {
         // an aborted CTA may not have waited for its MMAs: wait (bounded) before freeing TMEM
         if (*abort_flag && lane == 0) mbar_wait(acc_full, 0u);
         __syncwarp();
@@ -515,17 +548,34 @@ int plan(const TcArgs &a, TcPlan *p) {
         p->seg_tiles[s] = s < a.n_seg ? (a.seg_rows[s] + kBM - 1) / kBM : 0;
         p->tiles += p->seg_tiles[s];
     }
-    // deepest rings that fit: raw 2..3, A 2..4 (even), X 2..4
+    // K splits: fill the SMs when there are few tiles (plain stores only;
+    // the partial sums meet in fp32 reductions into a zeroed output)
+    p->ks = 1;
+    if (a.epi == kTcStore) {
+        int sms = 148;
+        int dev = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        while (p->ks * 2 * p->tiles <= sms && p->n_raw % (p->ks * 2) == 0 && p->n_raw / (p->ks * 2) >= 2)
+            p->ks *= 2;
+    }
+    p->raw_per_split = p->n_raw / p->ks;
+    // rings: raw 3 (2 for two weight matrices), A 4, X as deep as fits (<= 16 k-blocks)
     const size_t raw_b = (size_t)p->NW * kBM * p->RB, a_b = (size_t)p->NW * 16384, x_b = (size_t)p->Npad * 128;
-    const int cand[][3] = {{3, 4, 4}, {3, 4, 3}, {2, 4, 3}, {2, 2, 3}, {2, 2, 2}};
-    for (const auto &c : cand) {
-        p->RS = c[0]; p->AS = c[1]; p->XS = c[2];
-        p->off_a = 0;
-        p->off_x = (uint32_t)(p->AS * a_b);
-        p->off_raw = p->off_x + (uint32_t)(p->XS * x_b);
-        p->off_bar = p->off_raw + (uint32_t)(p->RS * raw_b);
-        p->smem = p->off_bar + 8 * (2 * p->RS + 2 * p->AS + 2 * p->XS + 1) + 16 + 1024;
-        if (p->smem <= (size_t)kMaxSmem) return 0;
+    const size_t fixed = 1024 + 512;   // alignment slack, barriers, TMEM holder
+    for (int rs = p->NW == 2 ? 2 : 3; rs >= 2; --rs) {
+        for (int as = 4; as >= 2; as -= 2) {   // slot kb % AS; each phase is filled by one group
+            const size_t used = rs * raw_b + as * a_b + fixed;
+            if (used + 2 * x_b > (size_t)kMaxSmem) continue;
+            int xs = (int)(((size_t)kMaxSmem - used) / x_b);
+            if (xs > 16) xs = 16;
+            p->RS = rs; p->AS = as; p->XS = xs;
+            p->off_a = 0;
+            p->off_x = (uint32_t)(as * a_b);
+            p->off_raw = p->off_x + (uint32_t)(xs * x_b);
+            p->off_bar = p->off_raw + (uint32_t)(rs * raw_b);
+            p->smem = p->off_bar + 8 * (2 * rs + 2 * as + 2 * xs + 1) + 16 + 1024;
+            if (p->smem <= (size_t)kMaxSmem) return 0;
+        }
     }
     return LI_ERR_BAD_SHAPE;
 }
@@ -540,8 +590,8 @@ int launch_kernel(const CUtensorMap *maps, const TcArgs &a, const TcPlan &p, cud
     });
     if (attr_err != cudaSuccess) return (int)attr_err;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)p.tiles);
-    cfg.blockDim = dim3(kThreads);
+    cfg.gridDim = dim3((unsigned)(p.tiles * p.ks));
+    cfg.blockDim = dim3((unsigned)((4 * p.AS + 2) * kWarp));
     cfg.dynamicSmemBytes = p.smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -559,6 +609,11 @@ int tc_prep_launch(const float *x, int x_stride, const float *gamma, float eps, 
     if (K % 8 || !aligned16(x) || (gamma && !aligned16(gamma)) || !aligned16(X16)) return LI_ERR_MISALIGNED;
     return (int)launch_pdl(tc_prep_kernel, dim3((unsigned)B), dim3(256), 0, stream, pdl, x, x_stride, gamma, eps,
                            K, X16, xscale);
+}
+
+bool tc_gemm_splits_k(const TcArgs &a) {
+    TcPlan p;
+    return plan(a, &p) == 0 && p.ks > 1;
 }
 
 int tc_gemm_launch(const TcArgs &a, cudaStream_t stream, bool pdl) {
