@@ -4,19 +4,25 @@
 // ggml Q4_K / Q8_0 rows. Swap-AB: the weight rows are the MMA's M side (128
 // per CTA tile), the batch is N (padded to a multiple of 32, up to 256).
 //
-// One CTA per 128-row weight tile, 10 warps:
-//   warp 4G producer: 2-D tiled TMA of raw weight blocks ([128 rows] x one
-//           256-value column: 144 B Q4_K / 272 B Q8_0 per row) and of the f16
-//           X tile (64 k x N rows, 128-byte swizzle) into shared-memory rings;
-//   warps 0..4G-1 dequant: raw blocks -> f16 weights written in the canonical
-//           K-major 128B-swizzled UMMA layout (one 16-byte granule per store,
-//           bank-conflict free); group g (4 warps, one row each per
-//           thread) takes k-blocks g, g+G, ... into A slot g (G = 2 or 4);
-//   warp 4G+1 MMA: allocates TMEM, issues tcgen05.mma kind::f16 (fp32
-//           accumulators in TMEM, N columns per weight matrix), commits slot
-//           releases to mbarriers;
-//   warps 0..4G-1 epilogue: tcgen05.ld 32x32b of their TMEM lane quarter, scale by
-//           the X row scale, store / SwiGLU / DeltaNet conv epilogue.
+// One CTA per 128-row weight tile (and K split), 5G+1 warps in G groups:
+//   warp 5G producer: allocates TMEM; lane 0 streams 2-D tiled TMA boxes of
+//           raw weight blocks ([128 rows] x SB 256-value columns: 144 B Q4_K /
+//           272 B Q8_0 per row and column) into a ring of raw stages, lane 1
+//           3-D boxes of G*XM f16 X k-blocks (64 k x N rows each, 128-byte
+//           swizzle) into a ring of X slots. The TMA engine's cost per copy
+//           is high for small copies, so both streams move 16-72 KB per copy;
+//   warps 4g..4g+3 (group g) dequant: take k-blocks g, g+G, ... and write
+//           them as f16 into the group's A slots, one tile row per thread:
+//           into tensor memory (tcgen05.st, the row's 64 k in 32 columns of
+//           its TMEM lane) when the TMEM has room next to the accumulators,
+//           else into shared memory (canonical K-major 128B-swizzled UMMA
+//           layout, one 16-byte granule per store, bank-conflict free);
+//   warp 4G+g (group g) MMA issuer, lane 0: issues tcgen05.mma kind::f16
+//           into the group's own fp32 accumulators in TMEM, commits slot
+//           releases, and releases raw stages and X slots once per group.
+//   The groups share only the raw and X rings. Epilogue (dequant warps): tcgen05.ld
+//   32x32b of their TMEM lane quarter, the G partial sums added in group
+//   order, scaled by the X row scale, then store / SwiGLU / DeltaNet conv.
 // Dequant: nibbles / bytes become f16 through the 0x6400 magic-exponent form
 // (one byte permute + one LOP3 per pair), then (q - 1024) * d*sc - dmin*m in
 // packed half2 arithmetic (Q8_0: (u - 1152) * d). The values are rounded to
@@ -26,7 +32,7 @@
 // the previous kernel) and dequantized right away; X and all global writes
 // come after it. Every mbarrier wait is bounded; on a timeout the CTA raises
 // the device flag, skips the remaining work, drains its copies and frees its
-// TMEM before returning.
+// TMEM after its MMAs have finished.
 #include "li_common.cuh"
 #include "li_tcgemm.cuh"
 
@@ -41,23 +47,27 @@ namespace li {
 namespace {
 
 constexpr int kBM = 128;                 // weight rows per tile
-// Dequant groups of 4 warps (one tile row per thread). The group count G
-// equals the number of A slots (2 or 4): group g owns slot g and its
-// k-blocks g, g+G, ..., so each slot's successive phases are produced and
-// awaited by one group and no parity wait can run two phases ahead.
+// Dequant + MMA groups of 4 warps (one tile row per thread). Each group owns
+// its A slots and X slots, so every barrier's successive phases are awaited
+// in order by one owner and no parity wait can run two phases ahead.
 constexpr int kMaxGroups = 4;
-constexpr int kMaxThreads = (4 * kMaxGroups + 2) * kWarp;
+constexpr int kMaxThreads = (5 * kMaxGroups + 1) * kWarp;
 constexpr int kMaxSmem = 227 * 1024;
 
 struct TcPlan {
     int NW;          // weight matrices per tile (2: SwiGLU gate/up)
-    int RB;          // raw bytes per row per raw stage (one 256-value column)
+    int SB;          // 256-value columns (super-blocks) per raw stage
+    int CB;          // bytes of one column per row (144 Q4_K, 272 Q8_0)
+    int RB;          // raw bytes per row per raw stage (SB * CB)
     int Npad;        // batch columns
-    int RS, AS, XS;  // ring depths
+    int G;           // dequant + MMA groups (4 warps each)
+    int RS, AG;      // raw stages, A slots per group
+    int XM, XS;      // X slots of G*XM k-blocks (XM per group), XS of them
+    int atm;         // 1: A slots in tensor memory (32 columns each), else in shared memory
     int tiles;       // CTAs
     int seg_tiles[3];
     int tmem_cols;
-    int n_raw;       // raw stages (K / 256)
+    int n_raw;       // raw stages (K / (256 * SB))
     int ks;          // K splits (CTAs per tile); > 1 only for kTcStore, reduced with fp32 red.add
     int raw_per_split;
     uint32_t off_a, off_x, off_raw, off_bar;
@@ -73,6 +83,15 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *m
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
         " [%0], [%1, {%2, %3}], [%4];"
         ::"r"(smem_addr(smem_dst)), "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *map, int x, int y, int z,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];"
+        ::"r"(smem_addr(smem_dst)), "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
         : "memory");
 }
 
@@ -110,27 +129,36 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64
         : "memory");
 }
 
+// The same with A read from tensor memory (M lanes x 8 columns: 16 f16 k
+// per lane, two per 32-bit column, low half first).
+__device__ __forceinline__ void umma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+
+// Warp-wide store of 32 registers per lane into 32 consecutive TMEM
+// columns of the warp's lane quarter.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+        ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+          "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+          "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]),
+          "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                  ::"r"(smem_addr(bar)) : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-          "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-                 : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
@@ -161,8 +189,9 @@ __device__ __forceinline__ __half2 h2_bits(uint32_t v) { return *reinterpret_cas
 __device__ __forceinline__ uint32_t bits_h2(__half2 v) { return *reinterpret_cast<uint32_t *>(&v); }
 
 // Q4_K: row m's 64 weights of sub-block pair `sub` of the staged super-block
-// (header at +0, nibbles at +16 + 32*sub) -> 8 granules of the A tile.
-__device__ __forceinline__ void dequant_q4k_row(const uint8_t *raw_row, int sub, uint8_t *a_tile, int m) {
+// (header at +0, nibbles at +16 + 32*sub) -> o[4*gi + t], granule gi = 0..7
+// of the row's 128-byte A line (k 8*gi .. 8*gi+7).
+__device__ __forceinline__ void dequant_q4k_regs(const uint8_t *raw_row, int sub, uint32_t (&o)[32]) {
     const uint4 h = *reinterpret_cast<const uint4 *>(raw_row);
     const uint4 q0 = *reinterpret_cast<const uint4 *>(raw_row + 16 + 32 * sub);
     const uint4 q1 = *reinterpret_cast<const uint4 *>(raw_row + 32 + 32 * sub);
@@ -187,25 +216,22 @@ __device__ __forceinline__ void dequant_q4k_row(const uint8_t *raw_row, int sub,
     const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
-        uint32_t lo[4], hi[4];
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
             const uint32_t x = w[2 * g + j];
             const uint32_t t01 = __byte_perm(x, 0u, 0x4140u);   // bytes 0,1 -> halves
             const uint32_t t23 = __byte_perm(x, 0u, 0x4342u);   // bytes 2,3 -> halves
-            lo[2 * j] = bits_h2(__hfma2(__hsub2(h2_bits(lop3_or_and(t01, 0x000F000Fu, 0x64006400u)), magic), dl0, ml0));
-            lo[2 * j + 1] = bits_h2(__hfma2(__hsub2(h2_bits(lop3_or_and(t23, 0x000F000Fu, 0x64006400u)), magic), dl0, ml0));
-            hi[2 * j] = bits_h2(__hfma2(__hsub2(h2_bits(lop3_or_and(t01, 0x00F000F0u, 0x64006400u)), magic), dl1, ml1));
-            hi[2 * j + 1] = bits_h2(__hfma2(__hsub2(h2_bits(lop3_or_and(t23, 0x00F000F0u, 0x64006400u)), magic), dl1, ml1));
+            o[4 * g + 2 * j] = bits_h2(__hfma2(__hsub2(h2_bits(lop3_or_and(t01, 0x000F000Fu, 0x64006400u)), magic), dl0, ml0));
+            o[4 * g + 2 * j + 1] = bits_h2(__hfma2(__hsub2(h2_bits(lop3_or_and(t23, 0x000F000Fu, 0x64006400u)), magic), dl0, ml0));
+            o[16 + 4 * g + 2 * j] = bits_h2(__hfma2(__hsub2(h2_bits(lop3_or_and(t01, 0x00F000F0u, 0x64006400u)), magic), dl1, ml1));
+            o[16 + 4 * g + 2 * j + 1] = bits_h2(__hfma2(__hsub2(h2_bits(lop3_or_and(t23, 0x00F000F0u, 0x64006400u)), magic), dl1, ml1));
         }
-        *reinterpret_cast<uint4 *>(a_tile + sw128_off(m, g)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-        *reinterpret_cast<uint4 *>(a_tile + sw128_off(m, 4 + g)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
     }
 }
 
 // Q8_0: row m's blocks 2*sub and 2*sub+1 of the staged 8-block column
-// (row copy 16-byte aligned, blocks 34 bytes apart) -> 8 granules.
-__device__ __forceinline__ void dequant_q80_row(const uint8_t *raw_row, int sub, uint8_t *a_tile, int m) {
+// (row copy 16-byte aligned, blocks 34 bytes apart) -> o[4*gi + t].
+__device__ __forceinline__ void dequant_q80_regs(const uint8_t *raw_row, int sub, uint32_t (&o)[32]) {
 #pragma unroll
     for (int bb = 0; bb < 2; ++bb) {
         const uint32_t off = 34u * (uint32_t)(2 * sub + bb);
@@ -220,18 +246,31 @@ __device__ __forceinline__ void dequant_q80_row(const uint8_t *raw_row, int sub,
         const __half2 bias = h2_bits(0x64806480u);          // 1152 = 1024 + 128
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
-            uint32_t o[4];
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
                 const uint32_t q = __funnelshift_rc(v[2 * g + j], v[2 * g + j + 1], sh) ^ 0x80808080u;
                 const uint32_t p01 = __byte_perm(q, 0x00006464u, 0x5140u);
                 const uint32_t p23 = __byte_perm(q, 0x00006464u, 0x5342u);
-                o[2 * j] = bits_h2(__hmul2(__hsub2(h2_bits(p01), bias), d2));
-                o[2 * j + 1] = bits_h2(__hmul2(__hsub2(h2_bits(p23), bias), d2));
+                o[16 * bb + 4 * g + 2 * j] = bits_h2(__hmul2(__hsub2(h2_bits(p01), bias), d2));
+                o[16 * bb + 4 * g + 2 * j + 1] = bits_h2(__hmul2(__hsub2(h2_bits(p23), bias), d2));
             }
-            *reinterpret_cast<uint4 *>(a_tile + sw128_off(m, 4 * bb + g)) = make_uint4(o[0], o[1], o[2], o[3]);
         }
     }
+}
+
+template <int WT>
+__device__ __forceinline__ void dequant_regs(const uint8_t *raw_row, int sub, uint32_t (&o)[32]) {
+    if (WT == LI_WTYPE_Q4_K) dequant_q4k_regs(raw_row, sub, o);
+    else dequant_q80_regs(raw_row, sub, o);
+}
+
+// The 8 granules of row m into the 128B-swizzled A tile (bank-conflict free:
+// the 8 rows of an atom put granule gi in 8 different 16-byte bank groups).
+__device__ __forceinline__ void store_row(uint8_t *a_tile, int m, const uint32_t (&o)[32]) {
+#pragma unroll
+    for (int gi = 0; gi < 8; ++gi)
+        *reinterpret_cast<uint4 *>(a_tile + sw128_off(m, gi)) =
+            make_uint4(o[4 * gi], o[4 * gi + 1], o[4 * gi + 2], o[4 * gi + 3]);
 }
 
 // Bounded wait that gives up at once when the CTA has already aborted.
@@ -244,7 +283,20 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, vo
     return true;
 }
 
-template <int WT, int EPI>
+// The same wait taken by a whole warp, with one verdict for all its lanes (the
+// warp-collective steps after it need every lane on the same path).
+__device__ __forceinline__ bool warp_wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+    return __all_sync(0xffffffffu, wait_or_abort(bar, parity, abort_flag));
+}
+
+__device__ __forceinline__ void tmem_ld8_nowait(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+template <int WT, int EPI, bool ATM>
 __global__ void __launch_bounds__(kMaxThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__ CUtensorMap tmW1,
                const __grid_constant__ CUtensorMap tmW2, const __grid_constant__ CUtensorMap tmX,
@@ -254,16 +306,16 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
     uint8_t *smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     constexpr int NW = EPI == kTcSwiGLU ? 2 : 1;
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
-    const int G = p.AS;                                   // dequant groups = A slots
-    const int deq_warps = 4 * G, producer_warp = deq_warps, mma_warp = deq_warps + 1;
+    const int G = p.G;                                    // groups
+    const int issuer0 = 4 * G, producer_warp = 5 * G;
 
-    uint8_t *a_ring = smem + p.off_a;      // [AS][NW][16 KB]
-    uint8_t *x_ring = smem + p.off_x;      // [XS][Npad*128]
+    uint8_t *a_ring = smem + p.off_a;      // [G*AG][NW][16 KB] (A in shared memory)
+    uint8_t *x_ring = smem + p.off_x;      // [XS][G*XM][Npad*128]
     uint8_t *raw_ring = smem + p.off_raw;  // [RS][NW][128*RB]
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + p.off_bar);
     uint64_t *raw_full = bars, *raw_empty = raw_full + p.RS;
-    uint64_t *a_full = raw_empty + p.RS, *a_empty = a_full + p.AS;
-    uint64_t *x_full = a_empty + p.AS, *x_empty = x_full + p.XS;
+    uint64_t *a_full = raw_empty + p.RS, *a_empty = a_full + G * p.AG;
+    uint64_t *x_full = a_empty + G * p.AG, *x_empty = x_full + p.XS;
     uint64_t *acc_full = x_empty + p.XS;
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(acc_full + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
@@ -282,21 +334,27 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
     const int dstride = seg == 0 ? a.dst_stride[0] : (seg == 1 ? a.dst_stride[1] : a.dst_stride[2]);
     const CUtensorMap *tmA = seg == 0 ? &tmW0 : (seg == 1 ? &tmW1 : &tmW2);
     const CUtensorMap *tmB = &tmW1;                       // SwiGLU: up matrix
-    const int r_base = split * p.raw_per_split;           // first raw stage (256 k) of this CTA
+    const int r_base = split * p.raw_per_split;           // first raw stage (256*SB k) of this CTA
     const int n_raw = p.raw_per_split;
-    const int nkb = n_raw * 4;                            // 64-value k-blocks
+    const int kpr = 4 * p.SB;                             // k-blocks per raw stage (>= G)
+    const int nkb = n_raw * kpr;                          // 64-value k-blocks (>= G)
     const uint32_t raw_stage_bytes = (uint32_t)(kBM * p.RB);
-    const uint32_t x_slot_bytes = (uint32_t)(p.Npad * 128);
+    const uint32_t xkb_bytes = (uint32_t)(p.Npad * 128);  // one X k-block
+    const int XK = G * p.XM;                              // k-blocks per X slot
+    const uint32_t x_slot_bytes = (uint32_t)XK * xkb_bytes;
+    const uint32_t acc_cols = (uint32_t)(NW * p.Npad);   // TMEM columns of one group's accumulators
+    // A in tensor memory: slot (group, a, w) = 32 columns after all accumulators
+    const uint32_t a_col0 = (uint32_t)G * acc_cols;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < p.RS; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], deq_warps); }   // every dequant warp once per raw stage
-        for (int i = 0; i < p.AS; ++i) { mbar_init(&a_full[i], kBM); mbar_init(&a_empty[i], 1); }
-        for (int i = 0; i < p.XS; ++i) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 1); }
-        mbar_init(acc_full, 1);
+        for (int i = 0; i < p.RS; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], G); }
+        for (int i = 0; i < G * p.AG; ++i) { mbar_init(&a_full[i], 4); mbar_init(&a_empty[i], 1); }
+        for (int i = 0; i < p.XS; ++i) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], G); }
+        mbar_init(acc_full, G);
         *abort_flag = 0;
         fence_mbar_init();
     }
-    if (warp == mma_warp) tmem_alloc(tmem_holder, (uint32_t)p.tmem_cols);
+    if (warp == producer_warp) tmem_alloc(tmem_holder, (uint32_t)p.tmem_cols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -305,90 +363,133 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
 
     if (warp == producer_warp) {
         if (lane == 0) {
-            int issued_raw = 0, issued_x = 0;
-            auto issue_raw = [&](int r) {
+            // weight stages: they do not depend on the previous kernel, so no
+            // griddepcontrol.wait here
+            int issued = 0;
+            for (int r = 0; r < n_raw; ++r) {
                 const int s = r % p.RS;
                 if (r >= p.RS && !wait_or_abort(&raw_empty[s], (uint32_t)(((r / p.RS) - 1) & 1), abort_flag))
-                    return false;
+                    break;
                 mbar_arrive_expect_tx(&raw_full[s], (uint32_t)NW * raw_stage_bytes);
                 uint8_t *dst = raw_ring + (size_t)s * NW * raw_stage_bytes;
-                tma_load_2d(dst, tmA, (r_base + r) * (p.RB / 2), row0, &raw_full[s]);
-                if (NW == 2) tma_load_2d(dst + raw_stage_bytes, tmB, (r_base + r) * (p.RB / 2), row0, &raw_full[s]);
-                issued_raw = r + 1;
-                return true;
-            };
-            // weights do not depend on the previous kernel: prefetch them first
-            const int pre = p.RS < n_raw ? p.RS : n_raw;
-            for (int r = 0; r < pre; ++r) issue_raw(r);
-            grid_dep_wait();
-            for (int kb = 0; kb < nkb && !*abort_flag; ++kb) {
-                const int s = kb % p.XS;
-                if (kb >= p.XS && !wait_or_abort(&x_empty[s], (uint32_t)(((kb / p.XS) - 1) & 1), abort_flag))
+                tma_load_2d(dst, tmA, (r_base + r) * (p.RB / 4), row0, &raw_full[s]);
+                if (NW == 2) tma_load_2d(dst + raw_stage_bytes, tmB, (r_base + r) * (p.RB / 4), row0, &raw_full[s]);
+                issued = r + 1;
+            }
+            // drain: every copy issued has landed before the CTA exits
+            for (int r = issued - p.RS < 0 ? 0 : issued - p.RS; r < issued; ++r)
+                mbar_wait(&raw_full[r % p.RS], (uint32_t)((r / p.RS) & 1));
+        } else if (lane == 1) {
+            // X slots of XK consecutive k-blocks, one 3-D TMA box each; slot j
+            // is free again when every group has committed its MMAs on it
+            grid_dep_wait();                      // X is written by the previous kernel
+            const int n_xs = nkb / XK;
+            int issued = 0;
+            for (int j = 0; j < n_xs; ++j) {
+                const int s = j % p.XS;
+                if (j >= p.XS && !wait_or_abort(&x_empty[s], (uint32_t)(((j / p.XS) - 1) & 1), abort_flag))
                     break;
                 mbar_arrive_expect_tx(&x_full[s], x_slot_bytes);
-                tma_load_2d(x_ring + (size_t)s * x_slot_bytes, &tmX, (r_base * 4 + kb) * 64, 0, &x_full[s]);
-                issued_x = kb + 1;
-                // keep the raw ring RS stages ahead of the X stream
-                const int want = kb / 4 + p.RS;
-                while (issued_raw < n_raw && issued_raw < want && !*abort_flag) issue_raw(issued_raw);
+                tma_load_3d(x_ring + (size_t)s * x_slot_bytes, &tmX, 0, 0, r_base * kpr + j * XK, &x_full[s]);
+                issued = j + 1;
             }
-            // drain: every copy this CTA issued has landed before it exits
-            for (int r = issued_raw - p.RS < 0 ? 0 : issued_raw - p.RS; r < issued_raw; ++r)
-                mbar_wait(&raw_full[r % p.RS], (uint32_t)((r / p.RS) & 1));
-            for (int kb = issued_x - p.XS < 0 ? 0 : issued_x - p.XS; kb < issued_x; ++kb)
-                mbar_wait(&x_full[kb % p.XS], (uint32_t)((kb / p.XS) & 1));
+            for (int j = issued - p.XS < 0 ? 0 : issued - p.XS; j < issued; ++j)
+                mbar_wait(&x_full[j % p.XS], (uint32_t)((j / p.XS) & 1));
         }
-    } else if (warp == mma_warp) {
+    } else if (warp >= issuer0) {
+        // ------------- MMA issuer of group grp (lane 0) -------------
+        // Issues the group's MMAs (k-blocks grp, grp+G, ...) into its own
+        // accumulators (TMEM columns [grp*acc_cols, (grp+1)*acc_cols)),
+        // releases A slots, X slots (after its last k-block in the slot) and
+        // raw stages (after its dequant warps are past them).
+        const int grp = warp - issuer0;
         if (lane == 0) {
+            const int n_it = nkb / G;
             const uint32_t idesc = idesc_f16(p.Npad);
-            for (int kb = 0; kb < nkb; ++kb) {
-                const int as = kb % p.AS, xs = kb % p.XS;
-                if (!wait_or_abort(&a_full[as], (uint32_t)((kb / p.AS) & 1), abort_flag)) break;
-                if (!wait_or_abort(&x_full[xs], (uint32_t)((kb / p.XS) & 1), abort_flag)) break;
+            const uint32_t d_tmem = tmem + (uint32_t)grp * acc_cols;
+            for (int i = 0; i < n_it; ++i) {
+                const int kb = grp + i * G;
+                const int slot = grp * p.AG + i % p.AG;
+                const int xj = i / p.XM, xs = xj % p.XS;
+                if (!wait_or_abort(&a_full[slot], (uint32_t)((i / p.AG) & 1), abort_flag)) break;
+                // the dequant warps have read this group's last k-block of the raw stage
+                if ((kb % kpr) + G >= kpr) mbar_arrive(&raw_empty[(kb / kpr) % p.RS]);
+                if (!wait_or_abort(&x_full[xs], (uint32_t)((xj / p.XS) & 1), abort_flag)) break;
                 tc_fence_after();
-                const uint64_t bdesc = sw128_desc(smem_addr(x_ring + (size_t)xs * x_slot_bytes));
+                const uint64_t bdesc =
+                    sw128_desc(smem_addr(x_ring + (size_t)xs * x_slot_bytes + (size_t)(kb % XK) * xkb_bytes));
 #pragma unroll
                 for (int w = 0; w < NW; ++w) {
-                    const uint64_t adesc = sw128_desc(smem_addr(a_ring + ((size_t)as * NW + w) * 16384));
+                    if constexpr (ATM) {
+                        const uint32_t at = tmem + a_col0 + (uint32_t)((slot * NW + w) * 32);
 #pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        umma_f16(tmem + (uint32_t)(w * p.Npad), adesc + 2 * j, bdesc + 2 * j, idesc,
-                                 (kb > 0 || j > 0) ? 1u : 0u);
+                        for (int j = 0; j < 4; ++j)
+                            umma_f16_ta(d_tmem + (uint32_t)(w * p.Npad), at + (uint32_t)(8 * j), bdesc + 2 * j, idesc,
+                                        (i > 0 || j > 0) ? 1u : 0u);
+                    } else {
+                        const uint64_t adesc =
+                            sw128_desc(smem_addr(a_ring + ((size_t)slot * NW + w) * 16384));
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            umma_f16(d_tmem + (uint32_t)(w * p.Npad), adesc + 2 * j, bdesc + 2 * j, idesc,
+                                     (i > 0 || j > 0) ? 1u : 0u);
+                    }
                 }
-                umma_commit(&a_empty[as]);
-                umma_commit(&x_empty[xs]);
+                umma_commit(&a_empty[slot]);
+                if (i % p.XM == p.XM - 1) umma_commit(&x_empty[xs]);
             }
-            umma_commit(acc_full);   // also orders every MMA issued before TMEM is read or freed
+            // every MMA this group issued has finished when acc_full sees this commit
+            umma_commit(acc_full);
         }
     } else {
         // ---------------- dequant warps ----------------
-        const int grp = warp / 4;                 // k-blocks grp, grp+G, ...
+        // Group grp (4 warps, one tile row per thread) dequantizes k-blocks
+        // grp, grp+G, ... into its A slots; the values are computed before
+        // the slot is known free, so the wait overlaps the arithmetic.
+        const int grp = warp / 4;
         const int m = threadIdx.x % kBM;          // tile row
-        for (int kb = grp; kb < nkb; kb += G) {
-            const int r = kb / 4, sub = kb % 4;
-            const int rs = r % p.RS, as = kb % p.AS;
-            if (!wait_or_abort(&raw_full[rs], (uint32_t)((r / p.RS) & 1), abort_flag)) break;
-            if (kb >= p.AS && !wait_or_abort(&a_empty[as], (uint32_t)(((kb / p.AS) - 1) & 1), abort_flag))
+        int r_have = -1;
+        for (int i = 0; i < nkb / G; ++i) {
+            const int kb = grp + i * G;
+            const int r = kb / kpr, sub = kb % kpr;   // column sub/4, pair (Q8_0: blocks) sub%4
+            const int rs = r % p.RS;
+            const int slot = grp * p.AG + i % p.AG;
+            if (r != r_have) {
+                if (!warp_wait_or_abort(&raw_full[rs], (uint32_t)((r / p.RS) & 1), abort_flag)) break;
+                r_have = r;
+            }
+            const uint8_t *row = raw_ring + (size_t)rs * NW * raw_stage_bytes + (size_t)m * p.RB + (size_t)(sub >> 2) * p.CB;
+            uint32_t o[32];
+            dequant_regs<WT>(row, sub & 3, o);
+            if (i >= p.AG && !warp_wait_or_abort(&a_empty[slot], (uint32_t)(((i / p.AG) - 1) & 1), abort_flag))
                 break;
-            const uint8_t *raw = raw_ring + (size_t)rs * NW * raw_stage_bytes;
-#pragma unroll
-            for (int w = 0; w < NW; ++w) {
-                const uint8_t *row = raw + (size_t)w * raw_stage_bytes + (size_t)m * p.RB;
-                uint8_t *at = a_ring + ((size_t)as * NW + w) * 16384;
-                if (WT == LI_WTYPE_Q4_K) dequant_q4k_row(row, sub, at, m);
-                else dequant_q80_row(row, sub, at, m);
+            if constexpr (ATM) {
+                // this thread's row = its TMEM lane; the 64 k of the block fill 32 columns
+                tc_fence_after();                 // the MMAs that read the slot before have finished
+                const uint32_t at = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + a_col0 + (uint32_t)(slot * NW * 32);
+                tmem_st32(at, o);
+                if (NW == 2) {
+                    dequant_regs<WT>(row + raw_stage_bytes, sub & 3, o);
+                    tmem_st32(at + 32u, o);
+                }
+                tmem_wait_st();
+                tc_fence_before();
+            } else {
+                uint8_t *at0 = a_ring + (size_t)slot * NW * 16384;
+                store_row(at0, m, o);
+                if (NW == 2) {
+                    dequant_regs<WT>(row + raw_stage_bytes, sub & 3, o);
+                    store_row(at0 + 16384, m, o);
+                }
+                fence_proxy_async_shared();       // generic-proxy writes -> tensor core reads
             }
-            fence_proxy_async_shared();           // generic-proxy writes -> tensor core reads
-            mbar_arrive(&a_full[as]);
-            if (sub + G >= 4) {                   // the group's last k-block of this raw stage
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&raw_empty[rs]);
-            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&a_full[slot]);
         }
 
         // ---------------- epilogue ----------------
         grid_dep_wait();                          // outputs may be read by the previous kernel
-        const bool ok = wait_or_abort(acc_full, 0u, abort_flag);
+        const bool ok = warp_wait_or_abort(acc_full, 0u, abort_flag) && __all_sync(0xffffffffu, *abort_flag == 0);
         tc_fence_after();
         const int q = warp & 3, part = warp >> 2;
         const int rloc = 32 * q + lane;           // tile row of this thread's TMEM lane
@@ -400,31 +501,43 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
         const int cols = p.Npad / G;              // batch columns of this warp
         const bool conv_row = EPI == kTcConv && row_ok && row < a.conv_channels;
         for (int c0 = part * cols; c0 < (part + 1) * cols; c0 += 8) {
-            uint32_t acc[8], acc2[8];
-            const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0;
+            float acc[8], acc2[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) acc[t] = acc2[t] = 0.f;
             if (ok) {
-                tmem_ld8(taddr, acc);
-                if (NW == 2) tmem_ld8(taddr + (uint32_t)p.Npad, acc2);
+                // the G groups' partial sums, added in group order
+                const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0;
+                for (int g = 0; g < G; ++g) {
+                    uint32_t v[8], u[8];
+                    tmem_ld8_nowait(taddr + (uint32_t)g * acc_cols, v);
+                    if (NW == 2) tmem_ld8_nowait(taddr + (uint32_t)g * acc_cols + (uint32_t)p.Npad, u);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int t = 0; t < 8; ++t) {
+                        acc[t] += __uint_as_float(v[t]);
+                        if (NW == 2) acc2[t] += __uint_as_float(u[t]);
+                    }
+                }
             }
             if (!row_ok) continue;
             // every load of the chunk is issued before the first use
             float sc[8], cst[8][3];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int b = c0 + i;
-                sc[i] = (a.xscale && b < a.B) ? a.xscale[b] : 1.0f;
+            for (int t = 0; t < 8; ++t) {
+                const int b = c0 + t;
+                sc[t] = (a.xscale && b < a.B) ? a.xscale[b] : 1.0f;
                 if (conv_row && b < a.B) {
                     const float *cs = a.conv_state + ((size_t)b * a.conv_channels + row) * 3;
-                    cst[i][0] = cs[0]; cst[i][1] = cs[1]; cst[i][2] = cs[2];
+                    cst[t][0] = cs[0]; cst[t][1] = cs[1]; cst[t][2] = cs[2];
                 }
             }
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int b = c0 + i;
+            for (int t = 0; t < 8; ++t) {
+                const int b = c0 + t;
                 if (b >= a.B) continue;
-                const float v = __uint_as_float(acc[i]) * sc[i];
+                const float v = acc[t] * sc[t];
                 if (EPI == kTcSwiGLU) {
-                    const float u = __uint_as_float(acc2[i]) * sc[i];
+                    const float u = acc2[t] * sc[t];
                     a.dst[0][(size_t)b * a.dst_stride[0] + row] = silu(v) * u;
                 } else if (EPI == kTcStore) {
                     float *d = dseg + (size_t)b * dstride + row;
@@ -433,9 +546,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
                     float out = v;
                     if (conv_row) {
                         float *cs = a.conv_state + ((size_t)b * a.conv_channels + row) * 3;
-                        const float accv = fmaf(cw.x, cst[i][0], fmaf(cw.y, cst[i][1], fmaf(cw.z, cst[i][2], cw.w * v)));
-                        cs[0] = cst[i][1];
-                        cs[1] = cst[i][2];
+                        const float accv = fmaf(cw.x, cst[t][0], fmaf(cw.y, cst[t][1], fmaf(cw.z, cst[t][2], cw.w * v)));
+                        cs[0] = cst[t][1];
+                        cs[1] = cst[t][2];
                         cs[2] = v;
                         out = silu(accv);
                     }
@@ -448,7 +561,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
     if (*abort_flag && threadIdx.x == 0) atomicExch(&g_device_error, LI_ERR_TIMEOUT);
     tc_fence_before();
     __syncthreads();
-    if (warp == mma_warp) {
+    if (warp == producer_warp) {
         // an aborted CTA may not have waited for its MMAs: wait (bounded) before freeing TMEM
         if (*abort_flag && lane == 0) mbar_wait(acc_full, 0u);
         __syncwarp();
@@ -532,57 +645,96 @@ int encode_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64
     return r == CUDA_SUCCESS ? 0 : LI_ERR_BAD_SHAPE;
 }
 
+int encode_x(CUtensorMap *map, const void *x16, int K, int B, uint32_t box_rows, uint32_t box_kb) {
+    EncodeTiledFn fn = encoder();
+    if (!fn) return LI_ERR_UNSUPPORTED;
+    const cuuint64_t dims[3] = {64, (cuuint64_t)B, (cuuint64_t)(K / 64)};
+    const cuuint64_t strides[2] = {(cuuint64_t)K * 2, 128};
+    const cuuint32_t box[3] = {64, box_rows, box_kb};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(x16), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : LI_ERR_BAD_SHAPE;
+}
+
+// Columns per raw stage to try first.
+int tc_default_sb() { return 2; }
+
 int plan(const TcArgs &a, TcPlan *p) {
     if (a.wtype != LI_WTYPE_Q4_K && a.wtype != LI_WTYPE_Q8_0) return LI_ERR_UNSUPPORTED;
     if (a.K <= 0 || a.K % 256 || a.B <= 0 || a.B > 256) return LI_ERR_BAD_SHAPE;
     p->NW = a.epi == kTcSwiGLU ? 2 : 1;
-    p->RB = a.wtype == LI_WTYPE_Q4_K ? 144 : 272;
+    p->CB = a.wtype == LI_WTYPE_Q4_K ? 144 : 272;
     p->Npad = (a.B + 31) / 32 * 32;
-    p->n_raw = a.K / 256;
-    int cols = 32;
-    while (cols < p->NW * p->Npad) cols <<= 1;
-    if (cols > 512) return LI_ERR_BAD_SHAPE;
-    p->tmem_cols = cols;
+    const int nwn = p->NW * p->Npad;                  // TMEM columns per group
+    if (nwn > 512) return LI_ERR_BAD_SHAPE;
     p->tiles = 0;
     for (int s = 0; s < 3; ++s) {
         p->seg_tiles[s] = s < a.n_seg ? (a.seg_rows[s] + kBM - 1) / kBM : 0;
         p->tiles += p->seg_tiles[s];
     }
-    // K splits: fill the SMs when there are few tiles (plain stores only;
-    // the partial sums meet in fp32 reductions into a zeroed output)
-    p->ks = 1;
-    if (a.epi == kTcStore) {
-        int sms = 148;
+    int sms = 148;
+    {
         int dev = 0;
         if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        while (p->ks * 2 * p->tiles <= sms && p->n_raw % (p->ks * 2) == 0 && p->n_raw / (p->ks * 2) >= 2)
-            p->ks *= 2;
     }
-    p->raw_per_split = p->n_raw / p->ks;
-    // rings: raw 3 (2 for two weight matrices), A 4, X as deep as fits (<= 16 k-blocks)
-    const size_t raw_b = (size_t)p->NW * kBM * p->RB, a_b = (size_t)p->NW * 16384, x_b = (size_t)p->Npad * 128;
-    const size_t fixed = 1024 + 512;   // alignment slack, barriers, TMEM holder
-    for (int rs = p->NW == 2 ? 2 : 3; rs >= 2; --rs) {
-        for (int as = 4; as >= 2; as -= 2) {   // slot kb % AS; each phase is filled by one group
-            const size_t used = rs * raw_b + as * a_b + fixed;
-            if (used + 2 * x_b > (size_t)kMaxSmem) continue;
-            int xs = (int)(((size_t)kMaxSmem - used) / x_b);
-            if (xs > 16) xs = 16;
-            p->RS = rs; p->AS = as; p->XS = xs;
-            p->off_a = 0;
-            p->off_x = (uint32_t)(as * a_b);
-            p->off_raw = p->off_x + (uint32_t)(xs * x_b);
-            p->off_bar = p->off_raw + (uint32_t)(rs * raw_b);
-            p->smem = p->off_bar + 8 * (2 * rs + 2 * as + 2 * xs + 1) + 16 + 1024;
-            if (p->smem <= (size_t)kMaxSmem) return 0;
+    const int cols256 = a.K / 256;
+    const size_t a_b = (size_t)p->NW * 16384, x_b = (size_t)p->Npad * 128;
+    // A in tensor memory first (the dequantized tile never touches shared
+    // memory, which leaves the shared-memory bandwidth to the raw blocks and
+    // X), with as many groups as the TMEM holds (each group: N accumulator
+    // columns and 32 columns per A slot, per weight matrix); A in shared
+    // memory when the accumulators leave no room. Then raw stages of SB
+    // columns, K splits to fill the SMs when there are few tiles (plain
+    // stores only; partial sums meet in fp32 reductions into a zeroed
+    // output), then the deepest rings that fit.
+    // {raw stages, A slots per group, k-blocks per group per X slot, X slots}
+    static const int kRings[][4] = {{4, 2, 2, 2}, {4, 2, 1, 2}, {3, 2, 2, 2}, {2, 2, 2, 2}, {3, 2, 1, 2},
+                                    {2, 2, 1, 2}, {3, 1, 2, 2}, {2, 1, 2, 2}, {3, 1, 1, 2}, {2, 1, 1, 2},
+                                    {2, 1, 1, 1}};
+    for (int atm = 1; atm >= 0; --atm) {
+        for (int G = kMaxGroups; G >= 1; G /= 2) {
+            if (G * nwn > 512) continue;
+            p->G = G;
+            p->atm = atm;
+            for (int sb : {tc_default_sb(), 2, 1}) {
+                if (sb < 1 || cols256 % sb || p->CB * sb / 4 > 256 || 4 * sb < G) continue;
+                p->SB = sb;
+                p->RB = sb * p->CB;
+                p->n_raw = cols256 / sb;
+                p->ks = 1;
+                if (a.epi == kTcStore)
+                    while (p->ks * 2 * p->tiles <= sms && p->n_raw % (p->ks * 2) == 0 && p->n_raw / (p->ks * 2) >= 2)
+                        p->ks *= 2;
+                p->raw_per_split = p->n_raw / p->ks;
+                const int nkb = p->raw_per_split * 4 * sb;
+                const size_t raw_b = (size_t)p->NW * kBM * p->RB;
+                for (const auto &rg : kRings) {
+                    const int rs = rg[0], ag = rg[1], xm = rg[2], xs = rg[3];
+                    if (nkb % (G * xm)) continue;
+                    const int tcols = G * nwn + (atm ? G * ag * p->NW * 32 : 0);
+                    if (tcols > 512) continue;
+                    int cols = 32;
+                    while (cols < tcols) cols <<= 1;
+                    p->tmem_cols = cols;
+                    p->RS = rs; p->AG = ag; p->XM = xm; p->XS = xs;
+                    p->off_a = 0;
+                    p->off_x = atm ? 0u : (uint32_t)(G * ag * a_b);
+                    p->off_raw = p->off_x + (uint32_t)((size_t)xs * G * xm * x_b);
+                    p->off_bar = p->off_raw + (uint32_t)(rs * raw_b);
+                    p->smem = p->off_bar + 8 * (2 * rs + 2 * G * ag + 2 * xs + 1) + 16 + 1024;
+                    if (p->smem <= (size_t)kMaxSmem) return 0;
+                }
+            }
         }
     }
     return LI_ERR_BAD_SHAPE;
 }
 
-template <int WT, int EPI>
+template <int WT, int EPI, bool ATM>
 int launch_kernel(const CUtensorMap *maps, const TcArgs &a, const TcPlan &p, cudaStream_t stream, bool pdl) {
-    auto kern = tc_gemm_kernel<WT, EPI>;
+    auto kern = tc_gemm_kernel<WT, EPI, ATM>;
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(once, [&] {
@@ -591,7 +743,7 @@ int launch_kernel(const CUtensorMap *maps, const TcArgs &a, const TcPlan &p, cud
     if (attr_err != cudaSuccess) return (int)attr_err;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(p.tiles * p.ks));
-    cfg.blockDim = dim3((unsigned)((4 * p.AS + 2) * kWarp));
+    cfg.blockDim = dim3((unsigned)((5 * p.G + 1) * kWarp));
     cfg.dynamicSmemBytes = p.smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -600,6 +752,12 @@ int launch_kernel(const CUtensorMap *maps, const TcArgs &a, const TcPlan &p, cud
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return (int)cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], maps[3], a, p);
+}
+
+template <int WT, int EPI>
+int launch_kernel(const CUtensorMap *maps, const TcArgs &a, const TcPlan &p, cudaStream_t stream, bool pdl) {
+    return p.atm ? launch_kernel<WT, EPI, true>(maps, a, p, stream, pdl)
+                 : launch_kernel<WT, EPI, false>(maps, a, p, stream, pdl);
 }
 
 }  // namespace
@@ -628,13 +786,14 @@ int tc_gemm_launch(const TcArgs &a, cudaStream_t stream, bool pdl) {
         const int src = s < nw ? s : 0;
         const int rows = a.epi == kTcSwiGLU ? a.seg_rows[0] : a.seg_rows[src];
         if (!aligned16(a.W[src])) return LI_ERR_MISALIGNED;
-        rc = encode_2d(&maps[s], CU_TENSOR_MAP_DATA_TYPE_UINT16, a.W[src], rb / 2, (uint64_t)rows, rb,
-                       (uint32_t)(p.RB / 2), kBM, CU_TENSOR_MAP_SWIZZLE_NONE);
+        rc = encode_2d(&maps[s], CU_TENSOR_MAP_DATA_TYPE_UINT32, a.W[src], rb / 4, (uint64_t)rows, rb,
+                       (uint32_t)(p.RB / 4), kBM, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (rc) return rc;
     }
     if (!aligned16(a.X16)) return LI_ERR_MISALIGNED;
-    rc = encode_2d(&maps[3], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.X16, (uint64_t)a.K, (uint64_t)a.B,
-                   (uint64_t)a.K * 2, 64, (uint32_t)p.Npad, CU_TENSOR_MAP_SWIZZLE_128B);
+    // X as [k-block][row][64 k]: one box brings G*XM consecutive k-blocks,
+    // each a [Npad rows][128 B] 128B-swizzled tile (rows past B read as zeros)
+    rc = encode_x(&maps[3], a.X16, a.K, a.B, (uint32_t)p.Npad, (uint32_t)(p.G * p.XM));
     if (rc) return rc;
     const bool q4 = a.wtype == LI_WTYPE_Q4_K;
     switch (a.epi) {

@@ -140,10 +140,12 @@ def test_matmul_q_shapes(cuda, oracle_mod, wtype, n_rows):
 
 
 @pytest.mark.parametrize("wtype", [8, 12])
-@pytest.mark.parametrize("n_rows", [2, 8, 32])
+@pytest.mark.parametrize("n_rows", [2, 8, 32, 64, 256])
 def test_ffn_q(cuda, oracle_mod, wtype, n_rows):
     """RMSNorm + SwiGLU gate/up + down, reduced width (K=1024, N=3072); from 8
-    rows on the gate/up and down contractions run on the tensor cores."""
+    rows on the gate/up and down contractions run on the tensor cores (A tiles
+    in tensor memory; at 256 rows the gate/up accumulators fill the TMEM and
+    the A tiles go through shared memory)."""
     from leaninfer_b200 import ops, synth
     r = rng(300 + wtype + n_rows)
     K, N_ = 1024, 3072
