@@ -282,6 +282,7 @@ def _layer(cuda, w, repeat_type=0, in_norm_w=None):
     (12, 8, 1024, 4, 8, 0),        # tensor-core projections from here on
     (8, 16, 1024, 2, 8, 1),
     (12, 64, 4096, 16, 32, 0),     # the decode workload: layer shape and batch
+    (8, 40, 1024, 4, 16, 1),       # 640 (sequence, head) items, k-heads repeated by tiling
 ])
 def test_layer_decode_steps(cuda, oracle_mod, wtype, B, hidden, Hk, Hv, repeat_type):
     import torch
