@@ -267,6 +267,24 @@ int li_launch_deltanet_layer_decode_noalloc(const li_deltanet_layer * L,
         const float * x, float * y, float * conv_state, float * state,
         int n_seqs, void * stream);
 
+/* Chunked (WY form, chunk 64) gated delta rule prefill of one sequence of T
+ * tokens on the tensor cores (bf16 operands, fp32 accumulation and state).
+ * No counterpart in the reference (its prefill is the upstream per-token
+ * DELTA_NET op); the arithmetic is the token recurrence
+ *   a = exp(g), q~ = scale q, v' = beta (v - a S^T k), S <- a S + k v'^T,
+ *   o = S^T q~
+ * (beta already a gate in (0,1), no clamp). Layouts: q, k bf16
+ * [T][n_k_heads][head_dim]; v bf16 [T][n_v_heads][head_dim]; g (log decay),
+ * beta fp32 [T][n_v_heads]; state fp32 [n_v_heads][D(k)][D(v)], updated in
+ * place to the state after token T-1; o fp32 [T][n_v_heads][head_dim]. v-head
+ * h reads k-head h / (n_v_heads / n_k_heads). head_dim 128. q, k, v and the
+ * workspace 16-byte aligned. */
+size_t li_deltanet_chunk_prefill_workspace_size(int T, int n_v_heads, int head_dim);
+int li_launch_deltanet_chunk_prefill_bf16(const void * q, const void * k, const void * v,
+        const float * g, const float * beta, float * state, float * o,
+        int T, int n_k_heads, int n_v_heads, int head_dim, float scale,
+        void * workspace, size_t workspace_bytes, void * stream);
+
 #else  /* no CUDA: the reference's no-op stubs, plus stubs for the new entries */
 
 static inline void li_launch_fused_rms_norm_silu_gate_f32(

@@ -77,6 +77,9 @@ _SIGS = {
         c_int, [c_void_p] * 8 + [c_int64, c_int64, c_int64, c_int64, c_int, c_int64,
                                  c_size_t, c_size_t, c_size_t, c_void_p]),
     "li_deltanet_layer_workspace_size": (c_size_t, [POINTER(DeltaNetLayer), c_int]),
+    "li_deltanet_chunk_prefill_workspace_size": (c_size_t, [c_int, c_int, c_int]),
+    "li_launch_deltanet_chunk_prefill_bf16": (c_int, [c_void_p] * 7 + [c_int] * 4 + [c_float, c_void_p, c_size_t,
+                                                                                     c_void_p]),
     "li_launch_deltanet_layer_decode": (
         c_int, [POINTER(DeltaNetLayer), c_void_p, c_void_p, c_void_p, c_void_p, c_int,
                 c_void_p, c_size_t, c_void_p]),

@@ -1,0 +1,605 @@
+// Chunked (WY form, chunk 64) gated delta rule prefill on the tensor cores.
+//
+// Semantics (per v-head h, k-head hk = h / (Hv/Hk), tokens t = 0..T-1):
+//   a_t = exp(g_t); q~_t = scale * q_t;
+//   v'_t = beta_t * (v_t - a_t * S^T k_t);  S <- a_t * S + k_t v'_t^T;  o_t = S^T q~_t
+// with S[k][v] fp32 (the oracle's token-by-token restatement, lio_gdr_prefill).
+// Over a chunk of C = 64 tokens with gamma_i = prod_{j<=i} a_j (computed as
+// exp of a prefix sum of g) the chunk is exactly
+//   A[i][j] = beta_i (gamma_i/gamma_j) k_i.k_j  (j < i),   T = (I + A)^-1,
+//   W = T diag(beta gamma) K,   U = T diag(beta) V,   Delta = U - W S0,
+//   P[i][j] = (gamma_i/gamma_j) q~_i.k_j (j <= i),
+//   O = diag(gamma) Q~ S0 + P Delta,   S = gamma_C S0 + K^T diag(gamma_C/gamma) Delta.
+//
+// Two kernels:
+//   gdr_prep_kernel (one CTA per v-head and pair of chunks, all in parallel):
+//     K K^T and Q K^T of the 128-token pair on tcgen05 (M = 128; the diagonal
+//     64x64 blocks are the chunks'), A and P from them, T by a blocked fp32
+//     forward substitution (16x16 diagonal blocks, then block rows), W and U
+//     on tcgen05 with T block-diagonal over the pair. It writes, per chunk, the
+//     state kernel's shared-memory image (W, Q~ gamma, P, K^T diag(gamma_C /
+//     gamma), gamma_C, already in the canonical 128B-swizzled K-major tile
+//     layout, bf16) and U (fp32).
+//   gdr_state_kernel (one CTA per v-head, chunks in order): the state lives
+//     transposed, S^T[v][k], in tensor memory (fp32) with a bf16 copy in shared
+//     memory as the MMA operand; per chunk one bulk copy brings the chunk
+//     image (prefetched two chunks ahead), and every contraction has M = 128
+//     (v): S^T W^T and S^T (Q~ gamma)^T, then Delta^T = U^T - S^T W^T, then
+//     O^T += Delta^T P^T and S^T = gamma_C S^T + Delta^T (diag(gamma_C/gamma) K).
+// All MMAs are kind::f16 with both operands bf16 and fp32 accumulation.
+#include "li_common.cuh"
+#include "li_tc.cuh"
+
+#include <cuda_bf16.h>
+#include <mutex>
+
+LI_DEFINE_TU_STATUS(prefill)
+
+namespace li {
+namespace {
+
+constexpr int kD = 128, kC = 64;
+// per-chunk image for the state kernel (bytes)
+constexpr uint32_t kImgW = 0;        // W [64 t][128 k]: two [64][64] tiles
+constexpr uint32_t kImgQ = 16384;    // Q~ gamma [64 t][128 k]: two tiles
+constexpr uint32_t kImgP = 32768;    // P [64 i][64 j]: one tile
+constexpr uint32_t kImgKd = 40960;   // (gamma_C/gamma_t) k_t as [128 k][64 t]: one tile
+constexpr uint32_t kImgG = 57344;    // gamma_C (fp32)
+constexpr uint32_t kImgBytes = 58368;
+
+struct PrefillArgs {
+    const __nv_bfloat16 *q, *k, *v;   // [T][Hk][D], [T][Hk][D], [T][Hv][D]
+    const float *g, *beta;            // [T][Hv]
+    float *state;                     // [Hv][D(k)][D(v)], in/out
+    float *o;                         // [T][Hv][D]
+    int T, Hk, Hv, n_chunks;
+    float scale;
+    uint8_t *img;                     // [Hv][n_chunks][kImgBytes]
+    float *U;                         // [Hv][n_chunks][64][128]
+};
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// element e (0..63) of row m of a [rows][64] bf16 tile
+__device__ __forceinline__ float tile_get(const uint8_t *tile, int m, int e) {
+    const uint16_t b = *reinterpret_cast<const uint16_t *>(tile + sw128_off(m, e >> 3) + (e & 7) * 2);
+    return __uint_as_float((uint32_t)b << 16);
+}
+
+// ---------------------------------------------------------------------------
+// prep: one CTA per (chunk pair, v-head), 256 threads
+// ---------------------------------------------------------------------------
+constexpr uint32_t kPrepKt = 0, kPrepQt = 32768, kPrepTt = 65536, kPrepKb = 98304, kPrepVb = 131072,
+                   kPrepAf = 163840, kPrepMisc = 196608;
+constexpr size_t kPrepSmem = 196608 + 8192 + 1024;
+
+__global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    uint8_t *Kt = sm + kPrepKt, *Qt = sm + kPrepQt, *Tt = sm + kPrepTt, *Kb = sm + kPrepKb, *Vb = sm + kPrepVb;
+    float *Af = reinterpret_cast<float *>(sm + kPrepAf);    // [2][64][64] strictly lower A
+    float *Tf = reinterpret_cast<float *>(sm + kPrepQt);    // [2][64][64] T (over Qt once it is consumed)
+    float *gc = reinterpret_cast<float *>(sm + kPrepMisc);  // [128] log gamma
+    float *gam = gc + 128, *bet = gam + 128, *wsum = bet + 128;   // wsum [4]
+    float *Mt = wsum + 8;                                    // [6][16][16] block-solve temporaries
+    uint64_t *bar = reinterpret_cast<uint64_t *>(Mt + 6 * 256);
+    uint32_t *holder = reinterpret_cast<uint32_t *>(bar + 2);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(holder + 1);
+
+    const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+    const int h = blockIdx.y, pair = blockIdx.x;
+    const int hk = h / (a.Hv / a.Hk);
+    const int t0 = pair * 2 * kC;
+
+    if (tid == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) tmem_alloc(holder, 512);
+
+    // 1. decay prefix sums (per 64-token chunk), beta
+    if (tid < 128) {
+        const int t = t0 + tid;
+        const bool ok = t < a.T;
+        float gv = ok ? a.g[(size_t)t * a.Hv + h] : 0.f;
+        bet[tid] = ok ? a.beta[(size_t)t * a.Hv + h] : 0.f;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, gv, o);
+            if (lane >= o) gv += y;
+        }
+        if (lane == 31) wsum[warp] = gv;
+        gc[tid] = gv;
+    }
+    __syncthreads();
+    if (tid < 128) {
+        if (warp & 1) gc[tid] += wsum[warp - 1];   // second warp of each chunk
+        gam[tid] = expf(gc[tid]);
+    }
+    // 2. operands: K, Q rows as [r][d] tiles; (beta gamma K)^T, (beta V)^T as [d][r] tiles
+    for (int e = tid; e < 128 * 16; e += 256) {
+        const int r = e >> 4, gi = e & 15, t = t0 + r;
+        uint4 kv = make_uint4(0, 0, 0, 0), qv = kv;
+        if (t < a.T) {
+            kv = *reinterpret_cast<const uint4 *>(a.k + ((size_t)t * a.Hk + hk) * kD + gi * 8);
+            qv = *reinterpret_cast<const uint4 *>(a.q + ((size_t)t * a.Hk + hk) * kD + gi * 8);
+        }
+        *reinterpret_cast<uint4 *>(Kt + (gi >> 3) * 16384 + sw128_off(r, gi & 7)) = kv;
+        *reinterpret_cast<uint4 *>(Qt + (gi >> 3) * 16384 + sw128_off(r, gi & 7)) = qv;
+    }
+    __syncthreads();   // gam, bet complete
+    for (int e = tid; e < 128 * 16; e += 256) {
+        const int d = e & 127, rg = e >> 7;   // output row d, granule rg: tokens 8rg .. 8rg+7
+        float kx[8], vx[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int r = rg * 8 + j, t = t0 + r;
+            float kk = 0.f, vv = 0.f;
+            if (t < a.T) {
+                kk = __bfloat162float(a.k[((size_t)t * a.Hk + hk) * kD + d]);
+                vv = __bfloat162float(a.v[((size_t)t * a.Hv + h) * kD + d]);
+            }
+            kx[j] = kk * (bet[r] * gam[r]);
+            vx[j] = vv * bet[r];
+        }
+        const uint32_t off = (rg >> 3) * 16384 + sw128_off(d, rg & 7);
+        *reinterpret_cast<uint4 *>(Kb + off) = make_uint4(pack_bf16x2(kx[0], kx[1]), pack_bf16x2(kx[2], kx[3]),
+                                                          pack_bf16x2(kx[4], kx[5]), pack_bf16x2(kx[6], kx[7]));
+        *reinterpret_cast<uint4 *>(Vb + off) = make_uint4(pack_bf16x2(vx[0], vx[1]), pack_bf16x2(vx[2], vx[3]),
+                                                          pack_bf16x2(vx[4], vx[5]), pack_bf16x2(vx[6], vx[7]));
+    }
+    fence_proxy_async_shared();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *holder;
+    const uint32_t idesc = idesc_kf16(128, 128, true);
+    // 3. K K^T -> cols [0,128), Q K^T -> cols [128,256)
+    if (tid == 0) {
+        for (int kb = 0; kb < 2; ++kb) {
+            const uint64_t dk = sw128_desc(smem_addr(Kt + kb * 16384)), dq = sw128_desc(smem_addr(Qt + kb * 16384));
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                umma_f16(tmem + 0, dk + 2 * j, dk + 2 * j, idesc, (kb | j) ? 1u : 0u);
+                umma_f16(tmem + 128, dq + 2 * j, dk + 2 * j, idesc, (kb | j) ? 1u : 0u);
+            }
+        }
+        umma_commit(&bar[0]);
+    }
+    bool ok = mbar_wait(&bar[0], 0);
+    tc_fence_after();
+    const int chunk0 = 2 * pair;
+    // 4. rows: A (to shared memory), P, Q~ gamma, gamma_C (to the chunk images)
+    if (ok && tid < 128) {
+        const int r = tid, c = r >> 6, i = r & 63;
+        const int chunk = chunk0 + c;
+        const uint32_t lane_addr = tmem + ((uint32_t)(32 * warp) << 16);
+        uint32_t kk[2][32], qk[2][32];
+        tmem_ld32_nowait(lane_addr + c * 64, kk[0]);
+        tmem_ld32_nowait(lane_addr + c * 64 + 32, kk[1]);
+        tmem_ld32_nowait(lane_addr + 128 + c * 64, qk[0]);
+        tmem_ld32_nowait(lane_addr + 128 + c * 64 + 32, qk[1]);
+        tmem_wait_ld();
+        float *Arow = Af + (c * 64 + i) * 64;
+        uint32_t prow[32];
+#pragma unroll
+        for (int jj = 0; jj < 64; jj += 2) {
+            float pv[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int j = jj + u;
+                const float ratio = j <= i ? expf(gc[r] - gc[c * 64 + j]) : 0.f;
+                const float kkv = __uint_as_float(kk[j >> 5][j & 31]);
+                const float qkv = __uint_as_float(qk[j >> 5][j & 31]);
+                Arow[j] = j < i ? bet[r] * ratio * kkv : 0.f;
+                pv[u] = a.scale * ratio * qkv;
+            }
+            prow[jj >> 1] = pack_bf16x2(pv[0], pv[1]);
+        }
+        if (chunk < a.n_chunks) {
+            uint8_t *img = a.img + ((size_t)h * a.n_chunks + chunk) * kImgBytes;
+#pragma unroll
+            for (int gg = 0; gg < 8; ++gg)
+                *reinterpret_cast<uint4 *>(img + kImgP + sw128_off(i, gg)) =
+                    make_uint4(prow[4 * gg], prow[4 * gg + 1], prow[4 * gg + 2], prow[4 * gg + 3]);
+            const float qs = a.scale * gam[r];
+#pragma unroll 4
+            for (int gi = 0; gi < 16; ++gi) {
+                const uint4 w = *reinterpret_cast<const uint4 *>(Qt + (gi >> 3) * 16384 + sw128_off(r, gi & 7));
+                const uint4 o4 = make_uint4(pack_bf16x2(bf16_lo(w.x) * qs, bf16_hi(w.x) * qs),
+                                            pack_bf16x2(bf16_lo(w.y) * qs, bf16_hi(w.y) * qs),
+                                            pack_bf16x2(bf16_lo(w.z) * qs, bf16_hi(w.z) * qs),
+                                            pack_bf16x2(bf16_lo(w.w) * qs, bf16_hi(w.w) * qs));
+                *reinterpret_cast<uint4 *>(img + kImgQ + (gi >> 3) * 8192 + sw128_off(i, gi & 7)) = o4;
+            }
+            if (i == 63) *reinterpret_cast<float *>(img + kImgG) = gam[r];
+        }
+    }
+    // K^T diag(gamma_C/gamma) as [128 k][64 t] per chunk
+    if (ok) {
+        for (int e = tid; e < 2 * 128 * 8; e += 256) {
+            const int kx = e & 127, tg = (e >> 7) & 7, c = e >> 10;
+            const int chunk = chunk0 + c;
+            if (chunk >= a.n_chunks) continue;
+            const float gl = gc[c * 64 + 63];
+            float vals[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int r = c * 64 + tg * 8 + j;
+                vals[j] = tile_get(Kt + (kx >> 6) * 16384, r, kx & 63) * expf(gl - gc[r]);
+            }
+            uint8_t *img = a.img + ((size_t)h * a.n_chunks + chunk) * kImgBytes;
+            *reinterpret_cast<uint4 *>(img + kImgKd + sw128_off(kx, tg)) =
+                make_uint4(pack_bf16x2(vals[0], vals[1]), pack_bf16x2(vals[2], vals[3]),
+                           pack_bf16x2(vals[4], vals[5]), pack_bf16x2(vals[6], vals[7]));
+        }
+    }
+    __syncthreads();   // Qt consumed: Tf may overwrite it
+    // 5. T = (I + A)^-1 per chunk, blocked by 16
+    for (int e = tid; e < 2 * 64 * 64; e += 256) Tf[e] = 0.f;
+    __syncthreads();
+    if (tid < 128) {
+        const int c = tid >> 6, blk = (tid >> 4) & 3, col = tid & 15;
+        const float *Ab = Af + (c * 64 + blk * 16) * 64 + blk * 16;
+        float x[16];
+#pragma unroll
+        for (int ii = 0; ii < 16; ++ii) {
+            float s = ii == col ? 1.f : 0.f;
+#pragma unroll
+            for (int kk2 = 0; kk2 < ii; ++kk2) s = fmaf(-Ab[ii * 64 + kk2], x[kk2], s);
+            x[ii] = s;
+        }
+        float *Tb = Tf + (c * 64 + blk * 16) * 64 + blk * 16;
+#pragma unroll
+        for (int ii = 0; ii < 16; ++ii) Tb[ii * 64 + col] = x[ii];
+    }
+    __syncthreads();
+    for (int dd = 1; dd < 4; ++dd) {
+        const int nb = 2 * (4 - dd);   // blocks (c, I, J = I - dd)
+        for (int q = tid; q < nb * 256; q += 256) {
+            const int bi = q >> 8, e2 = q & 255, ar = e2 >> 4, bc = e2 & 15;
+            const int c = bi / (4 - dd), I = dd + bi % (4 - dd), J = I - dd;
+            float s = 0.f;
+            for (int K = J; K < I; ++K)
+#pragma unroll
+                for (int kk2 = 0; kk2 < 16; ++kk2)
+                    s = fmaf(Af[(c * 64 + I * 16 + ar) * 64 + K * 16 + kk2], Tf[(c * 64 + K * 16 + kk2) * 64 + J * 16 + bc], s);
+            Mt[bi * 256 + e2] = s;
+        }
+        __syncthreads();
+        for (int q = tid; q < nb * 256; q += 256) {
+            const int bi = q >> 8, e2 = q & 255, ar = e2 >> 4, bc = e2 & 15;
+            const int c = bi / (4 - dd), I = dd + bi % (4 - dd), J = I - dd;
+            float s = 0.f;
+#pragma unroll
+            for (int kk2 = 0; kk2 < 16; ++kk2)
+                s = fmaf(Tf[(c * 64 + I * 16 + ar) * 64 + I * 16 + kk2], Mt[bi * 256 + kk2 * 16 + bc], s);
+            Tf[(c * 64 + I * 16 + ar) * 64 + J * 16 + bc] = -s;
+        }
+        __syncthreads();
+    }
+    // block-diagonal T over the pair -> bf16 tiles [128 i][128 j]
+    for (int e = tid; e < 128 * 16; e += 256) {
+        const int r = e >> 4, gi = e & 15, c = r >> 6, i = r & 63;
+        uint4 w = make_uint4(0, 0, 0, 0);
+        if ((gi >> 3) == c) {
+            const float *tr = Tf + (c * 64 + i) * 64 + (gi & 7) * 8;
+            w = make_uint4(pack_bf16x2(tr[0], tr[1]), pack_bf16x2(tr[2], tr[3]), pack_bf16x2(tr[4], tr[5]),
+                           pack_bf16x2(tr[6], tr[7]));
+        }
+        *reinterpret_cast<uint4 *>(Tt + (gi >> 3) * 16384 + sw128_off(r, gi & 7)) = w;
+    }
+    fence_proxy_async_shared();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    // 6. W = T (beta gamma K) -> cols [256,384), U = T (beta V) -> cols [384,512)
+    if (tid == 0 && ok) {
+        for (int kb = 0; kb < 2; ++kb) {
+            const uint64_t dt = sw128_desc(smem_addr(Tt + kb * 16384));
+            const uint64_t dkb = sw128_desc(smem_addr(Kb + kb * 16384)), dvb = sw128_desc(smem_addr(Vb + kb * 16384));
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                umma_f16(tmem + 256, dt + 2 * j, dkb + 2 * j, idesc, (kb | j) ? 1u : 0u);
+                umma_f16(tmem + 384, dt + 2 * j, dvb + 2 * j, idesc, (kb | j) ? 1u : 0u);
+            }
+        }
+        umma_commit(&bar[1]);
+    }
+    if (ok) ok = mbar_wait(&bar[1], 0);
+    tc_fence_after();
+    // 7. W rows (bf16 tiles) and U rows (fp32) to the workspace
+    if (ok && tid < 128) {
+        const int r = tid, c = r >> 6, i = r & 63, chunk = chunk0 + c;
+        if (chunk < a.n_chunks) {
+            const uint32_t lane_addr = tmem + ((uint32_t)(32 * warp) << 16);
+            uint8_t *img = a.img + ((size_t)h * a.n_chunks + chunk) * kImgBytes;
+            float *Ur = a.U + (((size_t)h * a.n_chunks + chunk) * kC + i) * kD;
+            for (int cb = 0; cb < 4; ++cb) {
+                uint32_t w[32], u[32];
+                tmem_ld32_nowait(lane_addr + 256 + cb * 32, w);
+                tmem_ld32_nowait(lane_addr + 384 + cb * 32, u);
+                tmem_wait_ld();
+#pragma unroll
+                for (int gg = 0; gg < 4; ++gg) {
+                    const int d0 = cb * 32 + gg * 8;
+                    *reinterpret_cast<uint4 *>(img + kImgW + (d0 >> 6) * 8192 + sw128_off(i, (d0 & 63) >> 3)) =
+                        make_uint4(pack_bf16x2(__uint_as_float(w[8 * gg]), __uint_as_float(w[8 * gg + 1])),
+                                   pack_bf16x2(__uint_as_float(w[8 * gg + 2]), __uint_as_float(w[8 * gg + 3])),
+                                   pack_bf16x2(__uint_as_float(w[8 * gg + 4]), __uint_as_float(w[8 * gg + 5])),
+                                   pack_bf16x2(__uint_as_float(w[8 * gg + 6]), __uint_as_float(w[8 * gg + 7])));
+                }
+#pragma unroll
+                for (int q4 = 0; q4 < 8; ++q4)
+                    *reinterpret_cast<float4 *>(Ur + cb * 32 + q4 * 4) =
+                        make_float4(__uint_as_float(u[4 * q4]), __uint_as_float(u[4 * q4 + 1]),
+                                    __uint_as_float(u[4 * q4 + 2]), __uint_as_float(u[4 * q4 + 3]));
+            }
+        }
+    }
+    if (!ok && tid == 0) {
+        // the MMAs may still run: wait (bounded) before the TMEM is freed
+        mbar_wait(&bar[0], 0);
+        mbar_wait(&bar[1], 0);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// state: one CTA per v-head, 128 threads (thread v = TMEM lane v), chunks in order
+// ---------------------------------------------------------------------------
+constexpr uint32_t kStRing = 0, kStS = 2 * kImgBytes, kStDt = kStS + 32768, kStMisc = kStDt + 16384;
+constexpr size_t kStateSmem = kStMisc + 64 + 1024;
+
+__global__ void __launch_bounds__(128, 1) gdr_state_kernel(PrefillArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    uint8_t *ring = sm + kStRing, *St = sm + kStS, *Dt = sm + kStDt;
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + kStMisc);   // [2]
+    uint64_t *mbar = full + 2;
+    uint32_t *holder = reinterpret_cast<uint32_t *>(mbar + 1);
+
+    const int v = threadIdx.x, warp = v / 32;
+    const int h = blockIdx.x;
+    const int nc = a.n_chunks;
+    if (v == 0) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        mbar_init(mbar, 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) tmem_alloc(holder, 256);
+    __syncthreads();
+    if (v == 0) {
+        for (int n = 0; n < 2 && n < nc; ++n) {
+            mbar_arrive_expect_tx(&full[n], kImgBytes);
+            bulk_g2s(ring + (size_t)n * kImgBytes, a.img + ((size_t)h * nc + n) * kImgBytes, kImgBytes, &full[n]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *holder;
+    const uint32_t lane_addr = tmem + ((uint32_t)(32 * warp) << 16);
+    float *Sg = a.state + (size_t)h * kD * kD;
+    // S^T row v: S[k][v], k = 0..127 -> TMEM cols [0,128) and the bf16 operand tiles
+    for (int cb = 0; cb < 4; ++cb) {
+        uint32_t r[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(Sg[(size_t)(cb * 32 + j) * kD + v]);
+        tmem_st32(lane_addr + cb * 32, r);
+#pragma unroll
+        for (int gg = 0; gg < 4; ++gg) {
+            const int k0 = cb * 32 + gg * 8;
+            *reinterpret_cast<uint4 *>(St + (k0 >> 6) * 16384 + sw128_off(v, (k0 & 63) >> 3)) =
+                make_uint4(pack_bf16x2(__uint_as_float(r[8 * gg]), __uint_as_float(r[8 * gg + 1])),
+                           pack_bf16x2(__uint_as_float(r[8 * gg + 2]), __uint_as_float(r[8 * gg + 3])),
+                           pack_bf16x2(__uint_as_float(r[8 * gg + 4]), __uint_as_float(r[8 * gg + 5])),
+                           pack_bf16x2(__uint_as_float(r[8 * gg + 6]), __uint_as_float(r[8 * gg + 7])));
+        }
+    }
+    tmem_wait_st();
+    fence_proxy_async_shared();
+    tc_fence_before();
+    __syncthreads();
+
+    const uint32_t id64 = idesc_kf16(128, 64, true), id128 = idesc_kf16(128, 128, true);
+    uint32_t mph = 0;
+    int n = 0;
+    for (; n < nc; ++n) {
+        const int b = n & 1;
+        const uint8_t *img = ring + (size_t)b * kImgBytes;
+        const bool okf = mbar_wait(&full[b], (uint32_t)((n >> 1) & 1));
+        if (__syncthreads_or(!okf)) break;
+        tc_fence_after();
+        // S^T W^T -> cols [128,192); S^T (Q~ gamma)^T -> cols [192,256)
+        if (v == 0) {
+            for (int kb = 0; kb < 2; ++kb) {
+                const uint64_t ds = sw128_desc(smem_addr(St + kb * 16384));
+                const uint64_t dw = sw128_desc(smem_addr(img + kImgW + kb * 8192));
+                const uint64_t dq = sw128_desc(smem_addr(img + kImgQ + kb * 8192));
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    umma_f16(tmem + 128, ds + 2 * j, dw + 2 * j, id64, (kb | j) ? 1u : 0u);
+                    umma_f16(tmem + 192, ds + 2 * j, dq + 2 * j, id64, (kb | j) ? 1u : 0u);
+                }
+            }
+            umma_commit(mbar);
+        }
+        // meanwhile: U^T row v of this chunk, and S^T *= gamma_C in TMEM
+        const float gC = *reinterpret_cast<const float *>(img + kImgG);
+        const float *Uc = a.U + ((size_t)h * nc + n) * kC * kD;
+        float u[64];
+#pragma unroll
+        for (int t = 0; t < 64; ++t) u[t] = Uc[(size_t)t * kD + v];
+        for (int cb = 0; cb < 4; ++cb) {
+            uint32_t r[32];
+            tmem_ld32_nowait(lane_addr + cb * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * gC);
+            tmem_st32(lane_addr + cb * 32, r);
+        }
+        tmem_wait_st();
+        bool okm = mbar_wait(mbar, mph);
+        mph ^= 1;
+        tc_fence_after();
+        // Delta^T row v = U^T - S^T W^T -> bf16 tile [128 v][64 t]
+        {
+            uint32_t d1[2][32];
+            tmem_ld32_nowait(lane_addr + 128, d1[0]);
+            tmem_ld32_nowait(lane_addr + 160, d1[1]);
+            tmem_wait_ld();
+#pragma unroll
+            for (int gg = 0; gg < 8; ++gg) {
+                float x[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int t = gg * 8 + j;
+                    x[j] = u[t] - __uint_as_float(d1[t >> 5][t & 31]);
+                }
+                *reinterpret_cast<uint4 *>(Dt + sw128_off(v, gg)) =
+                    make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]), pack_bf16x2(x[4], x[5]),
+                               pack_bf16x2(x[6], x[7]));
+            }
+        }
+        fence_proxy_async_shared();
+        tc_fence_before();
+        if (__syncthreads_or(!okm)) break;
+        tc_fence_after();
+        // O^T += Delta^T P^T; S^T += Delta^T (diag(gamma_C/gamma) K)
+        if (v == 0) {
+            const uint64_t dd = sw128_desc(smem_addr(Dt));
+            const uint64_t dp = sw128_desc(smem_addr(img + kImgP)), dk = sw128_desc(smem_addr(img + kImgKd));
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                umma_f16(tmem + 192, dd + 2 * j, dp + 2 * j, id64, 1u);
+                umma_f16(tmem + 0, dd + 2 * j, dk + 2 * j, id128, 1u);
+            }
+            umma_commit(mbar);
+        }
+        okm = mbar_wait(mbar, mph);
+        mph ^= 1;
+        tc_fence_after();
+        // outputs of the chunk, and the next chunk's bf16 S^T operand
+        {
+            uint32_t o2[2][32];
+            tmem_ld32_nowait(lane_addr + 192, o2[0]);
+            tmem_ld32_nowait(lane_addr + 224, o2[1]);
+            tmem_wait_ld();
+            const int tb = n * kC;
+#pragma unroll
+            for (int t = 0; t < 64; ++t)
+                if (tb + t < a.T) a.o[((size_t)(tb + t) * a.Hv + h) * kD + v] = __uint_as_float(o2[t >> 5][t & 31]);
+        }
+        for (int cb = 0; cb < 4; ++cb) {
+            uint32_t r[32];
+            tmem_ld32_nowait(lane_addr + cb * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int gg = 0; gg < 4; ++gg) {
+                const int k0 = cb * 32 + gg * 8;
+                *reinterpret_cast<uint4 *>(St + (k0 >> 6) * 16384 + sw128_off(v, (k0 & 63) >> 3)) =
+                    make_uint4(pack_bf16x2(__uint_as_float(r[8 * gg]), __uint_as_float(r[8 * gg + 1])),
+                               pack_bf16x2(__uint_as_float(r[8 * gg + 2]), __uint_as_float(r[8 * gg + 3])),
+                               pack_bf16x2(__uint_as_float(r[8 * gg + 4]), __uint_as_float(r[8 * gg + 5])),
+                               pack_bf16x2(__uint_as_float(r[8 * gg + 6]), __uint_as_float(r[8 * gg + 7])));
+            }
+        }
+        fence_proxy_async_shared();
+        tc_fence_before();
+        if (__syncthreads_or(!okm)) break;
+        // ring slot b is free (its MMAs have completed): chunk n+2 goes there
+        if (v == 0 && n + 2 < nc) {
+            mbar_arrive_expect_tx(&full[b], kImgBytes);
+            bulk_g2s(ring + (size_t)b * kImgBytes, a.img + ((size_t)h * nc + n + 2) * kImgBytes, kImgBytes, &full[b]);
+        }
+    }
+    tc_fence_after();
+    if (n == nc) {
+        // final state S[k][v] from S^T in TMEM
+        for (int cb = 0; cb < 4; ++cb) {
+            uint32_t r[32];
+            tmem_ld32_nowait(lane_addr + cb * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) Sg[(size_t)(cb * 32 + j) * kD + v] = __uint_as_float(r[j]);
+        }
+    } else if (v == 0) {
+        // a wait gave up: let the copies and MMAs in flight finish (bounded) before exit
+        for (int m = n; m < n + 2 && m < nc; ++m) mbar_wait(&full[m & 1], (uint32_t)((m >> 1) & 1));
+        mbar_wait(mbar, mph);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 256);
+    }
+}
+
+template <typename K>
+int set_smem(K kern, size_t bytes) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    return (int)e;
+}
+
+}  // namespace
+}  // namespace li
+
+using namespace li;
+
+extern "C" {
+
+size_t li_deltanet_chunk_prefill_workspace_size(int T, int n_v_heads, int head_dim) {
+    if (T <= 0 || n_v_heads <= 0 || head_dim != kD) return 0;
+    const size_t nc = (size_t)(T + kC - 1) / kC;
+    return (size_t)n_v_heads * nc * kImgBytes + (size_t)n_v_heads * nc * kC * kD * 4;
+}
+
+int li_launch_deltanet_chunk_prefill_bf16(const void *q, const void *k, const void *v, const float *g,
+                                          const float *beta, float *state, float *o, int T, int n_k_heads,
+                                          int n_v_heads, int head_dim, float scale, void *workspace,
+                                          size_t workspace_bytes, void *stream) {
+    if (!q || !k || !v || !g || !beta || !state || !o || T < 0 || n_k_heads <= 0 || n_v_heads <= 0)
+        return LI_ERR_BAD_ARG;
+    if (head_dim != kD) return LI_ERR_UNSUPPORTED;
+    if (n_v_heads % n_k_heads) return LI_ERR_BAD_SHAPE;
+    if (T == 0) return 0;
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(workspace)) return LI_ERR_MISALIGNED;
+    if (!workspace || workspace_bytes < li_deltanet_chunk_prefill_workspace_size(T, n_v_heads, head_dim))
+        return LI_ERR_WORKSPACE;
+    static std::once_flag once;
+    static int attr_rc = 0;
+    std::call_once(once, [] {
+        attr_rc = set_smem(gdr_prep_kernel, kPrepSmem);
+        if (!attr_rc) attr_rc = set_smem(gdr_state_kernel, kStateSmem);
+    });
+    if (attr_rc) return attr_rc;
+    PrefillArgs a = {};
+    a.q = (const __nv_bfloat16 *)q; a.k = (const __nv_bfloat16 *)k; a.v = (const __nv_bfloat16 *)v;
+    a.g = g; a.beta = beta; a.state = state; a.o = o;
+    a.T = T; a.Hk = n_k_heads; a.Hv = n_v_heads; a.n_chunks = (T + kC - 1) / kC; a.scale = scale;
+    a.img = (uint8_t *)workspace;
+    a.U = (float *)((uint8_t *)workspace + (size_t)n_v_heads * a.n_chunks * kImgBytes);
+    const cudaStream_t s = (cudaStream_t)stream;
+    gdr_prep_kernel<<<dim3((unsigned)((a.n_chunks + 1) / 2), (unsigned)n_v_heads), 256, kPrepSmem, s>>>(a);
+    int rc = launch_status();
+    if (rc) return rc;
+    gdr_state_kernel<<<(unsigned)n_v_heads, 128, kStateSmem, s>>>(a);
+    return launch_status();
+}
+
+}  // extern "C"

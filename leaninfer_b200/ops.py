@@ -178,6 +178,24 @@ def deltanet_recurrent_f32(q, k, v, g, beta, state_in, *, head_dim, n_tokens, n_
     return out, so
 
 
+def deltanet_chunk_prefill_bf16(q, k, v, g, beta, state, scale: float, workspace=None, out=None):
+    """Chunked (WY, chunk 64) gated delta rule prefill of one sequence on the
+    tensor cores. q, k bf16 [T, Hk, D]; v bf16 [T, Hv, D]; g (log decay), beta
+    fp32 [T, Hv]; state fp32 [Hv, D, D] updated in place. Returns o fp32
+    [T, Hv, D]."""
+    T, Hk, D = q.shape
+    Hv = v.shape[1]
+    lib = _lib.load()
+    ws_bytes = int(lib.li_deltanet_chunk_prefill_workspace_size(T, Hv, D))
+    if workspace is None:
+        workspace = torch.empty(max(ws_bytes, 16), device=q.device, dtype=torch.uint8)
+    o = out if out is not None else torch.empty(T, Hv, D, device=q.device, dtype=torch.float32)
+    check(lib.li_launch_deltanet_chunk_prefill_bf16(_p(q), _p(k), _p(v), _p(g), _p(beta), _p(state), _p(o), T, Hk,
+                                                    Hv, D, scale, _p(workspace), workspace.numel(), _stream()),
+          "li_launch_deltanet_chunk_prefill_bf16")
+    return o
+
+
 class DeltaNetLayerDecode:
     """One DeltaNet layer's device weights plus a workspace, stepping B
     sequences one token at a time through li_launch_deltanet_layer_decode."""

@@ -324,3 +324,45 @@ def test_layer_decode_with_input_norm(cuda, oracle_mod):
 def test_device_status_clean(cuda):
     from leaninfer_b200 import ops
     assert ops.device_status() == 0
+
+
+# --------------------------------------------------------------------------
+# chunked (WY) prefill on the tensor cores
+# --------------------------------------------------------------------------
+def _prefill_inputs(r, n_tok, Hk, Hv, D=128):
+    """Config-4 value distributions: q, k L2-normalised, v N(0,1) (bf16);
+    beta = sigmoid(N(0,1)); a = exp(-softplus(N(0,1)) * exp(N(0,0.5))), g = log a;
+    state N(0, 0.02)."""
+    def bf16_bits(x):
+        u = np.ascontiguousarray(x, np.float32).view(np.uint32)
+        return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)   # round to nearest even
+    q = r.standard_normal((n_tok, Hk, D)).astype(np.float32)
+    k = r.standard_normal((n_tok, Hk, D)).astype(np.float32)
+    q /= np.linalg.norm(q, axis=-1, keepdims=True)
+    k /= np.linalg.norm(k, axis=-1, keepdims=True)
+    v = r.standard_normal((n_tok, Hv, D)).astype(np.float32)
+    beta = (1.0 / (1.0 + np.exp(-r.standard_normal((n_tok, Hv))))).astype(np.float32)
+    g = (-np.log1p(np.exp(r.standard_normal((n_tok, Hv)))) * np.exp(r.normal(0.0, 0.5, (n_tok, Hv)))).astype(np.float32)
+    state = r.normal(0.0, 0.02, (Hv, D, D)).astype(np.float32)
+    return bf16_bits(q), bf16_bits(k), bf16_bits(v), g, beta, state
+
+
+@pytest.mark.parametrize("n_tok,Hk,Hv", [(64, 1, 1), (130, 2, 4), (1000, 2, 2), (2048, 1, 2)])
+def test_chunk_prefill_vs_token_recurrence(cuda, oracle_mod, n_tok, Hk, Hv):
+    """The tensor-core chunked prefill against the oracle's token-by-token
+    recurrence (double precision) on the same bf16 inputs: outputs and final
+    state within 2e-2 normwise (bf16 operands, fp32 accumulation); ragged T
+    covers the zero-padded last chunk."""
+    import torch
+    from leaninfer_b200 import ops
+    r = rng(900 + n_tok + Hv)
+    q, k, v, g, beta, state = _prefill_inputs(r, n_tok, Hk, Hv)
+    scale = 128 ** -0.5
+    st_ref = state.copy()
+    o_ref = oracle_mod.gdr_prefill(q, k, v, g, beta, st_ref, scale)
+    tb = lambda a: torch.from_numpy(a.view(np.int16)).to(cuda).view(torch.bfloat16)
+    st = T(state, cuda)
+    o = ops.deltanet_chunk_prefill_bf16(tb(q), tb(k), tb(v), T(g, cuda), T(beta, cuda), st, scale)
+    torch.cuda.synchronize()
+    assert_close(N(o), o_ref, 2e-2, "prefill outputs")
+    assert_close(N(st), st_ref, 2e-2, "prefill final state")
