@@ -19,11 +19,11 @@
 //     on tcgen05 with T block-diagonal over the pair. It writes, per chunk, the
 //     state kernel's shared-memory image (W, Q~ gamma, P, K^T diag(gamma_C /
 //     gamma), gamma_C, already in the canonical 128B-swizzled K-major tile
-//     layout, bf16) and U (fp32).
+//     layout, bf16) and U (bf16).
 //   gdr_state_kernel (one CTA per v-head, chunks in order): the state lives
 //     transposed, S^T[v][k], in tensor memory (fp32) with a bf16 copy in shared
 //     memory as the MMA operand; per chunk one bulk copy brings the chunk
-//     image (prefetched two chunks ahead), and every contraction has M = 128
+//     image (prefetched two chunks ahead; it also carries U in bf16), and every contraction has M = 128
 //     (v): S^T W^T and S^T (Q~ gamma)^T, then Delta^T = U^T - S^T W^T, then
 //     O^T += Delta^T P^T and S^T = gamma_C S^T + Delta^T (diag(gamma_C/gamma) K).
 // All MMAs are kind::f16 with both operands bf16 and fp32 accumulation.
@@ -44,8 +44,9 @@ constexpr uint32_t kImgW = 0;        // W [64 t][128 k]: two [64][64] tiles
 constexpr uint32_t kImgQ = 16384;    // Q~ gamma [64 t][128 k]: two tiles
 constexpr uint32_t kImgP = 32768;    // P [64 i][64 j]: one tile
 constexpr uint32_t kImgKd = 40960;   // (gamma_C/gamma_t) k_t as [128 k][64 t]: one tile
-constexpr uint32_t kImgG = 57344;    // gamma_C (fp32)
-constexpr uint32_t kImgBytes = 58368;
+constexpr uint32_t kImgU = 57344;    // U [64 t][128 v] bf16, plain row-major
+constexpr uint32_t kImgG = 73728;    // gamma_C (fp32)
+constexpr uint32_t kImgBytes = 74752;
 
 struct PrefillArgs {
     const __nv_bfloat16 *q, *k, *v;   // [T][Hk][D], [T][Hk][D], [T][Hv][D]
@@ -55,7 +56,6 @@ struct PrefillArgs {
     int T, Hk, Hv, n_chunks;
     float scale;
     uint8_t *img;                     // [Hv][n_chunks][kImgBytes]
-    float *U;                         // [Hv][n_chunks][64][128]
 };
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -123,37 +123,49 @@ __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a) {
         if (warp & 1) gc[tid] += wsum[warp - 1];   // second warp of each chunk
         gam[tid] = expf(gc[tid]);
     }
-    // 2. operands: K, Q rows as [r][d] tiles; (beta gamma K)^T, (beta V)^T as [d][r] tiles
+    // 2. operands: K, Q rows as [r][d] tiles (V rows staged in the T tile's
+    // space); then (beta gamma K)^T, (beta V)^T as [d][r] tiles and each
+    // chunk's K^T diag(gamma_C/gamma) image tile, all from shared memory
+    uint8_t *Vs = Tt;
     for (int e = tid; e < 128 * 16; e += 256) {
         const int r = e >> 4, gi = e & 15, t = t0 + r;
-        uint4 kv = make_uint4(0, 0, 0, 0), qv = kv;
+        uint4 kv = make_uint4(0, 0, 0, 0), qv = kv, vv = kv;
         if (t < a.T) {
             kv = *reinterpret_cast<const uint4 *>(a.k + ((size_t)t * a.Hk + hk) * kD + gi * 8);
             qv = *reinterpret_cast<const uint4 *>(a.q + ((size_t)t * a.Hk + hk) * kD + gi * 8);
+            vv = *reinterpret_cast<const uint4 *>(a.v + ((size_t)t * a.Hv + h) * kD + gi * 8);
         }
-        *reinterpret_cast<uint4 *>(Kt + (gi >> 3) * 16384 + sw128_off(r, gi & 7)) = kv;
-        *reinterpret_cast<uint4 *>(Qt + (gi >> 3) * 16384 + sw128_off(r, gi & 7)) = qv;
+        const uint32_t off = (gi >> 3) * 16384 + sw128_off(r, gi & 7);
+        *reinterpret_cast<uint4 *>(Kt + off) = kv;
+        *reinterpret_cast<uint4 *>(Qt + off) = qv;
+        *reinterpret_cast<uint4 *>(Vs + off) = vv;
     }
-    __syncthreads();   // gam, bet complete
+    __syncthreads();   // gam, bet and the row tiles complete
+    const int chunk0 = 2 * pair;
     for (int e = tid; e < 128 * 16; e += 256) {
         const int d = e & 127, rg = e >> 7;   // output row d, granule rg: tokens 8rg .. 8rg+7
-        float kx[8], vx[8];
+        const int c = rg >> 3, tg = rg & 7;
+        const float gl = gc[c * 64 + 63];
+        float kx[8], vx[8], kd[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const int r = rg * 8 + j, t = t0 + r;
-            float kk = 0.f, vv = 0.f;
-            if (t < a.T) {
-                kk = __bfloat162float(a.k[((size_t)t * a.Hk + hk) * kD + d]);
-                vv = __bfloat162float(a.v[((size_t)t * a.Hv + h) * kD + d]);
-            }
+            const int r = rg * 8 + j;
+            const float kk = tile_get(Kt + (d >> 6) * 16384, r, d & 63);
             kx[j] = kk * (bet[r] * gam[r]);
-            vx[j] = vv * bet[r];
+            kd[j] = kk * expf(gl - gc[r]);
+            vx[j] = tile_get(Vs + (d >> 6) * 16384, r, d & 63) * bet[r];
         }
         const uint32_t off = (rg >> 3) * 16384 + sw128_off(d, rg & 7);
         *reinterpret_cast<uint4 *>(Kb + off) = make_uint4(pack_bf16x2(kx[0], kx[1]), pack_bf16x2(kx[2], kx[3]),
                                                           pack_bf16x2(kx[4], kx[5]), pack_bf16x2(kx[6], kx[7]));
         *reinterpret_cast<uint4 *>(Vb + off) = make_uint4(pack_bf16x2(vx[0], vx[1]), pack_bf16x2(vx[2], vx[3]),
                                                           pack_bf16x2(vx[4], vx[5]), pack_bf16x2(vx[6], vx[7]));
+        if (chunk0 + c < a.n_chunks) {
+            uint8_t *img = a.img + ((size_t)h * a.n_chunks + chunk0 + c) * kImgBytes;
+            *reinterpret_cast<uint4 *>(img + kImgKd + sw128_off(d, tg)) =
+                make_uint4(pack_bf16x2(kd[0], kd[1]), pack_bf16x2(kd[2], kd[3]), pack_bf16x2(kd[4], kd[5]),
+                           pack_bf16x2(kd[6], kd[7]));
+        }
     }
     fence_proxy_async_shared();
     tc_fence_before();
@@ -175,7 +187,6 @@ __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a) {
     }
     bool ok = mbar_wait(&bar[0], 0);
     tc_fence_after();
-    const int chunk0 = 2 * pair;
     // 4. rows: A (to shared memory), P, Q~ gamma, gamma_C (to the chunk images)
     if (ok && tid < 128) {
         const int r = tid, c = r >> 6, i = r & 63;
@@ -220,25 +231,6 @@ __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a) {
                 *reinterpret_cast<uint4 *>(img + kImgQ + (gi >> 3) * 8192 + sw128_off(i, gi & 7)) = o4;
             }
             if (i == 63) *reinterpret_cast<float *>(img + kImgG) = gam[r];
-        }
-    }
-    // K^T diag(gamma_C/gamma) as [128 k][64 t] per chunk
-    if (ok) {
-        for (int e = tid; e < 2 * 128 * 8; e += 256) {
-            const int kx = e & 127, tg = (e >> 7) & 7, c = e >> 10;
-            const int chunk = chunk0 + c;
-            if (chunk >= a.n_chunks) continue;
-            const float gl = gc[c * 64 + 63];
-            float vals[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int r = c * 64 + tg * 8 + j;
-                vals[j] = tile_get(Kt + (kx >> 6) * 16384, r, kx & 63) * expf(gl - gc[r]);
-            }
-            uint8_t *img = a.img + ((size_t)h * a.n_chunks + chunk) * kImgBytes;
-            *reinterpret_cast<uint4 *>(img + kImgKd + sw128_off(kx, tg)) =
-                make_uint4(pack_bf16x2(vals[0], vals[1]), pack_bf16x2(vals[2], vals[3]),
-                           pack_bf16x2(vals[4], vals[5]), pack_bf16x2(vals[6], vals[7]));
         }
     }
     __syncthreads();   // Qt consumed: Tf may overwrite it
@@ -321,7 +313,7 @@ __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a) {
         if (chunk < a.n_chunks) {
             const uint32_t lane_addr = tmem + ((uint32_t)(32 * warp) << 16);
             uint8_t *img = a.img + ((size_t)h * a.n_chunks + chunk) * kImgBytes;
-            float *Ur = a.U + (((size_t)h * a.n_chunks + chunk) * kC + i) * kD;
+            uint4 *Ur = reinterpret_cast<uint4 *>(img + kImgU + i * 256);
             for (int cb = 0; cb < 4; ++cb) {
                 uint32_t w[32], u[32];
                 tmem_ld32_nowait(lane_addr + 256 + cb * 32, w);
@@ -335,12 +327,12 @@ __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a) {
                                    pack_bf16x2(__uint_as_float(w[8 * gg + 2]), __uint_as_float(w[8 * gg + 3])),
                                    pack_bf16x2(__uint_as_float(w[8 * gg + 4]), __uint_as_float(w[8 * gg + 5])),
                                    pack_bf16x2(__uint_as_float(w[8 * gg + 6]), __uint_as_float(w[8 * gg + 7])));
+                    Ur[cb * 4 + gg] =
+                        make_uint4(pack_bf16x2(__uint_as_float(u[8 * gg]), __uint_as_float(u[8 * gg + 1])),
+                                   pack_bf16x2(__uint_as_float(u[8 * gg + 2]), __uint_as_float(u[8 * gg + 3])),
+                                   pack_bf16x2(__uint_as_float(u[8 * gg + 4]), __uint_as_float(u[8 * gg + 5])),
+                                   pack_bf16x2(__uint_as_float(u[8 * gg + 6]), __uint_as_float(u[8 * gg + 7])));
                 }
-#pragma unroll
-                for (int q4 = 0; q4 < 8; ++q4)
-                    *reinterpret_cast<float4 *>(Ur + cb * 32 + q4 * 4) =
-                        make_float4(__uint_as_float(u[4 * q4]), __uint_as_float(u[4 * q4 + 1]),
-                                    __uint_as_float(u[4 * q4 + 2]), __uint_as_float(u[4 * q4 + 3]));
             }
         }
     }
@@ -358,12 +350,26 @@ __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// state: one CTA per v-head, 128 threads (thread v = TMEM lane v), chunks in order
+// state: one CTA per v-head, 256 threads; warp w serves TMEM lane quarter
+// w % 4 (v = 32 (w % 4) + lane) and column half w / 4; chunks in order
 // ---------------------------------------------------------------------------
 constexpr uint32_t kStRing = 0, kStS = 2 * kImgBytes, kStDt = kStS + 32768, kStMisc = kStDt + 16384;
 constexpr size_t kStateSmem = kStMisc + 64 + 1024;
 
-__global__ void __launch_bounds__(128, 1) gdr_state_kernel(PrefillArgs a) {
+__device__ __forceinline__ void st_bf16_granules(uint8_t *tile_base, int row, int k0, const uint32_t (&r)[32]) {
+    // 32 values of `row` (columns k0 .. k0+31, k0 a multiple of 32) into [rows][64] tiles by 64 columns
+#pragma unroll
+    for (int gg = 0; gg < 4; ++gg) {
+        const int k = k0 + gg * 8;
+        *reinterpret_cast<uint4 *>(tile_base + (k >> 6) * 16384 + sw128_off(row, (k & 63) >> 3)) =
+            make_uint4(pack_bf16x2(__uint_as_float(r[8 * gg]), __uint_as_float(r[8 * gg + 1])),
+                       pack_bf16x2(__uint_as_float(r[8 * gg + 2]), __uint_as_float(r[8 * gg + 3])),
+                       pack_bf16x2(__uint_as_float(r[8 * gg + 4]), __uint_as_float(r[8 * gg + 5])),
+                       pack_bf16x2(__uint_as_float(r[8 * gg + 6]), __uint_as_float(r[8 * gg + 7])));
+    }
+}
+
+__global__ void __launch_bounds__(256, 1) gdr_state_kernel(PrefillArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     uint8_t *ring = sm + kStRing, *St = sm + kStS, *Dt = sm + kStDt;
@@ -371,10 +377,12 @@ __global__ void __launch_bounds__(128, 1) gdr_state_kernel(PrefillArgs a) {
     uint64_t *mbar = full + 2;
     uint32_t *holder = reinterpret_cast<uint32_t *>(mbar + 1);
 
-    const int v = threadIdx.x, warp = v / 32;
+    const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+    const int q4 = warp & 3, half = warp >> 2;
+    const int v = 32 * q4 + lane;
     const int h = blockIdx.x;
     const int nc = a.n_chunks;
-    if (v == 0) {
+    if (tid == 0) {
         mbar_init(&full[0], 1);
         mbar_init(&full[1], 1);
         mbar_init(mbar, 1);
@@ -382,7 +390,7 @@ __global__ void __launch_bounds__(128, 1) gdr_state_kernel(PrefillArgs a) {
     }
     if (warp == 0) tmem_alloc(holder, 256);
     __syncthreads();
-    if (v == 0) {
+    if (tid == 0) {
         for (int n = 0; n < 2 && n < nc; ++n) {
             mbar_arrive_expect_tx(&full[n], kImgBytes);
             bulk_g2s(ring + (size_t)n * kImgBytes, a.img + ((size_t)h * nc + n) * kImgBytes, kImgBytes, &full[n]);
@@ -392,23 +400,16 @@ __global__ void __launch_bounds__(128, 1) gdr_state_kernel(PrefillArgs a) {
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *holder;
-    const uint32_t lane_addr = tmem + ((uint32_t)(32 * warp) << 16);
+    const uint32_t lane_addr = tmem + ((uint32_t)(32 * q4) << 16);
     float *Sg = a.state + (size_t)h * kD * kD;
-    // S^T row v: S[k][v], k = 0..127 -> TMEM cols [0,128) and the bf16 operand tiles
-    for (int cb = 0; cb < 4; ++cb) {
+    // S^T row v, columns k in this warp's half: S[k][v] -> TMEM and the bf16 operand tiles
+    for (int cb = 0; cb < 2; ++cb) {
+        const int k0 = half * 64 + cb * 32;
         uint32_t r[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(Sg[(size_t)(cb * 32 + j) * kD + v]);
-        tmem_st32(lane_addr + cb * 32, r);
-#pragma unroll
-        for (int gg = 0; gg < 4; ++gg) {
-            const int k0 = cb * 32 + gg * 8;
-            *reinterpret_cast<uint4 *>(St + (k0 >> 6) * 16384 + sw128_off(v, (k0 & 63) >> 3)) =
-                make_uint4(pack_bf16x2(__uint_as_float(r[8 * gg]), __uint_as_float(r[8 * gg + 1])),
-                           pack_bf16x2(__uint_as_float(r[8 * gg + 2]), __uint_as_float(r[8 * gg + 3])),
-                           pack_bf16x2(__uint_as_float(r[8 * gg + 4]), __uint_as_float(r[8 * gg + 5])),
-                           pack_bf16x2(__uint_as_float(r[8 * gg + 6]), __uint_as_float(r[8 * gg + 7])));
-        }
+        for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(Sg[(size_t)(k0 + j) * kD + v]);
+        tmem_st32(lane_addr + k0, r);
+        st_bf16_granules(St, v, k0, r);
     }
     tmem_wait_st();
     fence_proxy_async_shared();
@@ -425,7 +426,7 @@ __global__ void __launch_bounds__(128, 1) gdr_state_kernel(PrefillArgs a) {
         if (__syncthreads_or(!okf)) break;
         tc_fence_after();
         // S^T W^T -> cols [128,192); S^T (Q~ gamma)^T -> cols [192,256)
-        if (v == 0) {
+        if (tid == 0) {
             for (int kb = 0; kb < 2; ++kb) {
                 const uint64_t ds = sw128_desc(smem_addr(St + kb * 16384));
                 const uint64_t dw = sw128_desc(smem_addr(img + kImgW + kb * 8192));
@@ -438,49 +439,48 @@ __global__ void __launch_bounds__(128, 1) gdr_state_kernel(PrefillArgs a) {
             }
             umma_commit(mbar);
         }
-        // meanwhile: U^T row v of this chunk, and S^T *= gamma_C in TMEM
+        // meanwhile: U^T (this thread's 32 tokens) and S^T *= gamma_C (its 64 columns)
         const float gC = *reinterpret_cast<const float *>(img + kImgG);
-        const float *Uc = a.U + ((size_t)h * nc + n) * kC * kD;
-        float u[64];
+        float u[32];
+        {
+            const __nv_bfloat16 *Ub = reinterpret_cast<const __nv_bfloat16 *>(img + kImgU);
 #pragma unroll
-        for (int t = 0; t < 64; ++t) u[t] = Uc[(size_t)t * kD + v];
-        for (int cb = 0; cb < 4; ++cb) {
+            for (int t = 0; t < 32; ++t) u[t] = __bfloat162float(Ub[(half * 32 + t) * kD + v]);
+        }
+        for (int cb = 0; cb < 2; ++cb) {
+            const uint32_t col = half * 64 + cb * 32;
             uint32_t r[32];
-            tmem_ld32_nowait(lane_addr + cb * 32, r);
+            tmem_ld32_nowait(lane_addr + col, r);
             tmem_wait_ld();
 #pragma unroll
             for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * gC);
-            tmem_st32(lane_addr + cb * 32, r);
+            tmem_st32(lane_addr + col, r);
         }
         tmem_wait_st();
         bool okm = mbar_wait(mbar, mph);
         mph ^= 1;
         tc_fence_after();
-        // Delta^T row v = U^T - S^T W^T -> bf16 tile [128 v][64 t]
+        // Delta^T row v (tokens half*32 ..) = U^T - S^T W^T -> bf16 tile [128 v][64 t]
         {
-            uint32_t d1[2][32];
-            tmem_ld32_nowait(lane_addr + 128, d1[0]);
-            tmem_ld32_nowait(lane_addr + 160, d1[1]);
+            uint32_t d1[32];
+            tmem_ld32_nowait(lane_addr + 128 + half * 32, d1);
             tmem_wait_ld();
 #pragma unroll
-            for (int gg = 0; gg < 8; ++gg) {
-                float x[8];
+            for (int t = 0; t < 32; ++t) d1[t] = __float_as_uint(u[t] - __uint_as_float(d1[t]));
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int t = gg * 8 + j;
-                    x[j] = u[t] - __uint_as_float(d1[t >> 5][t & 31]);
-                }
-                *reinterpret_cast<uint4 *>(Dt + sw128_off(v, gg)) =
-                    make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]), pack_bf16x2(x[4], x[5]),
-                               pack_bf16x2(x[6], x[7]));
-            }
+            for (int gg = 0; gg < 4; ++gg)
+                *reinterpret_cast<uint4 *>(Dt + sw128_off(v, half * 4 + gg)) =
+                    make_uint4(pack_bf16x2(__uint_as_float(d1[8 * gg]), __uint_as_float(d1[8 * gg + 1])),
+                               pack_bf16x2(__uint_as_float(d1[8 * gg + 2]), __uint_as_float(d1[8 * gg + 3])),
+                               pack_bf16x2(__uint_as_float(d1[8 * gg + 4]), __uint_as_float(d1[8 * gg + 5])),
+                               pack_bf16x2(__uint_as_float(d1[8 * gg + 6]), __uint_as_float(d1[8 * gg + 7])));
         }
         fence_proxy_async_shared();
         tc_fence_before();
         if (__syncthreads_or(!okm)) break;
         tc_fence_after();
         // O^T += Delta^T P^T; S^T += Delta^T (diag(gamma_C/gamma) K)
-        if (v == 0) {
+        if (tid == 0) {
             const uint64_t dd = sw128_desc(smem_addr(Dt));
             const uint64_t dp = sw128_desc(smem_addr(img + kImgP)), dk = sw128_desc(smem_addr(img + kImgKd));
 #pragma unroll
@@ -493,36 +493,28 @@ __global__ void __launch_bounds__(128, 1) gdr_state_kernel(PrefillArgs a) {
         okm = mbar_wait(mbar, mph);
         mph ^= 1;
         tc_fence_after();
-        // outputs of the chunk, and the next chunk's bf16 S^T operand
+        // outputs of the chunk (tokens half*32 ..), and the next chunk's bf16 S^T operand
         {
-            uint32_t o2[2][32];
-            tmem_ld32_nowait(lane_addr + 192, o2[0]);
-            tmem_ld32_nowait(lane_addr + 224, o2[1]);
+            uint32_t o2[32];
+            tmem_ld32_nowait(lane_addr + 192 + half * 32, o2);
             tmem_wait_ld();
-            const int tb = n * kC;
+            const int tb = n * kC + half * 32;
 #pragma unroll
-            for (int t = 0; t < 64; ++t)
-                if (tb + t < a.T) a.o[((size_t)(tb + t) * a.Hv + h) * kD + v] = __uint_as_float(o2[t >> 5][t & 31]);
+            for (int t = 0; t < 32; ++t)
+                if (tb + t < a.T) a.o[((size_t)(tb + t) * a.Hv + h) * kD + v] = __uint_as_float(o2[t]);
         }
-        for (int cb = 0; cb < 4; ++cb) {
+        for (int cb = 0; cb < 2; ++cb) {
+            const int k0 = half * 64 + cb * 32;
             uint32_t r[32];
-            tmem_ld32_nowait(lane_addr + cb * 32, r);
+            tmem_ld32_nowait(lane_addr + k0, r);
             tmem_wait_ld();
-#pragma unroll
-            for (int gg = 0; gg < 4; ++gg) {
-                const int k0 = cb * 32 + gg * 8;
-                *reinterpret_cast<uint4 *>(St + (k0 >> 6) * 16384 + sw128_off(v, (k0 & 63) >> 3)) =
-                    make_uint4(pack_bf16x2(__uint_as_float(r[8 * gg]), __uint_as_float(r[8 * gg + 1])),
-                               pack_bf16x2(__uint_as_float(r[8 * gg + 2]), __uint_as_float(r[8 * gg + 3])),
-                               pack_bf16x2(__uint_as_float(r[8 * gg + 4]), __uint_as_float(r[8 * gg + 5])),
-                               pack_bf16x2(__uint_as_float(r[8 * gg + 6]), __uint_as_float(r[8 * gg + 7])));
-            }
+            st_bf16_granules(St, v, k0, r);
         }
         fence_proxy_async_shared();
         tc_fence_before();
         if (__syncthreads_or(!okm)) break;
         // ring slot b is free (its MMAs have completed): chunk n+2 goes there
-        if (v == 0 && n + 2 < nc) {
+        if (tid == 0 && n + 2 < nc) {
             mbar_arrive_expect_tx(&full[b], kImgBytes);
             bulk_g2s(ring + (size_t)b * kImgBytes, a.img + ((size_t)h * nc + n + 2) * kImgBytes, kImgBytes, &full[b]);
         }
@@ -530,14 +522,15 @@ __global__ void __launch_bounds__(128, 1) gdr_state_kernel(PrefillArgs a) {
     tc_fence_after();
     if (n == nc) {
         // final state S[k][v] from S^T in TMEM
-        for (int cb = 0; cb < 4; ++cb) {
+        for (int cb = 0; cb < 2; ++cb) {
+            const int k0 = half * 64 + cb * 32;
             uint32_t r[32];
-            tmem_ld32_nowait(lane_addr + cb * 32, r);
+            tmem_ld32_nowait(lane_addr + k0, r);
             tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) Sg[(size_t)(cb * 32 + j) * kD + v] = __uint_as_float(r[j]);
+            for (int j = 0; j < 32; ++j) Sg[(size_t)(k0 + j) * kD + v] = __uint_as_float(r[j]);
         }
-    } else if (v == 0) {
+    } else if (tid == 0) {
         // a wait gave up: let the copies and MMAs in flight finish (bounded) before exit
         for (int m = n; m < n + 2 && m < nc; ++m) mbar_wait(&full[m & 1], (uint32_t)((m >> 1) & 1));
         mbar_wait(mbar, mph);
@@ -566,7 +559,7 @@ extern "C" {
 size_t li_deltanet_chunk_prefill_workspace_size(int T, int n_v_heads, int head_dim) {
     if (T <= 0 || n_v_heads <= 0 || head_dim != kD) return 0;
     const size_t nc = (size_t)(T + kC - 1) / kC;
-    return (size_t)n_v_heads * nc * kImgBytes + (size_t)n_v_heads * nc * kC * kD * 4;
+    return (size_t)n_v_heads * nc * kImgBytes;
 }
 
 int li_launch_deltanet_chunk_prefill_bf16(const void *q, const void *k, const void *v, const float *g,
@@ -593,12 +586,11 @@ int li_launch_deltanet_chunk_prefill_bf16(const void *q, const void *k, const vo
     a.g = g; a.beta = beta; a.state = state; a.o = o;
     a.T = T; a.Hk = n_k_heads; a.Hv = n_v_heads; a.n_chunks = (T + kC - 1) / kC; a.scale = scale;
     a.img = (uint8_t *)workspace;
-    a.U = (float *)((uint8_t *)workspace + (size_t)n_v_heads * a.n_chunks * kImgBytes);
     const cudaStream_t s = (cudaStream_t)stream;
     gdr_prep_kernel<<<dim3((unsigned)((a.n_chunks + 1) / 2), (unsigned)n_v_heads), 256, kPrepSmem, s>>>(a);
     int rc = launch_status();
     if (rc) return rc;
-    gdr_state_kernel<<<(unsigned)n_v_heads, 128, kStateSmem, s>>>(a);
+    gdr_state_kernel<<<(unsigned)n_v_heads, 256, kStateSmem, s>>>(a);
     return launch_status();
 }
 
