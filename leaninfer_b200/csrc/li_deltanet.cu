@@ -47,6 +47,9 @@ namespace li {
 namespace {
 
 constexpr int kRecThreads = 256;
+// Three resident CTAs per SM (registers capped at 80 per thread, a few
+// spilled): more state loads stay in flight while other CTAs compute.
+constexpr int kRecMinBlocks = 3;
 constexpr int kRecWarps = 8;
 
 struct RecArgs {
@@ -101,7 +104,7 @@ __device__ __forceinline__ void vstore(float *dst, const float *src) {
 }
 
 template <int D, bool LAYER, int RB>
-__global__ void __launch_bounds__(kRecThreads)
+__global__ void __launch_bounds__(kRecThreads, kRecMinBlocks)
 recurrent_kernel(RecArgs a) {
     constexpr int RPL = RB / 32;                 // value rows per lane
     constexpr int CPW = D / kRecWarps;           // key columns per warp
