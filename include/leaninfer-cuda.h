@@ -214,7 +214,7 @@ int li_launch_fused_rms_norm_swiglu_q(int wtype,
         int K, int N, int n_rows, float eps, void * stream);
 
 /* Whole SwiGLU FFN: y = Wd . (silu(Wg.xn) * (Wu.xn)), xn = rmsnorm(x).
- * Wg, Wu [N, K]; Wd [K, N]. The intermediate h (and, from 8 rows on, the
+ * Wg, Wu [N, K]; Wd [K, N]. The intermediate h (and, from 3 rows on, the
  * f16 operands of the tensor-core path) live in the workspace. */
 size_t li_fused_ffn_workspace_size(int K, int N, int n_rows);
 int li_launch_fused_ffn_q(int wtype,

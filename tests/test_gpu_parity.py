@@ -140,9 +140,9 @@ def test_matmul_q_shapes(cuda, oracle_mod, wtype, n_rows):
 
 
 @pytest.mark.parametrize("wtype", [8, 12])
-@pytest.mark.parametrize("n_rows", [2, 8, 32, 64, 256])
+@pytest.mark.parametrize("n_rows", [2, 5, 8, 32, 64, 256])
 def test_ffn_q(cuda, oracle_mod, wtype, n_rows):
-    """RMSNorm + SwiGLU gate/up + down, reduced width (K=1024, N=3072); from 8
+    """RMSNorm + SwiGLU gate/up + down, reduced width (K=1024, N=3072); from 3
     rows on the gate/up and down contractions run on the tensor cores (A tiles
     in tensor memory; at 256 rows the gate/up accumulators fill the TMEM and
     the A tiles go through shared memory)."""
@@ -279,7 +279,8 @@ def _layer(cuda, w, repeat_type=0, in_norm_w=None):
     (12, 2, 1024, 4, 8, 0),
     (8, 3, 1024, 2, 8, 1),
     (12, 1, 4096, 16, 32, 0),      # the decode workload's layer shape
-    (12, 8, 1024, 4, 8, 0),        # tensor-core projections from here on
+    (12, 5, 1024, 4, 8, 0),        # tensor-core projections from 3 sequences on
+    (12, 8, 1024, 4, 8, 0),
     (8, 16, 1024, 2, 8, 1),
     (12, 64, 4096, 16, 32, 0),     # the decode workload: layer shape and batch
     (8, 40, 1024, 4, 16, 1),       # 640 (sequence, head) items, k-heads repeated by tiling
