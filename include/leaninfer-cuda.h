@@ -285,6 +285,19 @@ int li_launch_deltanet_chunk_prefill_bf16(const void * q, const void * k, const 
         int T, int n_k_heads, int n_v_heads, int head_dim, float scale,
         void * workspace, size_t workspace_bytes, void * stream);
 
+/* The prefill's output stage (no counterpart in the reference). Gated RMSNorm
+ * of n_rows rows of K values written as bf16:
+ *   dst = bf16(silu(z) * (o * gamma * rsqrt(mean(o^2) + eps)))
+ * (the arithmetic of li_launch_fused_rms_norm_silu_gate_f32); and a bf16
+ * GEMM on the tensor cores, C[M][N] (fp32, row-major) = A[M][K] . W[N][K]^T
+ * with A and W bf16 row-major (fp32 accumulation); M a multiple of 128, N of
+ * 256, K of 64; A, W, C 16-byte aligned. The norm needs K % 4 == 0, o, z,
+ * gamma 16-byte and dst 8-byte aligned. */
+int li_launch_gated_rmsnorm_bf16(const float * o, const float * z, const float * gamma,
+        void * dst, int K, int64_t n_rows, float eps, void * stream);
+int li_launch_gemm_bf16_f32(const void * A, const void * W, float * C,
+        int M, int N, int K, void * stream);
+
 #else  /* no CUDA: the reference's no-op stubs, plus stubs for the new entries */
 
 static inline void li_launch_fused_rms_norm_silu_gate_f32(

@@ -80,6 +80,8 @@ _SIGS = {
     "li_deltanet_chunk_prefill_workspace_size": (c_size_t, [c_int, c_int, c_int]),
     "li_launch_deltanet_chunk_prefill_bf16": (c_int, [c_void_p] * 7 + [c_int] * 4 + [c_float, c_void_p, c_size_t,
                                                                                      c_void_p]),
+    "li_launch_gated_rmsnorm_bf16": (c_int, [c_void_p] * 4 + [c_int, c_int64, c_float, c_void_p]),
+    "li_launch_gemm_bf16_f32": (c_int, [c_void_p] * 3 + [c_int] * 3 + [c_void_p]),
     "li_launch_deltanet_layer_decode": (
         c_int, [POINTER(DeltaNetLayer), c_void_p, c_void_p, c_void_p, c_void_p, c_int,
                 c_void_p, c_size_t, c_void_p]),

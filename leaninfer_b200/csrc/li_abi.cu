@@ -7,6 +7,8 @@ int li_tu_status_dense(int clear);
 int li_tu_status_qgemv(int clear);
 int li_tu_status_deltanet(int clear);
 int li_tu_status_tcgemm(int clear);
+int li_tu_status_prefill(int clear);
+int li_tu_status_gemm_bf16(int clear);
 
 namespace li {
 
@@ -68,6 +70,8 @@ int li_device_status(void) {
     if ((v = li_tu_status_qgemv(1)) && !s) s = v;
     if ((v = li_tu_status_deltanet(1)) && !s) s = v;
     if ((v = li_tu_status_tcgemm(1)) && !s) s = v;
+    if ((v = li_tu_status_prefill(1)) && !s) s = v;
+    if ((v = li_tu_status_gemm_bf16(1)) && !s) s = v;
     return s;
 }
 

@@ -196,6 +196,25 @@ def deltanet_chunk_prefill_bf16(q, k, v, g, beta, state, scale: float, workspace
     return o
 
 
+def gated_rmsnorm_bf16(o, z, gamma, eps: float = 1e-6):
+    """bf16(silu(z) * rmsnorm(o) * gamma) over the last dimension."""
+    K = o.shape[-1]
+    n = o.numel() // K
+    dst = torch.empty(o.shape, device=o.device, dtype=torch.bfloat16)
+    check(_lib.load().li_launch_gated_rmsnorm_bf16(_p(o), _p(z), _p(gamma), _p(dst), K, n, eps, _stream()),
+          "li_launch_gated_rmsnorm_bf16")
+    return dst
+
+
+def gemm_bf16(A, W, out=None):
+    """C (fp32) = A . W^T with A [M, K], W [N, K] bf16, on the tensor cores."""
+    M, K = A.shape
+    N = W.shape[0]
+    C = out if out is not None else torch.empty(M, N, device=A.device, dtype=torch.float32)
+    check(_lib.load().li_launch_gemm_bf16_f32(_p(A), _p(W), _p(C), M, N, K, _stream()), "li_launch_gemm_bf16_f32")
+    return C
+
+
 class DeltaNetLayerDecode:
     """One DeltaNet layer's device weights plus a workspace, stepping B
     sequences one token at a time through li_launch_deltanet_layer_decode."""

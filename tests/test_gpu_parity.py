@@ -367,3 +367,34 @@ def test_chunk_prefill_vs_token_recurrence(cuda, oracle_mod, n_tok, Hk, Hv):
     torch.cuda.synchronize()
     assert_close(N(o), o_ref, 2e-2, "prefill outputs")
     assert_close(N(st), st_ref, 2e-2, "prefill final state")
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 1024), (512, 256, 4096)])
+def test_gemm_bf16_vs_torch_fp32(cuda, M, N, K):
+    """The tensor-core bf16 GEMM (out-projection of the prefill) against a
+    torch fp32 matmul of the same bf16 values: the products are exact and the
+    sums fp32, so only the summation order differs (1e-4 normwise)."""
+    import torch
+    from leaninfer_b200 import ops
+    g = torch.Generator(device=cuda)
+    g.manual_seed(M + N + K)
+    A = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    W = (0.02 * torch.randn(N, K, device=cuda, generator=g)).bfloat16()
+    C = ops.gemm_bf16(A, W)
+    ref = A.float() @ W.float().T
+    torch.cuda.synchronize()
+    assert_close(N_(C), N_(ref), 1e-4, "bf16 gemm")
+
+
+def test_gated_rmsnorm_bf16_vs_oracle(cuda, oracle_mod):
+    from leaninfer_b200 import ops
+    r = rng(4242)
+    o = r.standard_normal((300, 128)).astype(np.float32)
+    z = r.standard_normal((300, 128)).astype(np.float32)
+    gamma = r.uniform(0.5, 1.5, 128).astype(np.float32)
+    got = ops.gated_rmsnorm_bf16(T(o, cuda), T(z, cuda), T(gamma, cuda)).float()
+    assert_close(N_(got), oracle_mod.silu_gate(o, z, gamma), 8e-3, "gated rmsnorm (bf16 output)")
+
+
+def N_(t):
+    return t.detach().float().cpu().numpy()
