@@ -75,14 +75,16 @@ __device__ __forceinline__ float tile_get(const uint8_t *tile, int m, int e) {
 // prep: one CTA per (chunk pair, v-head), 256 threads
 // ---------------------------------------------------------------------------
 constexpr uint32_t kPrepKt = 0, kPrepQt = 32768, kPrepTt = 65536, kPrepKb = 98304, kPrepVb = 131072,
-                   kPrepAf = 163840, kPrepMisc = 196608;
-constexpr size_t kPrepSmem = 196608 + 8192 + 1024;
+                   kPrepAf = 163840;
+constexpr int kAS = 65;   // row stride of the fp32 A matrix (padded: row-parallel column writes)
+constexpr uint32_t kPrepMisc = kPrepAf + 2 * 64 * kAS * 4;
+constexpr size_t kPrepSmem = kPrepMisc + 8192 + 1024;
 
 __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     uint8_t *Kt = sm + kPrepKt, *Qt = sm + kPrepQt, *Tt = sm + kPrepTt, *Kb = sm + kPrepKb, *Vb = sm + kPrepVb;
-    float *Af = reinterpret_cast<float *>(sm + kPrepAf);    // [2][64][64] strictly lower A
+    float *Af = reinterpret_cast<float *>(sm + kPrepAf);    // [2][64][kAS] strictly lower A
     float *Tf = reinterpret_cast<float *>(sm + kPrepQt);    // [2][64][64] T (over Qt once it is consumed)
     float *gc = reinterpret_cast<float *>(sm + kPrepMisc);  // [128] log gamma
     float *gam = gc + 128, *bet = gam + 128, *wsum = bet + 128;   // wsum [4]
@@ -127,6 +129,7 @@ __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a) {
     // space); then (beta gamma K)^T, (beta V)^T as [d][r] tiles and each
     // chunk's K^T diag(gamma_C/gamma) image tile, all from shared memory
     uint8_t *Vs = Tt;
+#pragma unroll
     for (int e = tid; e < 128 * 16; e += 256) {
         const int r = e >> 4, gi = e & 15, t = t0 + r;
         uint4 kv = make_uint4(0, 0, 0, 0), qv = kv, vv = kv;
@@ -187,50 +190,49 @@ __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a) {
     }
     bool ok = mbar_wait(&bar[0], 0);
     tc_fence_after();
-    // 4. rows: A (to shared memory), P, Q~ gamma, gamma_C (to the chunk images)
-    if (ok && tid < 128) {
-        const int r = tid, c = r >> 6, i = r & 63;
+    // 4. rows: A (to shared memory), P, Q~ gamma, gamma_C (to the chunk images);
+    // warp w serves TMEM lane quarter w % 4 (row r) and column half w / 4
+    if (ok) {
+        const int q4 = warp & 3, half = warp >> 2;
+        const int r = 32 * q4 + lane, c = r >> 6, i = r & 63;
         const int chunk = chunk0 + c;
-        const uint32_t lane_addr = tmem + ((uint32_t)(32 * warp) << 16);
-        uint32_t kk[2][32], qk[2][32];
-        tmem_ld32_nowait(lane_addr + c * 64, kk[0]);
-        tmem_ld32_nowait(lane_addr + c * 64 + 32, kk[1]);
-        tmem_ld32_nowait(lane_addr + 128 + c * 64, qk[0]);
-        tmem_ld32_nowait(lane_addr + 128 + c * 64 + 32, qk[1]);
+        const uint32_t lane_addr = tmem + ((uint32_t)(32 * q4) << 16);
+        uint32_t kk[32], qk[32];
+        tmem_ld32_nowait(lane_addr + c * 64 + half * 32, kk);
+        tmem_ld32_nowait(lane_addr + 128 + c * 64 + half * 32, qk);
         tmem_wait_ld();
-        float *Arow = Af + (c * 64 + i) * 64;
-        uint32_t prow[32];
+        float *Arow = Af + (c * 64 + i) * kAS + half * 32;
+        const float gr = gc[r], br = bet[r];
+        uint32_t prow[16];
 #pragma unroll
-        for (int jj = 0; jj < 64; jj += 2) {
+        for (int jj = 0; jj < 32; jj += 2) {
             float pv[2];
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
-                const int j = jj + u;
-                const float ratio = j <= i ? expf(gc[r] - gc[c * 64 + j]) : 0.f;
-                const float kkv = __uint_as_float(kk[j >> 5][j & 31]);
-                const float qkv = __uint_as_float(qk[j >> 5][j & 31]);
-                Arow[j] = j < i ? bet[r] * ratio * kkv : 0.f;
-                pv[u] = a.scale * ratio * qkv;
+                const int jl = jj + u, j = half * 32 + jl;
+                const float ratio = j <= i ? expf(gr - gc[c * 64 + j]) : 0.f;
+                Arow[jl] = j < i ? br * ratio * __uint_as_float(kk[jl]) : 0.f;
+                pv[u] = a.scale * ratio * __uint_as_float(qk[jl]);
             }
             prow[jj >> 1] = pack_bf16x2(pv[0], pv[1]);
         }
         if (chunk < a.n_chunks) {
             uint8_t *img = a.img + ((size_t)h * a.n_chunks + chunk) * kImgBytes;
 #pragma unroll
-            for (int gg = 0; gg < 8; ++gg)
-                *reinterpret_cast<uint4 *>(img + kImgP + sw128_off(i, gg)) =
+            for (int gg = 0; gg < 4; ++gg)
+                *reinterpret_cast<uint4 *>(img + kImgP + sw128_off(i, half * 4 + gg)) =
                     make_uint4(prow[4 * gg], prow[4 * gg + 1], prow[4 * gg + 2], prow[4 * gg + 3]);
             const float qs = a.scale * gam[r];
-#pragma unroll 4
-            for (int gi = 0; gi < 16; ++gi) {
-                const uint4 w = *reinterpret_cast<const uint4 *>(Qt + (gi >> 3) * 16384 + sw128_off(r, gi & 7));
+#pragma unroll
+            for (int g8 = 0; g8 < 8; ++g8) {
+                const uint4 w = *reinterpret_cast<const uint4 *>(Qt + half * 16384 + sw128_off(r, g8));
                 const uint4 o4 = make_uint4(pack_bf16x2(bf16_lo(w.x) * qs, bf16_hi(w.x) * qs),
                                             pack_bf16x2(bf16_lo(w.y) * qs, bf16_hi(w.y) * qs),
                                             pack_bf16x2(bf16_lo(w.z) * qs, bf16_hi(w.z) * qs),
                                             pack_bf16x2(bf16_lo(w.w) * qs, bf16_hi(w.w) * qs));
-                *reinterpret_cast<uint4 *>(img + kImgQ + (gi >> 3) * 8192 + sw128_off(i, gi & 7)) = o4;
+                *reinterpret_cast<uint4 *>(img + kImgQ + half * 8192 + sw128_off(i, g8)) = o4;
             }
-            if (i == 63) *reinterpret_cast<float *>(img + kImgG) = gam[r];
+            if (i == 63 && half == 0) *reinterpret_cast<float *>(img + kImgG) = gam[r];
         }
     }
     __syncthreads();   // Qt consumed: Tf may overwrite it
@@ -239,13 +241,13 @@ __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a) {
     __syncthreads();
     if (tid < 128) {
         const int c = tid >> 6, blk = (tid >> 4) & 3, col = tid & 15;
-        const float *Ab = Af + (c * 64 + blk * 16) * 64 + blk * 16;
+        const float *Ab = Af + (c * 64 + blk * 16) * kAS + blk * 16;
         float x[16];
 #pragma unroll
         for (int ii = 0; ii < 16; ++ii) {
             float s = ii == col ? 1.f : 0.f;
 #pragma unroll
-            for (int kk2 = 0; kk2 < ii; ++kk2) s = fmaf(-Ab[ii * 64 + kk2], x[kk2], s);
+            for (int kk2 = 0; kk2 < ii; ++kk2) s = fmaf(-Ab[ii * kAS + kk2], x[kk2], s);
             x[ii] = s;
         }
         float *Tb = Tf + (c * 64 + blk * 16) * 64 + blk * 16;
@@ -262,7 +264,7 @@ __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a) {
             for (int K = J; K < I; ++K)
 #pragma unroll
                 for (int kk2 = 0; kk2 < 16; ++kk2)
-                    s = fmaf(Af[(c * 64 + I * 16 + ar) * 64 + K * 16 + kk2], Tf[(c * 64 + K * 16 + kk2) * 64 + J * 16 + bc], s);
+                    s = fmaf(Af[(c * 64 + I * 16 + ar) * kAS + K * 16 + kk2], Tf[(c * 64 + K * 16 + kk2) * 64 + J * 16 + bc], s);
             Mt[bi * 256 + e2] = s;
         }
         __syncthreads();
