@@ -290,6 +290,144 @@ def cpu_baseline(batch: int, steps: int) -> dict:
             "seconds": round(dt, 3)}
 
 
+# --------------------------------------------------------------------------
+# chunked prefill workload (one sequence; replicas only across GPUs)
+# --------------------------------------------------------------------------
+PF_T, PF_HK, PF_HV, PF_D, PF_HIDDEN = 8192, 16, 32, 128, 4096
+# algorithmic FLOPs of one sequence: chunked gated delta rule (per v-head and
+# chunk of 64: 5 C x C x D products, 3 C x D x D, the C^3/3 triangular
+# solve) + the 4096 x 4096 out-projection
+PF_FLOPS = PF_HV * (PF_T // 64) * (5 * 2 * 64 * 64 * 128 + 3 * 2 * 64 * 128 * 128 + 2 * 64 ** 3 // 3) + \
+    2 * PF_T * PF_HIDDEN * PF_HV * PF_D
+
+
+def run_prefill(args, rank: int, world: int, dist) -> dict | None:
+    """One step = one 8192-token sequence through the chunked WY prefill
+    (bf16 q/k/v, fp32 state), the bf16 gated RMSNorm and the bf16 4096x4096
+    out-projection. Each rank runs its own sequences (independent replicas)."""
+    import torch
+    from leaninfer_b200 import _lib, ops
+    from leaninfer_b200.shard import max_over_ranks
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    T, Hk, Hv, Dh = PF_T, PF_HK, PF_HV, PF_D
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    nrm = torch.nn.functional.normalize
+    q = nrm(torch.randn(T, Hk, Dh, device=dev, generator=g), dim=-1).bfloat16()
+    k = nrm(torch.randn(T, Hk, Dh, device=dev, generator=g), dim=-1).bfloat16()
+    v = torch.randn(T, Hv, Dh, device=dev, generator=g).bfloat16()
+    beta = torch.sigmoid(torch.randn(T, Hv, device=dev, generator=g))
+    gl = -torch.nn.functional.softplus(torch.randn(T, Hv, device=dev, generator=g)) * \
+        torch.exp(0.5 * torch.randn(T, Hv, device=dev, generator=g))
+    z = torch.randn(T, Hv * Dh, device=dev, generator=g)
+    gamma = torch.rand(Dh, device=dev, generator=g) + 0.5
+    w_out = (0.02 * torch.randn(PF_HIDDEN, Hv * Dh, device=dev, generator=g)).bfloat16()
+    state0 = 0.02 * torch.randn(Hv, Dh, Dh, device=dev, generator=g)
+    states = [state0.clone() for _ in range(2)]
+    ws = torch.empty(int(_lib.load().li_deltanet_chunk_prefill_workspace_size(T, Hv, Dh)), device=dev,
+                     dtype=torch.uint8)
+    o = torch.empty(T, Hv, Dh, device=dev)
+    y = torch.empty(T, PF_HIDDEN, device=dev)
+    scale = Dh ** -0.5
+
+    def step(i: int):
+        ops.deltanet_chunk_prefill_bf16(q, k, v, gl, beta, states[i % 2], scale, workspace=ws, out=o)
+        og = ops.gated_rmsnorm_bf16(o.view(T * Hv, Dh), z.view(T * Hv, Dh), gamma)
+        ops.gemm_bf16(og.view(T, Hv * Dh), w_out, out=y)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    sampler = ClockSampler(dev.index)
+    sampler.start()
+    time.sleep(0.3)
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_wall0 = time.time()
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    ms = e0.elapsed_time(e1)
+    sampler.stop()
+    # e2e: q, k, v, g, beta, z from pinned host memory, y back, every step
+    hin = [t.cpu().pin_memory() for t in (q, k, v, gl, beta, z)]
+    hy = torch.empty(T, PF_HIDDEN, pin_memory=True)
+    e_steps = max(1, min(args.steps, 5))
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(e_steps):
+        for dst, src in zip((q, k, v, gl, beta, z), hin):
+            dst.copy_(src, non_blocking=True)
+        step(i)
+        hy.copy_(y, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    status = ops.device_status()
+    if status:
+        raise RuntimeError(f"device status {status} after the timed region")
+    ms, e2e_ms = max_over_ranks([ms, e2e_ms], dist, device=dev)
+    if rank != 0:
+        return None
+    peaks = measured_peaks()
+    step_s = ms / 1e3 / args.steps
+    achieved = PF_FLOPS / step_s / 1e12
+    h2d = sum(t.numel() * t.element_size() for t in hin)
+    line = {
+        "metric": "chunked prefill tokens/s", "value": round(world * T * args.steps / (ms / 1e3), 1),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 (fp32 accumulation and state)", "data": "synthetic",
+        "config": {"workload": "deltanet_chunk_prefill_bf16", "tokens_per_sequence": T, "chunk": 64,
+                   "k_heads": Hk, "v_heads": Hv, "head_dim": Dh, "out_proj": "bf16 4096x4096",
+                   "parallelism": f"replicas x{world} (one sequence per step per GPU)",
+                   "l2": "working set per step (q/k/v/z/o/y/workspace, ~1 GB) larger than L2"},
+        "roofline": {"bound": "tensor", "kernel": "prefill step: chunk prep + chunk state + gated norm + bf16 GEMM",
+                     "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": round(achieved / peaks["bf16_tflops"], 4), "peak_source": peaks["source"],
+                     "algorithmic_flops_per_step": PF_FLOPS, "traffic": None},
+        "e2e": {"value": round(world * T * e_steps / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": T * PF_HIDDEN * 4},
+        "gpu_launches": 4 * args.steps,
+        "clocks": sampler.summary(t_wall0, t_wall1),
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_prefill()
+    return line
+
+
+def cpu_baseline_prefill() -> dict:
+    """The oracle's token-by-token recurrence (double precision, all host
+    threads over the heads) on the first 256 tokens of a sequence; the
+    out-projection is not in the sample."""
+    from oracle import oracle
+    r = np.random.Generator(np.random.PCG64(11))
+    n = 256
+
+    def bf16(a):
+        u = np.ascontiguousarray(a, np.float32).view(np.uint32)
+        return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    q = bf16(r.standard_normal((n, PF_HK, PF_D)) / np.sqrt(PF_D))
+    k = bf16(r.standard_normal((n, PF_HK, PF_D)) / np.sqrt(PF_D))
+    v = bf16(r.standard_normal((n, PF_HV, PF_D)))
+    g = (-np.log1p(np.exp(r.standard_normal((n, PF_HV))))).astype(np.float32)
+    beta = (1 / (1 + np.exp(-r.standard_normal((n, PF_HV))))).astype(np.float32)
+    st = np.zeros((PF_HV, PF_D, PF_D), np.float32)
+    t0 = time.perf_counter()
+    oracle.gdr_prefill(q, k, v, g, beta, st, PF_D ** -0.5)
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 2), "unit": "tokens/s", "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"{n} tokens of the chunk recurrence, 32 v-heads (oracle/li_oracle.c token by token, "
+                      f"double precision, {oracle.num_threads()} host threads; out-projection not included)",
+            "seconds": round(dt, 3)}
+
+
 def run_reference(args, rank: int) -> dict | None:
     if rank != 0:
         return None
@@ -314,6 +452,9 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--traffic", type=float, default=None, help="ncu DRAM bytes per step, if captured")
+    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+                    help="decode: the fused DeltaNet layer decode step (the headline); prefill: one 8192-token "
+                         "chunked prefill + gated norm + bf16 out-projection")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -343,7 +484,7 @@ def main():
             dist.barrier()
     _lib.load()
     try:
-        line = run_ours(args, rank, world, dist)
+        line = run_prefill(args, rank, world, dist) if args.workload == "prefill" else run_ours(args, rank, world, dist)
     finally:
         if dist:
             dist.destroy_process_group()
