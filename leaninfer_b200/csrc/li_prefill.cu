@@ -18,18 +18,23 @@
 //     forward substitution (16x16 diagonal blocks, then block rows), W and U
 //     on tcgen05 with T block-diagonal over the pair. It writes, per chunk, the
 //     state kernel's shared-memory image (W, Q~ gamma, P, K^T diag(gamma_C /
-//     gamma), gamma_C, already in the canonical 128B-swizzled K-major tile
-//     layout, bf16) and U (bf16).
+//     gamma), already in the canonical 128B-swizzled K-major tile layout,
+//     bf16) and U (bf16), and gamma_C to a small array beside the images.
 //   gdr_state_kernel (one CTA per v-head, chunks in order): the state lives
 //     transposed, S^T[v][k], in tensor memory (fp32) with a bf16 copy in shared
 //     memory as the MMA operand; per chunk one bulk copy brings the chunk
 //     image (prefetched two chunks ahead; it also carries U in bf16), and every contraction has M = 128
-//     (v): S^T W^T and S^T (Q~ gamma)^T, then Delta^T = U^T - S^T W^T, then
-//     O^T += Delta^T P^T and S^T = gamma_C S^T + Delta^T (diag(gamma_C/gamma) K).
+//     (v): S^T W^T (committed alone, Delta waits only for it), S^T (Q~ gamma)^T
+//     (left to run under Delta), then Delta^T = U^T - S^T W^T, then O^T +=
+//     Delta^T P^T and S^T = gamma_C S^T + Delta^T (diag(gamma_C/gamma) K). O^T is
+//     double-buffered in TMEM; while the next chunk runs it is staged in shared
+//     memory and leaves as one 3-D TMA store. One warp of the nine issues every
+//     MMA and every copy, so the other eight never wait on issue.
 // All MMAs are kind::f16 with both operands bf16 and fp32 accumulation.
 #include "li_common.cuh"
 #include "li_tc.cuh"
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <mutex>
 
@@ -45,8 +50,7 @@ constexpr uint32_t kImgQ = 16384;    // Q~ gamma [64 t][128 k]: two tiles
 constexpr uint32_t kImgP = 32768;    // P [64 i][64 j]: one tile
 constexpr uint32_t kImgKd = 40960;   // (gamma_C/gamma_t) k_t as [128 k][64 t]: one tile
 constexpr uint32_t kImgU = 57344;    // U [64 t][128 v] bf16, plain row-major
-constexpr uint32_t kImgG = 73728;    // gamma_C (fp32)
-constexpr uint32_t kImgBytes = 74752;
+constexpr uint32_t kImgBytes = 73728;   // (gamma_C lives in PrefillArgs::gC)
 
 struct PrefillArgs {
     const __nv_bfloat16 *q, *k, *v;   // [T][Hk][D], [T][Hk][D], [T][Hv][D]
@@ -56,6 +60,7 @@ struct PrefillArgs {
     int T, Hk, Hv, n_chunks;
     float scale;
     uint8_t *img;                     // [Hv][n_chunks][kImgBytes]
+    float *gC;                        // [Hv][n_chunks] gamma_C of each chunk
 };
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -232,7 +237,7 @@ __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a) {
                                             pack_bf16x2(bf16_lo(w.w) * qs, bf16_hi(w.w) * qs));
                 *reinterpret_cast<uint4 *>(img + kImgQ + half * 8192 + sw128_off(i, g8)) = o4;
             }
-            if (i == 63 && half == 0) *reinterpret_cast<float *>(img + kImgG) = gam[r];
+            if (i == 63 && half == 0) a.gC[(size_t)h * a.n_chunks + chunk] = gam[r];
         }
     }
     __syncthreads();   // Qt consumed: Tf may overwrite it
@@ -352,10 +357,13 @@ __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// state: one CTA per v-head, 256 threads; warp w serves TMEM lane quarter
-// w % 4 (v = 32 (w % 4) + lane) and column half w / 4; chunks in order
+// state: one CTA per v-head, chunks in order; 9 warps: warps 0-7 compute (warp
+// w serves TMEM lane quarter w % 4, v = 32 (w % 4) + lane, and column half
+// w / 4), warp 8 issues the MMAs and all TMA traffic (chunk images in, the
+// chunk's outputs out as one 3-D TMA store)
 // ---------------------------------------------------------------------------
-constexpr uint32_t kStRing = 0, kStS = 2 * kImgBytes, kStDt = kStS + 32768, kStMisc = kStDt + 16384;
+constexpr uint32_t kStRing = 0, kStS = 2 * kImgBytes, kStDt = kStS + 32768, kStO = kStDt + 16384,
+                   kStMisc = kStO + 32768;
 constexpr size_t kStateSmem = kStMisc + 64 + 1024;
 
 __device__ __forceinline__ void st_bf16_granules(uint8_t *tile_base, int row, int k0, const uint32_t (&r)[32]) {
@@ -371,16 +379,25 @@ __device__ __forceinline__ void st_bf16_granules(uint8_t *tile_base, int row, in
     }
 }
 
-__global__ void __launch_bounds__(256, 1) gdr_state_kernel(PrefillArgs a) {
+// TMA store of a [64 t][128 v] fp32 tile to o rows (t, h) (tokens past T are clipped)
+__device__ __forceinline__ void tma_store_o(const CUtensorMap *m, const void *src, int h, int t0) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
+                 ::"l"(m), "r"(0), "r"(h), "r"(t0), "r"(smem_addr(src)) : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(288, 1) gdr_state_kernel(PrefillArgs a, const __grid_constant__ CUtensorMap tmO) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     uint8_t *ring = sm + kStRing, *St = sm + kStS, *Dt = sm + kStDt;
+    float *Os = reinterpret_cast<float *>(sm + kStO);                // [64 t][128 v] output staging
     uint64_t *full = reinterpret_cast<uint64_t *>(sm + kStMisc);   // [2]
     uint64_t *mbar = full + 2;
     uint32_t *holder = reinterpret_cast<uint32_t *>(mbar + 1);
 
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-    const int q4 = warp & 3, half = warp >> 2;
+    const bool issuer = warp == 8;
+    const int q4 = warp & 3, half = (warp >> 2) & 1;
     const int v = 32 * q4 + lane;
     const int h = blockIdx.x;
     const int nc = a.n_chunks;
@@ -390,9 +407,9 @@ __global__ void __launch_bounds__(256, 1) gdr_state_kernel(PrefillArgs a) {
         mbar_init(mbar, 1);
         fence_mbar_init();
     }
-    if (warp == 0) tmem_alloc(holder, 256);
+    if (issuer) tmem_alloc(holder, 512);
     __syncthreads();
-    if (tid == 0) {
+    if (issuer && lane == 0) {
         for (int n = 0; n < 2 && n < nc; ++n) {
             mbar_arrive_expect_tx(&full[n], kImgBytes);
             bulk_g2s(ring + (size_t)n * kImgBytes, a.img + ((size_t)h * nc + n) * kImgBytes, kImgBytes, &full[n]);
@@ -404,66 +421,87 @@ __global__ void __launch_bounds__(256, 1) gdr_state_kernel(PrefillArgs a) {
     const uint32_t tmem = *holder;
     const uint32_t lane_addr = tmem + ((uint32_t)(32 * q4) << 16);
     float *Sg = a.state + (size_t)h * kD * kD;
-    // S^T row v, columns k in this warp's half: S[k][v] -> TMEM and the bf16 operand tiles
-    for (int cb = 0; cb < 2; ++cb) {
-        const int k0 = half * 64 + cb * 32;
-        uint32_t r[32];
+    if (!issuer) {
+        // S^T row v, columns k in this warp's half: S[k][v] -> TMEM and the bf16 operand tiles
+        for (int cb = 0; cb < 2; ++cb) {
+            const int k0 = half * 64 + cb * 32;
+            uint32_t r[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(Sg[(size_t)(k0 + j) * kD + v]);
-        tmem_st32(lane_addr + k0, r);
-        st_bf16_granules(St, v, k0, r);
+            for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(Sg[(size_t)(k0 + j) * kD + v]);
+            tmem_st32(lane_addr + k0, r);
+            st_bf16_granules(St, v, k0, r);
+        }
+        tmem_wait_st();
+        fence_proxy_async_shared();
     }
-    tmem_wait_st();
-    fence_proxy_async_shared();
     tc_fence_before();
     __syncthreads();
 
     const uint32_t id64 = idesc_kf16(128, 64, true), id128 = idesc_kf16(128, 128, true);
+    // TMEM columns: S^T [0,128), S^T W^T [128,192), O^T of chunk n in [192 + 64 (n & 1), +64)
+    // (double-buffered: chunk n's outputs leave while chunk n+1 runs)
+    auto stage_o = [&](int m) {   // compute threads: O^T of chunk m (TMEM) -> Os[t][v]
+        uint32_t o2[32];
+        tmem_ld32_nowait(lane_addr + 192 + 64 * (m & 1) + half * 32, o2);
+        tmem_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 32; ++t) Os[(half * 32 + t) * kD + v] = __uint_as_float(o2[t]);
+    };
+    float gC_next = (!issuer && nc > 0) ? a.gC[(size_t)h * nc] : 1.f;
     uint32_t mph = 0;
     int n = 0;
     for (; n < nc; ++n) {
         const int b = n & 1;
         const uint8_t *img = ring + (size_t)b * kImgBytes;
-        const bool okf = mbar_wait(&full[b], (uint32_t)((n >> 1) & 1));
-        if (__syncthreads_or(!okf)) break;
+        const uint32_t d2col = 192 + 64 * (uint32_t)b;
+        const float gC = gC_next;
+        if (!issuer && n + 1 < nc) gC_next = a.gC[(size_t)h * nc + n + 1];
+        bool ok = mbar_wait(&full[b], (uint32_t)((n >> 1) & 1));
+        if (issuer && lane == 0) {
+            asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");   // the last output store has left Os
+        }
+        if (__syncthreads_or(!ok)) break;
         tc_fence_after();
-        // S^T W^T -> cols [128,192); S^T (Q~ gamma)^T -> cols [192,256)
-        if (tid == 0) {
-            for (int kb = 0; kb < 2; ++kb) {
-                const uint64_t ds = sw128_desc(smem_addr(St + kb * 16384));
-                const uint64_t dw = sw128_desc(smem_addr(img + kImgW + kb * 8192));
-                const uint64_t dq = sw128_desc(smem_addr(img + kImgQ + kb * 8192));
+        if (issuer) {
+            if (lane == 0) {
+                // S^T W^T -> cols [128,192), committed alone (Delta needs only it);
+                // then S^T (Q~ gamma)^T -> this chunk's O^T buffer
+                for (int kb = 0; kb < 2; ++kb) {
+                    const uint64_t ds = sw128_desc(smem_addr(St + kb * 16384));
+                    const uint64_t dw = sw128_desc(smem_addr(img + kImgW + kb * 8192));
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    umma_f16(tmem + 128, ds + 2 * j, dw + 2 * j, id64, (kb | j) ? 1u : 0u);
-                    umma_f16(tmem + 192, ds + 2 * j, dq + 2 * j, id64, (kb | j) ? 1u : 0u);
+                    for (int j = 0; j < 4; ++j) umma_f16(tmem + 128, ds + 2 * j, dw + 2 * j, id64, (kb | j) ? 1u : 0u);
+                }
+                umma_commit(mbar);
+                for (int kb = 0; kb < 2; ++kb) {
+                    const uint64_t ds = sw128_desc(smem_addr(St + kb * 16384));
+                    const uint64_t dq = sw128_desc(smem_addr(img + kImgQ + kb * 8192));
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) umma_f16(tmem + d2col, ds + 2 * j, dq + 2 * j, id64, (kb | j) ? 1u : 0u);
                 }
             }
-            umma_commit(mbar);
-        }
-        // meanwhile: U^T (this thread's 32 tokens) and S^T *= gamma_C (its 64 columns)
-        const float gC = *reinterpret_cast<const float *>(img + kImgG);
-        float u[32];
-        {
-            const __nv_bfloat16 *Ub = reinterpret_cast<const __nv_bfloat16 *>(img + kImgU);
+        } else {
+            // the previous chunk's outputs to the staging tile, U^T (this thread's 32
+            // tokens), S^T *= gamma_C (its 64 columns), then Delta^T = U^T - S^T W^T
+            if (n > 0) stage_o(n - 1);
+            float u[32];
+            {
+                const __nv_bfloat16 *Ub = reinterpret_cast<const __nv_bfloat16 *>(img + kImgU);
 #pragma unroll
-            for (int t = 0; t < 32; ++t) u[t] = __bfloat162float(Ub[(half * 32 + t) * kD + v]);
-        }
-        for (int cb = 0; cb < 2; ++cb) {
-            const uint32_t col = half * 64 + cb * 32;
-            uint32_t r[32];
-            tmem_ld32_nowait(lane_addr + col, r);
-            tmem_wait_ld();
+                for (int t = 0; t < 32; ++t) u[t] = __bfloat162float(Ub[(half * 32 + t) * kD + v]);
+            }
+            for (int cb = 0; cb < 2; ++cb) {
+                const uint32_t col = half * 64 + cb * 32;
+                uint32_t r[32];
+                tmem_ld32_nowait(lane_addr + col, r);
+                tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * gC);
-            tmem_st32(lane_addr + col, r);
-        }
-        tmem_wait_st();
-        bool okm = mbar_wait(mbar, mph);
-        mph ^= 1;
-        tc_fence_after();
-        // Delta^T row v (tokens half*32 ..) = U^T - S^T W^T -> bf16 tile [128 v][64 t]
-        {
+                for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * gC);
+                tmem_st32(lane_addr + col, r);
+            }
+            tmem_wait_st();
+            ok = mbar_wait(mbar, mph);
+            tc_fence_after();
             uint32_t d1[32];
             tmem_ld32_nowait(lane_addr + 128 + half * 32, d1);
             tmem_wait_ld();
@@ -476,73 +514,103 @@ __global__ void __launch_bounds__(256, 1) gdr_state_kernel(PrefillArgs a) {
                                pack_bf16x2(__uint_as_float(d1[8 * gg + 2]), __uint_as_float(d1[8 * gg + 3])),
                                pack_bf16x2(__uint_as_float(d1[8 * gg + 4]), __uint_as_float(d1[8 * gg + 5])),
                                pack_bf16x2(__uint_as_float(d1[8 * gg + 6]), __uint_as_float(d1[8 * gg + 7])));
+            fence_proxy_async_shared();   // Dt and Os writes -> the MMAs' and the TMA store's reads
         }
-        fence_proxy_async_shared();
+        mph ^= 1;
         tc_fence_before();
-        if (__syncthreads_or(!okm)) break;
+        if (__syncthreads_or(!ok)) break;
         tc_fence_after();
-        // O^T += Delta^T P^T; S^T += Delta^T (diag(gamma_C/gamma) K)
-        if (tid == 0) {
+        if (issuer && lane == 0) {
+            // O^T += Delta^T P^T; S^T += Delta^T (diag(gamma_C/gamma) K); one commit covers
+            // every MMA of the chunk (the image slot and Delta are free when it arrives)
             const uint64_t dd = sw128_desc(smem_addr(Dt));
             const uint64_t dp = sw128_desc(smem_addr(img + kImgP)), dk = sw128_desc(smem_addr(img + kImgKd));
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                umma_f16(tmem + 192, dd + 2 * j, dp + 2 * j, id64, 1u);
-                umma_f16(tmem + 0, dd + 2 * j, dk + 2 * j, id128, 1u);
-            }
-            umma_commit(mbar);
-        }
-        okm = mbar_wait(mbar, mph);
-        mph ^= 1;
-        tc_fence_after();
-        // outputs of the chunk (tokens half*32 ..), and the next chunk's bf16 S^T operand
-        {
-            uint32_t o2[32];
-            tmem_ld32_nowait(lane_addr + 192 + half * 32, o2);
-            tmem_wait_ld();
-            const int tb = n * kC + half * 32;
+            for (int j = 0; j < 4; ++j) umma_f16(tmem + d2col, dd + 2 * j, dp + 2 * j, id64, 1u);
 #pragma unroll
-            for (int t = 0; t < 32; ++t)
-                if (tb + t < a.T) a.o[((size_t)(tb + t) * a.Hv + h) * kD + v] = __uint_as_float(o2[t]);
+            for (int j = 0; j < 4; ++j) umma_f16(tmem + 0, dd + 2 * j, dk + 2 * j, id128, 1u);
+            umma_commit(mbar);
+            if (n > 0) tma_store_o(&tmO, Os, h, (n - 1) * kC);   // the previous chunk's outputs
         }
-        for (int cb = 0; cb < 2; ++cb) {
-            const int k0 = half * 64 + cb * 32;
-            uint32_t r[32];
-            tmem_ld32_nowait(lane_addr + k0, r);
-            tmem_wait_ld();
-            st_bf16_granules(St, v, k0, r);
+        if (!issuer) {
+            ok = mbar_wait(mbar, mph);
+            tc_fence_after();
+            // the next chunk's bf16 S^T operand
+            for (int cb = 0; cb < 2; ++cb) {
+                const int k0 = half * 64 + cb * 32;
+                uint32_t r[32];
+                tmem_ld32_nowait(lane_addr + k0, r);
+                tmem_wait_ld();
+                st_bf16_granules(St, v, k0, r);
+            }
+            fence_proxy_async_shared();
         }
-        fence_proxy_async_shared();
+        mph ^= 1;
         tc_fence_before();
-        if (__syncthreads_or(!okm)) break;
-        // ring slot b is free (its MMAs have completed): chunk n+2 goes there
-        if (tid == 0 && n + 2 < nc) {
+        if (__syncthreads_or(!ok)) break;
+        // ring slot b is free (every MMA reading it has completed): chunk n+2 goes there
+        if (issuer && lane == 0 && n + 2 < nc) {
             mbar_arrive_expect_tx(&full[b], kImgBytes);
             bulk_g2s(ring + (size_t)b * kImgBytes, a.img + ((size_t)h * nc + n + 2) * kImgBytes, kImgBytes, &full[b]);
         }
     }
     tc_fence_after();
-    if (n == nc) {
-        // final state S[k][v] from S^T in TMEM
-        for (int cb = 0; cb < 2; ++cb) {
-            const int k0 = half * 64 + cb * 32;
-            uint32_t r[32];
-            tmem_ld32_nowait(lane_addr + k0, r);
-            tmem_wait_ld();
+    const bool done = n == nc;
+    if (done) {
+        if (issuer && lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        __syncthreads();
+        if (!issuer) {
+            stage_o(nc - 1);
+            fence_proxy_async_shared();
+            // final state S[k][v] from S^T in TMEM
+            for (int cb = 0; cb < 2; ++cb) {
+                const int k0 = half * 64 + cb * 32;
+                uint32_t r[32];
+                tmem_ld32_nowait(lane_addr + k0, r);
+                tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) Sg[(size_t)(k0 + j) * kD + v] = __uint_as_float(r[j]);
+                for (int j = 0; j < 32; ++j) Sg[(size_t)(k0 + j) * kD + v] = __uint_as_float(r[j]);
+            }
         }
-    } else if (tid == 0) {
+        __syncthreads();
+        if (issuer && lane == 0) tma_store_o(&tmO, Os, h, (nc - 1) * kC);
+    } else if (issuer && lane == 0) {
         // a wait gave up: let the copies and MMAs in flight finish (bounded) before exit
         for (int m = n; m < n + 2 && m < nc; ++m) mbar_wait(&full[m & 1], (uint32_t)((m >> 1) & 1));
         mbar_wait(mbar, mph);
     }
+    if (issuer && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");   // outputs written
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) {
+    if (issuer) {
         tc_fence_after();
-        tmem_dealloc(tmem, 256);
+        tmem_dealloc(tmem, 512);
     }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// o [T][Hv][128] fp32 as a 3-D tensor (v, head, token) for [64 t][128 v] box stores
+int encode_o_map(CUtensorMap *m, float *o, int T, int Hv) {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    if (!fn) return LI_ERR_UNSUPPORTED;
+    const cuuint64_t dims[3] = {(cuuint64_t)kD, (cuuint64_t)Hv, (cuuint64_t)T};
+    const cuuint64_t strides[2] = {(cuuint64_t)kD * 4, (cuuint64_t)Hv * kD * 4};
+    const cuuint32_t box[3] = {(cuuint32_t)kD, 1, (cuuint32_t)kC};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, o, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : LI_ERR_BAD_SHAPE;
 }
 
 template <typename K>
@@ -561,7 +629,7 @@ extern "C" {
 size_t li_deltanet_chunk_prefill_workspace_size(int T, int n_v_heads, int head_dim) {
     if (T <= 0 || n_v_heads <= 0 || head_dim != kD) return 0;
     const size_t nc = (size_t)(T + kC - 1) / kC;
-    return (size_t)n_v_heads * nc * kImgBytes;
+    return (size_t)n_v_heads * nc * kImgBytes + ((size_t)n_v_heads * nc * 4 + 255) / 256 * 256;
 }
 
 int li_launch_deltanet_chunk_prefill_bf16(const void *q, const void *k, const void *v, const float *g,
@@ -583,16 +651,21 @@ int li_launch_deltanet_chunk_prefill_bf16(const void *q, const void *k, const vo
         if (!attr_rc) attr_rc = set_smem(gdr_state_kernel, kStateSmem);
     });
     if (attr_rc) return attr_rc;
+    int rc0 = 0;
     PrefillArgs a = {};
     a.q = (const __nv_bfloat16 *)q; a.k = (const __nv_bfloat16 *)k; a.v = (const __nv_bfloat16 *)v;
     a.g = g; a.beta = beta; a.state = state; a.o = o;
     a.T = T; a.Hk = n_k_heads; a.Hv = n_v_heads; a.n_chunks = (T + kC - 1) / kC; a.scale = scale;
     a.img = (uint8_t *)workspace;
+    a.gC = (float *)((uint8_t *)workspace + (size_t)n_v_heads * a.n_chunks * kImgBytes);
+    if (!aligned16(o)) return LI_ERR_MISALIGNED;
+    CUtensorMap tmO;
+    if ((rc0 = encode_o_map(&tmO, o, T, n_v_heads))) return rc0;
     const cudaStream_t s = (cudaStream_t)stream;
     gdr_prep_kernel<<<dim3((unsigned)((a.n_chunks + 1) / 2), (unsigned)n_v_heads), 256, kPrepSmem, s>>>(a);
     int rc = launch_status();
     if (rc) return rc;
-    gdr_state_kernel<<<(unsigned)n_v_heads, 256, kStateSmem, s>>>(a);
+    gdr_state_kernel<<<(unsigned)n_v_heads, 288, kStateSmem, s>>>(a, tmO);
     return launch_status();
 }
 
