@@ -13,13 +13,14 @@
 //
 // Two kernels:
 //   gdr_prep_kernel (one CTA per v-head and pair of chunks, all in parallel):
-//     K K^T and Q K^T of the 128-token pair on tcgen05 (M = 128; the diagonal
-//     64x64 blocks are the chunks'), A and P from them, T by a blocked fp32
-//     forward substitution (16x16 diagonal blocks, then block rows), W and U
-//     on tcgen05 with T block-diagonal over the pair. It writes, per chunk, the
-//     state kernel's shared-memory image (W, Q~ gamma, P, K^T diag(gamma_C /
-//     gamma), already in the canonical 128B-swizzled K-major tile layout,
-//     bf16) and U (bf16), and gamma_C to a small array beside the images.
+//     K, Q, V rows of the 128-token pair by TMA, K K^T and Q K^T on tcgen05
+//     (M = 128; the diagonal 64x64 blocks are the chunks'), A and P from them,
+//     T by fp32 forward substitution (one column per thread, in registers), W
+//     and U on tcgen05 with T block-diagonal over the pair (the column scalings
+//     folded into T, K and V rows as MN-major operands). It writes, per chunk,
+//     the state kernel's shared-memory image (W, Q~ gamma, P, diag(gamma_C /
+//     gamma) K, all bf16 in the canonical 128B-swizzled tile layouts, and U)
+//     by bulk copies, and gamma_C to a small array beside the images.
 //   gdr_state_kernel (one CTA per v-head, chunks in order): the state lives
 //     transposed, S^T[v][k], in tensor memory (fp32) with a bf16 copy in shared
 //     memory as the MMA operand; per chunk one bulk copy brings the chunk
@@ -48,8 +49,8 @@ constexpr int kD = 128, kC = 64;
 constexpr uint32_t kImgW = 0;        // W [64 t][128 k]: two [64][64] tiles
 constexpr uint32_t kImgQ = 16384;    // Q~ gamma [64 t][128 k]: two tiles
 constexpr uint32_t kImgP = 32768;    // P [64 i][64 j]: one tile
-constexpr uint32_t kImgKd = 40960;   // (gamma_C/gamma_t) k_t as [128 k][64 t]: one tile
-constexpr uint32_t kImgU = 57344;    // U [64 t][128 v] bf16, plain row-major
+constexpr uint32_t kImgKd = 40960;   // (gamma_C/gamma_t) k_t as [64 t][128 k]: two MN-major tiles
+constexpr uint32_t kImgU = 57344;    // U [64 t][128 v] bf16, 256-byte rows, 16-byte granules swizzled (u_off)
 constexpr uint32_t kImgBytes = 73728;   // (gamma_C lives in PrefillArgs::gC)
 
 struct PrefillArgs {
@@ -70,46 +71,132 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
-// element e (0..63) of row m of a [rows][64] bf16 tile
-__device__ __forceinline__ float tile_get(const uint8_t *tile, int m, int e) {
-    const uint16_t b = *reinterpret_cast<const uint16_t *>(tile + sw128_off(m, e >> 3) + (e & 7) * 2);
-    return __uint_as_float((uint32_t)b << 16);
+// byte offset of U[t][v] in the image: granule v / 8 of row t sits at granule
+// (v / 8) ^ (t % 16), so row-parallel granule writes and column-parallel
+// element reads are both free of bank conflicts
+__host__ __device__ __forceinline__ uint32_t u_off(int t, int v) {
+    return (uint32_t)(t * 256 + ((((v >> 3) ^ (t & 15))) << 4) + (v & 7) * 2);
 }
 
 // ---------------------------------------------------------------------------
-// prep: one CTA per (chunk pair, v-head), 256 threads
+// prep: one CTA per (chunk pair, v-head), 256 threads. The 128 rows of K, Q
+// and V come in by TMA as [128 t][64 d] 128B-swizzled tiles (two per
+// matrix); K and V serve unchanged as the MN-major B operands of W and U, and
+// the column scalings diag(beta gamma), diag(beta) go into two bf16 copies of
+// T. Every piece of the chunk images is finished in shared memory in its
+// image layout and leaves by bulk copy.
 // ---------------------------------------------------------------------------
-constexpr uint32_t kPrepKt = 0, kPrepQt = 32768, kPrepTt = 65536, kPrepKb = 98304, kPrepVb = 131072,
-                   kPrepAf = 163840;
-constexpr int kAS = 65;   // row stride of the fp32 A matrix (padded: row-parallel column writes)
+constexpr uint32_t kPrepKt = 0, kPrepQt = 32768, kPrepVt = 65536, kPrepTk = 98304, kPrepTv = 131072,
+                   kPrepPs = 163840, kPrepAf = 180224;
+constexpr int kAS = 68;   // row stride of the fp32 A matrix (16-byte rows; float4 row writes are conflict-free)
 constexpr uint32_t kPrepMisc = kPrepAf + 2 * 64 * kAS * 4;
-constexpr size_t kPrepSmem = kPrepMisc + 8192 + 1024;
+constexpr size_t kPrepSmem = kPrepMisc + 4096 + 1024;
 
-__global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a) {
+__device__ __forceinline__ void st_bf16_granules(uint8_t *tile_base, int row, int k0, const uint32_t (&r)[32]) {
+    // 32 values of `row` (columns k0 .. k0+31, k0 a multiple of 32) into [rows][64] tiles by 64 columns
+#pragma unroll
+    for (int gg = 0; gg < 4; ++gg) {
+        const int k = k0 + gg * 8;
+        *reinterpret_cast<uint4 *>(tile_base + (k >> 6) * 16384 + sw128_off(row, (k & 63) >> 3)) =
+            make_uint4(pack_bf16x2(__uint_as_float(r[8 * gg]), __uint_as_float(r[8 * gg + 1])),
+                       pack_bf16x2(__uint_as_float(r[8 * gg + 2]), __uint_as_float(r[8 * gg + 3])),
+                       pack_bf16x2(__uint_as_float(r[8 * gg + 4]), __uint_as_float(r[8 * gg + 5])),
+                       pack_bf16x2(__uint_as_float(r[8 * gg + 6]), __uint_as_float(r[8 * gg + 7])));
+    }
+}
+
+__device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *map, int x, int y, int z,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];"
+        ::"r"(smem_addr(smem_dst)), "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void bulk_s2g(void *gdst, const void *ssrc, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+                 ::"l"(gdst), "r"(smem_addr(ssrc)), "r"(bytes) : "memory");
+}
+
+// Column j of T = (I + A)^-1 for one chunk by forward substitution, in
+// registers: x_i = [i == j] - sum_{k<i} A[i][k] x_k. Rows below SB and columns
+// k < SB are skipped (every column this is called for has j >= SB, so those x
+// are zero). A rows are zero from the diagonal on, so the float4 steps past
+// k = i - 1 add zeros. Writes T[i][j] beta_j gamma_j and T[i][j] beta_j.
+template <int SB>
+__device__ __forceinline__ void solve_column(const float *Ac, int j, float fk, float fv, uint8_t *tk, uint8_t *tv,
+                                             int row0) {
+    float x[64];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) x[i] = 0.f;
+#pragma unroll
+    for (int i = SB; i < 64; ++i) {
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+        for (int k = SB; k < i; k += 4) {
+            const float4 a4 = *reinterpret_cast<const float4 *>(Ac + i * kAS + k);
+            s0 = fmaf(a4.x, x[k], s0);
+            s1 = fmaf(a4.y, x[k + 1], s1);
+            s2 = fmaf(a4.z, x[k + 2], s2);
+            s3 = fmaf(a4.w, x[k + 3], s3);
+        }
+        const float t = -((s0 + s1) + (s2 + s3));
+        x[i] = i < j ? 0.f : (i == j ? 1.f : t);
+    }
+    const uint32_t cb = (uint32_t)(j & 7) * 2;
+#pragma unroll
+    for (int i = SB; i < 64; ++i) {
+        const uint32_t off = sw128_off(row0 + i, j >> 3) + cb;
+        *reinterpret_cast<__nv_bfloat16 *>(tk + off) = __float2bfloat16_rn(x[i] * fk);
+        *reinterpret_cast<__nv_bfloat16 *>(tv + off) = __float2bfloat16_rn(x[i] * fv);
+    }
+    if (SB > 0) {
+#pragma unroll
+        for (int i = 0; i < SB; ++i) {
+            const uint32_t off = sw128_off(row0 + i, j >> 3) + cb;
+            *reinterpret_cast<__nv_bfloat16 *>(tk + off) = __float2bfloat16_rn(0.f);
+            *reinterpret_cast<__nv_bfloat16 *>(tv + off) = __float2bfloat16_rn(0.f);
+        }
+    }
+}
+
+struct PrepMaps {
+    CUtensorMap k, q, v;   // [T][H][128] bf16 as (d, head, token), box [128 t][64 d], 128B swizzle
+};
+
+__global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a, const __grid_constant__ PrepMaps maps) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
-    uint8_t *Kt = sm + kPrepKt, *Qt = sm + kPrepQt, *Tt = sm + kPrepTt, *Kb = sm + kPrepKb, *Vb = sm + kPrepVb;
+    uint8_t *Kt = sm + kPrepKt, *Qt = sm + kPrepQt, *Vt = sm + kPrepVt, *Tk = sm + kPrepTk, *Tv = sm + kPrepTv;
+    uint8_t *Ps = sm + kPrepPs;                              // P image tiles of both chunks
+    uint8_t *Ws = Vt, *Us = Tk;                              // W, U staging once V, T are consumed
     float *Af = reinterpret_cast<float *>(sm + kPrepAf);    // [2][64][kAS] strictly lower A
-    float *Tf = reinterpret_cast<float *>(sm + kPrepQt);    // [2][64][64] T (over Qt once it is consumed)
     float *gc = reinterpret_cast<float *>(sm + kPrepMisc);  // [128] log gamma
-    float *gam = gc + 128, *bet = gam + 128, *wsum = bet + 128;   // wsum [4]
-    float *Mt = wsum + 8;                                    // [6][16][16] block-solve temporaries
-    uint64_t *bar = reinterpret_cast<uint64_t *>(Mt + 6 * 256);
-    uint32_t *holder = reinterpret_cast<uint32_t *>(bar + 2);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(holder + 1);
+    float *gam = gc + 128, *bet = gam + 128, *fkd = bet + 128, *wsum = fkd + 128;   // wsum [8]
+    uint64_t *bar = reinterpret_cast<uint64_t *>(wsum + 8);   // [3]: loads, K K^T + Q K^T, W + U
+    uint32_t *holder = reinterpret_cast<uint32_t *>(bar + 3);
 
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
     const int h = blockIdx.y, pair = blockIdx.x;
     const int hk = h / (a.Hv / a.Hk);
     const int t0 = pair * 2 * kC;
+    const int chunk0 = 2 * pair;
+    const int nc = a.n_chunks;
+    const int n_valid = nc - chunk0 >= 2 ? 2 : 1;   // chunks of this pair inside the sequence
+    constexpr int kStoreThread = 128;                // issues every bulk store of the CTA
 
     if (tid == 0) {
-        mbar_init(&bar[0], 1);
-        mbar_init(&bar[1], 1);
-        *abort_flag = 0;
+        for (int b = 0; b < 3; ++b) mbar_init(&bar[b], 1);
         fence_mbar_init();
+        mbar_arrive_expect_tx(&bar[0], 6 * 16384);
+        for (int hh = 0; hh < 2; ++hh) {
+            tma_load_3d(Kt + hh * 16384, &maps.k, hh * 64, hk, t0, &bar[0]);
+            tma_load_3d(Qt + hh * 16384, &maps.q, hh * 64, hk, t0, &bar[0]);
+            tma_load_3d(Vt + hh * 16384, &maps.v, hh * 64, h, t0, &bar[0]);
+        }
     }
-    if (warp == 0) tmem_alloc(holder, 512);
+    if (warp == 1) tmem_alloc(holder, 512);
 
     // 1. decay prefix sums (per 64-token chunk), beta
     if (tid < 128) {
@@ -129,60 +216,17 @@ __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a) {
     if (tid < 128) {
         if (warp & 1) gc[tid] += wsum[warp - 1];   // second warp of each chunk
         gam[tid] = expf(gc[tid]);
+        fkd[tid] = expf(gc[(tid & 64) + 63] - gc[tid]);   // gamma_C / gamma_t
     }
-    // 2. operands: K, Q rows as [r][d] tiles (V rows staged in the T tile's
-    // space); then (beta gamma K)^T, (beta V)^T as [d][r] tiles and each
-    // chunk's K^T diag(gamma_C/gamma) image tile, all from shared memory
-    uint8_t *Vs = Tt;
-#pragma unroll
-    for (int e = tid; e < 128 * 16; e += 256) {
-        const int r = e >> 4, gi = e & 15, t = t0 + r;
-        uint4 kv = make_uint4(0, 0, 0, 0), qv = kv, vv = kv;
-        if (t < a.T) {
-            kv = *reinterpret_cast<const uint4 *>(a.k + ((size_t)t * a.Hk + hk) * kD + gi * 8);
-            qv = *reinterpret_cast<const uint4 *>(a.q + ((size_t)t * a.Hk + hk) * kD + gi * 8);
-            vv = *reinterpret_cast<const uint4 *>(a.v + ((size_t)t * a.Hv + h) * kD + gi * 8);
-        }
-        const uint32_t off = (gi >> 3) * 16384 + sw128_off(r, gi & 7);
-        *reinterpret_cast<uint4 *>(Kt + off) = kv;
-        *reinterpret_cast<uint4 *>(Qt + off) = qv;
-        *reinterpret_cast<uint4 *>(Vs + off) = vv;
-    }
-    __syncthreads();   // gam, bet and the row tiles complete
-    const int chunk0 = 2 * pair;
-    for (int e = tid; e < 128 * 16; e += 256) {
-        const int d = e & 127, rg = e >> 7;   // output row d, granule rg: tokens 8rg .. 8rg+7
-        const int c = rg >> 3, tg = rg & 7;
-        const float gl = gc[c * 64 + 63];
-        float kx[8], vx[8], kd[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int r = rg * 8 + j;
-            const float kk = tile_get(Kt + (d >> 6) * 16384, r, d & 63);
-            kx[j] = kk * (bet[r] * gam[r]);
-            kd[j] = kk * expf(gl - gc[r]);
-            vx[j] = tile_get(Vs + (d >> 6) * 16384, r, d & 63) * bet[r];
-        }
-        const uint32_t off = (rg >> 3) * 16384 + sw128_off(d, rg & 7);
-        *reinterpret_cast<uint4 *>(Kb + off) = make_uint4(pack_bf16x2(kx[0], kx[1]), pack_bf16x2(kx[2], kx[3]),
-                                                          pack_bf16x2(kx[4], kx[5]), pack_bf16x2(kx[6], kx[7]));
-        *reinterpret_cast<uint4 *>(Vb + off) = make_uint4(pack_bf16x2(vx[0], vx[1]), pack_bf16x2(vx[2], vx[3]),
-                                                          pack_bf16x2(vx[4], vx[5]), pack_bf16x2(vx[6], vx[7]));
-        if (chunk0 + c < a.n_chunks) {
-            uint8_t *img = a.img + ((size_t)h * a.n_chunks + chunk0 + c) * kImgBytes;
-            *reinterpret_cast<uint4 *>(img + kImgKd + sw128_off(d, tg)) =
-                make_uint4(pack_bf16x2(kd[0], kd[1]), pack_bf16x2(kd[2], kd[3]), pack_bf16x2(kd[4], kd[5]),
-                           pack_bf16x2(kd[6], kd[7]));
-        }
-    }
-    fence_proxy_async_shared();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *holder;
     const uint32_t idesc = idesc_kf16(128, 128, true);
-    // 3. K K^T -> cols [0,128), Q K^T -> cols [128,256)
-    if (tid == 0) {
+    // 2. K K^T -> cols [0,128), Q K^T -> cols [128,256)
+    bool ok = mbar_wait(&bar[0], 0);
+    if (tid == 0 && ok) {
+        tc_fence_after();
         for (int kb = 0; kb < 2; ++kb) {
             const uint64_t dk = sw128_desc(smem_addr(Kt + kb * 16384)), dq = sw128_desc(smem_addr(Qt + kb * 16384));
 #pragma unroll
@@ -191,17 +235,17 @@ __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a) {
                 umma_f16(tmem + 128, dq + 2 * j, dk + 2 * j, idesc, (kb | j) ? 1u : 0u);
             }
         }
-        umma_commit(&bar[0]);
+        umma_commit(&bar[1]);
     }
-    bool ok = mbar_wait(&bar[0], 0);
+    if (ok) ok = mbar_wait(&bar[1], 0);
     tc_fence_after();
-    // 4. rows: A (to shared memory), P, Q~ gamma, gamma_C (to the chunk images);
-    // warp w serves TMEM lane quarter w % 4 (row r) and column half w / 4
+    // 3. rows: A (fp32, shared), P (image tile), Q~ gamma (Q rows scaled in
+    // place: they are the image tiles); warp w serves TMEM lane quarter w % 4
+    // (row r) and column half w / 4
+    const int q4 = warp & 3, half = warp >> 2;
+    const int r = 32 * q4 + lane, c = r >> 6, i = r & 63;
+    const uint32_t lane_addr = tmem + ((uint32_t)(32 * q4) << 16);
     if (ok) {
-        const int q4 = warp & 3, half = warp >> 2;
-        const int r = 32 * q4 + lane, c = r >> 6, i = r & 63;
-        const int chunk = chunk0 + c;
-        const uint32_t lane_addr = tmem + ((uint32_t)(32 * q4) << 16);
         uint32_t kk[32], qk[32];
         tmem_ld32_nowait(lane_addr + c * 64 + half * 32, kk);
         tmem_ld32_nowait(lane_addr + 128 + c * 64 + half * 32, qk);
@@ -210,147 +254,144 @@ __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a) {
         const float gr = gc[r], br = bet[r];
         uint32_t prow[16];
 #pragma unroll
-        for (int jj = 0; jj < 32; jj += 2) {
-            float pv[2];
+        for (int jj = 0; jj < 32; jj += 4) {
+            float av[4];
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
+            for (int u = 0; u < 4; ++u) {
                 const int jl = jj + u, j = half * 32 + jl;
                 const float ratio = j <= i ? expf(gr - gc[c * 64 + j]) : 0.f;
-                Arow[jl] = j < i ? br * ratio * __uint_as_float(kk[jl]) : 0.f;
-                pv[u] = a.scale * ratio * __uint_as_float(qk[jl]);
+                av[u] = j < i ? br * ratio * __uint_as_float(kk[jl]) : 0.f;
+                qk[jl] = __float_as_uint(a.scale * ratio * __uint_as_float(qk[jl]));
             }
-            prow[jj >> 1] = pack_bf16x2(pv[0], pv[1]);
+            *reinterpret_cast<float4 *>(Arow + jj) = make_float4(av[0], av[1], av[2], av[3]);
+            prow[jj >> 1] = pack_bf16x2(__uint_as_float(qk[jj]), __uint_as_float(qk[jj + 1]));
+            prow[(jj >> 1) + 1] = pack_bf16x2(__uint_as_float(qk[jj + 2]), __uint_as_float(qk[jj + 3]));
         }
-        if (chunk < a.n_chunks) {
-            uint8_t *img = a.img + ((size_t)h * a.n_chunks + chunk) * kImgBytes;
 #pragma unroll
-            for (int gg = 0; gg < 4; ++gg)
-                *reinterpret_cast<uint4 *>(img + kImgP + sw128_off(i, half * 4 + gg)) =
-                    make_uint4(prow[4 * gg], prow[4 * gg + 1], prow[4 * gg + 2], prow[4 * gg + 3]);
-            const float qs = a.scale * gam[r];
+        for (int gg = 0; gg < 4; ++gg)
+            *reinterpret_cast<uint4 *>(Ps + c * 8192 + sw128_off(i, half * 4 + gg)) =
+                make_uint4(prow[4 * gg], prow[4 * gg + 1], prow[4 * gg + 2], prow[4 * gg + 3]);
+        const float qs = a.scale * gam[r];
 #pragma unroll
-            for (int g8 = 0; g8 < 8; ++g8) {
-                const uint4 w = *reinterpret_cast<const uint4 *>(Qt + half * 16384 + sw128_off(r, g8));
-                const uint4 o4 = make_uint4(pack_bf16x2(bf16_lo(w.x) * qs, bf16_hi(w.x) * qs),
-                                            pack_bf16x2(bf16_lo(w.y) * qs, bf16_hi(w.y) * qs),
-                                            pack_bf16x2(bf16_lo(w.z) * qs, bf16_hi(w.z) * qs),
-                                            pack_bf16x2(bf16_lo(w.w) * qs, bf16_hi(w.w) * qs));
-                *reinterpret_cast<uint4 *>(img + kImgQ + half * 8192 + sw128_off(i, g8)) = o4;
+        for (int g8 = 0; g8 < 8; ++g8) {
+            uint4 *p = reinterpret_cast<uint4 *>(Qt + half * 16384 + sw128_off(r, g8));
+            const uint4 w = *p;
+            *p = make_uint4(pack_bf16x2(bf16_lo(w.x) * qs, bf16_hi(w.x) * qs),
+                            pack_bf16x2(bf16_lo(w.y) * qs, bf16_hi(w.y) * qs),
+                            pack_bf16x2(bf16_lo(w.z) * qs, bf16_hi(w.z) * qs),
+                            pack_bf16x2(bf16_lo(w.w) * qs, bf16_hi(w.w) * qs));
+        }
+        if (i == 63 && half == 0 && chunk0 + c < nc) a.gC[(size_t)h * nc + chunk0 + c] = gam[r];
+    }
+    fence_proxy_async_shared();
+    if (__syncthreads_or(!ok)) ok = false;
+    uint8_t *img0 = a.img + ((size_t)h * nc + chunk0) * kImgBytes;
+    if (tid == kStoreThread && ok) {
+        for (int cc = 0; cc < n_valid; ++cc) {
+            uint8_t *img = img0 + (size_t)cc * kImgBytes;
+            bulk_s2g(img + kImgP, Ps + cc * 8192, 8192);
+            bulk_s2g(img + kImgQ, Qt + cc * 8192, 8192);
+            bulk_s2g(img + kImgQ + 8192, Qt + 16384 + cc * 8192, 8192);
+        }
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+    // 4. T = (I + A)^-1 of each chunk, one column per thread (warps 0-3);
+    // warps 4-7 zero the off-diagonal blocks of the two bf16 copies of T
+    if (ok) {
+        if (warp < 4) {
+            const int cc = warp >> 1, j = 32 * (warp & 1) + lane, rr = cc * 64 + j;
+            const float fk = bet[rr] * gam[rr], fv = bet[rr];
+            uint8_t *tk = Tk + cc * 16384, *tv = Tv + cc * 16384;
+            if (warp & 1)
+                solve_column<32>(Af + cc * 64 * kAS, j, fk, fv, tk, tv, cc * 64);
+            else
+                solve_column<0>(Af + cc * 64 * kAS, j, fk, fv, tk, tv, cc * 64);
+        } else {
+            // rows of chunk cc, columns of the other chunk: tile (1 - cc), rows 64 cc ..
+            for (int e = tid - 128; e < 2 * 2 * 512; e += 128) {
+                const int which = e >> 10, cc = (e >> 9) & 1, g = e & 511;
+                uint8_t *t = (which ? Tv : Tk) + (1 - cc) * 16384 + cc * 8192;
+                reinterpret_cast<uint4 *>(t)[g] = make_uint4(0, 0, 0, 0);
             }
-            if (i == 63 && half == 0) a.gC[(size_t)h * a.n_chunks + chunk] = gam[r];
         }
-    }
-    __syncthreads();   // Qt consumed: Tf may overwrite it
-    // 5. T = (I + A)^-1 per chunk, blocked by 16
-    for (int e = tid; e < 2 * 64 * 64; e += 256) Tf[e] = 0.f;
-    __syncthreads();
-    if (tid < 128) {
-        const int c = tid >> 6, blk = (tid >> 4) & 3, col = tid & 15;
-        const float *Ab = Af + (c * 64 + blk * 16) * kAS + blk * 16;
-        float x[16];
-#pragma unroll
-        for (int ii = 0; ii < 16; ++ii) {
-            float s = ii == col ? 1.f : 0.f;
-#pragma unroll
-            for (int kk2 = 0; kk2 < ii; ++kk2) s = fmaf(-Ab[ii * kAS + kk2], x[kk2], s);
-            x[ii] = s;
-        }
-        float *Tb = Tf + (c * 64 + blk * 16) * 64 + blk * 16;
-#pragma unroll
-        for (int ii = 0; ii < 16; ++ii) Tb[ii * 64 + col] = x[ii];
-    }
-    __syncthreads();
-    for (int dd = 1; dd < 4; ++dd) {
-        const int nb = 2 * (4 - dd);   // blocks (c, I, J = I - dd)
-        for (int q = tid; q < nb * 256; q += 256) {
-            const int bi = q >> 8, e2 = q & 255, ar = e2 >> 4, bc = e2 & 15;
-            const int c = bi / (4 - dd), I = dd + bi % (4 - dd), J = I - dd;
-            float s = 0.f;
-            for (int K = J; K < I; ++K)
-#pragma unroll
-                for (int kk2 = 0; kk2 < 16; ++kk2)
-                    s = fmaf(Af[(c * 64 + I * 16 + ar) * kAS + K * 16 + kk2], Tf[(c * 64 + K * 16 + kk2) * 64 + J * 16 + bc], s);
-            Mt[bi * 256 + e2] = s;
-        }
-        __syncthreads();
-        for (int q = tid; q < nb * 256; q += 256) {
-            const int bi = q >> 8, e2 = q & 255, ar = e2 >> 4, bc = e2 & 15;
-            const int c = bi / (4 - dd), I = dd + bi % (4 - dd), J = I - dd;
-            float s = 0.f;
-#pragma unroll
-            for (int kk2 = 0; kk2 < 16; ++kk2)
-                s = fmaf(Tf[(c * 64 + I * 16 + ar) * 64 + I * 16 + kk2], Mt[bi * 256 + kk2 * 16 + bc], s);
-            Tf[(c * 64 + I * 16 + ar) * 64 + J * 16 + bc] = -s;
-        }
-        __syncthreads();
-    }
-    // block-diagonal T over the pair -> bf16 tiles [128 i][128 j]
-    for (int e = tid; e < 128 * 16; e += 256) {
-        const int r = e >> 4, gi = e & 15, c = r >> 6, i = r & 63;
-        uint4 w = make_uint4(0, 0, 0, 0);
-        if ((gi >> 3) == c) {
-            const float *tr = Tf + (c * 64 + i) * 64 + (gi & 7) * 8;
-            w = make_uint4(pack_bf16x2(tr[0], tr[1]), pack_bf16x2(tr[2], tr[3]), pack_bf16x2(tr[4], tr[5]),
-                           pack_bf16x2(tr[6], tr[7]));
-        }
-        *reinterpret_cast<uint4 *>(Tt + (gi >> 3) * 16384 + sw128_off(r, gi & 7)) = w;
     }
     fence_proxy_async_shared();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    // 6. W = T (beta gamma K) -> cols [256,384), U = T (beta V) -> cols [384,512)
+    // 5. W = (T diag(beta gamma)) K -> cols [256,384), U = (T diag(beta)) V -> cols [384,512);
+    // K and V rows are the MN-major B operands (N = d in two 64-wide blocks 16 KB apart)
     if (tid == 0 && ok) {
-        for (int kb = 0; kb < 2; ++kb) {
-            const uint64_t dt = sw128_desc(smem_addr(Tt + kb * 16384));
-            const uint64_t dkb = sw128_desc(smem_addr(Kb + kb * 16384)), dvb = sw128_desc(smem_addr(Vb + kb * 16384));
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                umma_f16(tmem + 256, dt + 2 * j, dkb + 2 * j, idesc, (kb | j) ? 1u : 0u);
-                umma_f16(tmem + 384, dt + 2 * j, dvb + 2 * j, idesc, (kb | j) ? 1u : 0u);
-            }
+        const uint32_t idmn = idesc | kIdescBMajorMN;
+        for (int ks = 0; ks < 8; ++ks) {
+            const uint64_t dtk = sw128_desc(smem_addr(Tk + (ks >> 2) * 16384)) + 2 * (ks & 3);
+            const uint64_t dtv = sw128_desc(smem_addr(Tv + (ks >> 2) * 16384)) + 2 * (ks & 3);
+            const uint64_t dk = sw128_mn_desc(smem_addr(Kt + ks * 2048), 16384);
+            const uint64_t dv = sw128_mn_desc(smem_addr(Vt + ks * 2048), 16384);
+            umma_f16(tmem + 256, dtk, dk, idmn, ks ? 1u : 0u);
+            umma_f16(tmem + 384, dtv, dv, idmn, ks ? 1u : 0u);
         }
-        umma_commit(&bar[1]);
+        umma_commit(&bar[2]);
     }
-    if (ok) ok = mbar_wait(&bar[1], 0);
+    if (ok) ok = mbar_wait(&bar[2], 0);
     tc_fence_after();
-    // 7. W rows (bf16 tiles) and U rows (fp32) to the workspace
-    if (ok && tid < 128) {
-        const int r = tid, c = r >> 6, i = r & 63, chunk = chunk0 + c;
-        if (chunk < a.n_chunks) {
-            const uint32_t lane_addr = tmem + ((uint32_t)(32 * warp) << 16);
-            uint8_t *img = a.img + ((size_t)h * a.n_chunks + chunk) * kImgBytes;
-            uint4 *Ur = reinterpret_cast<uint4 *>(img + kImgU + i * 256);
-            for (int cb = 0; cb < 4; ++cb) {
-                uint32_t w[32], u[32];
-                tmem_ld32_nowait(lane_addr + 256 + cb * 32, w);
-                tmem_ld32_nowait(lane_addr + 384 + cb * 32, u);
-                tmem_wait_ld();
+    // 6. W rows (warps 0-3) and U rows (warps 4-7) from TMEM to their image
+    // layouts; K rows scaled by gamma_C/gamma_t in place (the K^T diag image,
+    // MN-major), d-half by warp group
+    if (ok) {
+        const uint32_t col = half ? 384 : 256;
+        for (int cb = 0; cb < 4; ++cb) {
+            uint32_t w[32];
+            tmem_ld32_nowait(lane_addr + col + cb * 32, w);
+            tmem_wait_ld();
+            if (half == 0) {
+                st_bf16_granules(Ws, r, cb * 32, w);
+            } else {
 #pragma unroll
-                for (int gg = 0; gg < 4; ++gg) {
-                    const int d0 = cb * 32 + gg * 8;
-                    *reinterpret_cast<uint4 *>(img + kImgW + (d0 >> 6) * 8192 + sw128_off(i, (d0 & 63) >> 3)) =
+                for (int gg = 0; gg < 4; ++gg)
+                    *reinterpret_cast<uint4 *>(Us + u_off(r, cb * 32 + gg * 8)) =
                         make_uint4(pack_bf16x2(__uint_as_float(w[8 * gg]), __uint_as_float(w[8 * gg + 1])),
                                    pack_bf16x2(__uint_as_float(w[8 * gg + 2]), __uint_as_float(w[8 * gg + 3])),
                                    pack_bf16x2(__uint_as_float(w[8 * gg + 4]), __uint_as_float(w[8 * gg + 5])),
                                    pack_bf16x2(__uint_as_float(w[8 * gg + 6]), __uint_as_float(w[8 * gg + 7])));
-                    Ur[cb * 4 + gg] =
-                        make_uint4(pack_bf16x2(__uint_as_float(u[8 * gg]), __uint_as_float(u[8 * gg + 1])),
-                                   pack_bf16x2(__uint_as_float(u[8 * gg + 2]), __uint_as_float(u[8 * gg + 3])),
-                                   pack_bf16x2(__uint_as_float(u[8 * gg + 4]), __uint_as_float(u[8 * gg + 5])),
-                                   pack_bf16x2(__uint_as_float(u[8 * gg + 6]), __uint_as_float(u[8 * gg + 7])));
-                }
             }
         }
+        const float kd = fkd[r];
+#pragma unroll
+        for (int g8 = 0; g8 < 8; ++g8) {
+            uint4 *p = reinterpret_cast<uint4 *>(Kt + half * 16384 + sw128_off(r, (g8 + r) & 7));
+            const uint4 w = *p;
+            *p = make_uint4(pack_bf16x2(bf16_lo(w.x) * kd, bf16_hi(w.x) * kd),
+                            pack_bf16x2(bf16_lo(w.y) * kd, bf16_hi(w.y) * kd),
+                            pack_bf16x2(bf16_lo(w.z) * kd, bf16_hi(w.z) * kd),
+                            pack_bf16x2(bf16_lo(w.w) * kd, bf16_hi(w.w) * kd));
+        }
+    }
+    fence_proxy_async_shared();
+    tc_fence_before();
+    if (__syncthreads_or(!ok)) ok = false;
+    if (tid == kStoreThread) {
+        if (ok) {
+            for (int cc = 0; cc < n_valid; ++cc) {
+                uint8_t *img = img0 + (size_t)cc * kImgBytes;
+                bulk_s2g(img + kImgW, Ws + cc * 8192, 8192);
+                bulk_s2g(img + kImgW + 8192, Ws + 16384 + cc * 8192, 8192);
+                bulk_s2g(img + kImgKd, Kt + cc * 8192, 8192);
+                bulk_s2g(img + kImgKd + 8192, Kt + 16384 + cc * 8192, 8192);
+                bulk_s2g(img + kImgU, Us + cc * 16384, 16384);
+            }
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+        asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
     if (!ok && tid == 0) {
-        // the MMAs may still run: wait (bounded) before the TMEM is freed
+        // a wait gave up: let the copies and MMAs in flight finish (bounded) before the TMEM is freed
         mbar_wait(&bar[0], 0);
         mbar_wait(&bar[1], 0);
+        mbar_wait(&bar[2], 0);
     }
-    tc_fence_before();
     __syncthreads();
-    if (warp == 0) {
+    if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, 512);
     }
@@ -365,19 +406,6 @@ __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a) {
 constexpr uint32_t kStRing = 0, kStS = 2 * kImgBytes, kStDt = kStS + 32768, kStO = kStDt + 16384,
                    kStMisc = kStO + 32768;
 constexpr size_t kStateSmem = kStMisc + 64 + 1024;
-
-__device__ __forceinline__ void st_bf16_granules(uint8_t *tile_base, int row, int k0, const uint32_t (&r)[32]) {
-    // 32 values of `row` (columns k0 .. k0+31, k0 a multiple of 32) into [rows][64] tiles by 64 columns
-#pragma unroll
-    for (int gg = 0; gg < 4; ++gg) {
-        const int k = k0 + gg * 8;
-        *reinterpret_cast<uint4 *>(tile_base + (k >> 6) * 16384 + sw128_off(row, (k & 63) >> 3)) =
-            make_uint4(pack_bf16x2(__uint_as_float(r[8 * gg]), __uint_as_float(r[8 * gg + 1])),
-                       pack_bf16x2(__uint_as_float(r[8 * gg + 2]), __uint_as_float(r[8 * gg + 3])),
-                       pack_bf16x2(__uint_as_float(r[8 * gg + 4]), __uint_as_float(r[8 * gg + 5])),
-                       pack_bf16x2(__uint_as_float(r[8 * gg + 6]), __uint_as_float(r[8 * gg + 7])));
-    }
-}
 
 // TMA store of a [64 t][128 v] fp32 tile to o rows (t, h) (tokens past T are clipped)
 __device__ __forceinline__ void tma_store_o(const CUtensorMap *m, const void *src, int h, int t0) {
@@ -486,9 +514,9 @@ __global__ void __launch_bounds__(288, 1) gdr_state_kernel(PrefillArgs a, const 
             if (n > 0) stage_o(n - 1);
             float u[32];
             {
-                const __nv_bfloat16 *Ub = reinterpret_cast<const __nv_bfloat16 *>(img + kImgU);
 #pragma unroll
-                for (int t = 0; t < 32; ++t) u[t] = __bfloat162float(Ub[(half * 32 + t) * kD + v]);
+                for (int t = 0; t < 32; ++t)
+                    u[t] = __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(img + kImgU + u_off(half * 32 + t, v)));
             }
             for (int cb = 0; cb < 2; ++cb) {
                 const uint32_t col = half * 64 + cb * 32;
@@ -524,11 +552,14 @@ __global__ void __launch_bounds__(288, 1) gdr_state_kernel(PrefillArgs a, const 
             // O^T += Delta^T P^T; S^T += Delta^T (diag(gamma_C/gamma) K); one commit covers
             // every MMA of the chunk (the image slot and Delta are free when it arrives)
             const uint64_t dd = sw128_desc(smem_addr(Dt));
-            const uint64_t dp = sw128_desc(smem_addr(img + kImgP)), dk = sw128_desc(smem_addr(img + kImgKd));
+            const uint64_t dp = sw128_desc(smem_addr(img + kImgP));
 #pragma unroll
             for (int j = 0; j < 4; ++j) umma_f16(tmem + d2col, dd + 2 * j, dp + 2 * j, id64, 1u);
+            // B = diag(gamma_C/gamma) K rows, MN-major (two 64-wide k blocks 8 KB apart)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) umma_f16(tmem + 0, dd + 2 * j, dk + 2 * j, id128, 1u);
+            for (int j = 0; j < 4; ++j)
+                umma_f16(tmem + 0, dd + 2 * j, sw128_mn_desc(smem_addr(img + kImgKd + j * 2048), 8192),
+                         id128 | kIdescBMajorMN, 1u);
             umma_commit(mbar);
             if (n > 0) tma_store_o(&tmO, Os, h, (n - 1) * kC);   // the previous chunk's outputs
         }
@@ -592,8 +623,7 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t
                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-// o [T][Hv][128] fp32 as a 3-D tensor (v, head, token) for [64 t][128 v] box stores
-int encode_o_map(CUtensorMap *m, float *o, int T, int Hv) {
+EncodeTiledFn encoder() {
     static EncodeTiledFn fn = nullptr;
     static std::once_flag once;
     std::call_once(once, [] {
@@ -603,13 +633,23 @@ int encode_o_map(CUtensorMap *m, float *o, int T, int Hv) {
             q == cudaDriverEntryPointSuccess)
             fn = reinterpret_cast<EncodeTiledFn>(p);
     });
+    return fn;
+}
+
+// [T][H][128] rows as a 3-D tensor (d, head, token) with a [tokens][1][128 or 64 d] box
+int encode_rows(CUtensorMap *m, void *base, bool bf16, int T, int H, int box_d, int box_t) {
+    EncodeTiledFn fn = encoder();
     if (!fn) return LI_ERR_UNSUPPORTED;
-    const cuuint64_t dims[3] = {(cuuint64_t)kD, (cuuint64_t)Hv, (cuuint64_t)T};
-    const cuuint64_t strides[2] = {(cuuint64_t)kD * 4, (cuuint64_t)Hv * kD * 4};
-    const cuuint32_t box[3] = {(cuuint32_t)kD, 1, (cuuint32_t)kC};
+    const cuuint64_t es = bf16 ? 2 : 4;
+    const cuuint64_t dims[3] = {(cuuint64_t)kD, (cuuint64_t)H, (cuuint64_t)T};
+    const cuuint64_t strides[2] = {(cuuint64_t)kD * es, (cuuint64_t)H * kD * es};
+    const cuuint32_t box[3] = {(cuuint32_t)box_d, 1, (cuuint32_t)box_t};
     const cuuint32_t estr[3] = {1, 1, 1};
-    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, o, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                          CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims,
+                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          bf16 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                          bf16 ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B : CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? 0 : LI_ERR_BAD_SHAPE;
 }
 
@@ -660,9 +700,14 @@ int li_launch_deltanet_chunk_prefill_bf16(const void *q, const void *k, const vo
     a.gC = (float *)((uint8_t *)workspace + (size_t)n_v_heads * a.n_chunks * kImgBytes);
     if (!aligned16(o)) return LI_ERR_MISALIGNED;
     CUtensorMap tmO;
-    if ((rc0 = encode_o_map(&tmO, o, T, n_v_heads))) return rc0;
+    PrepMaps maps;
+    if ((rc0 = encode_rows(&tmO, o, false, T, n_v_heads, kD, kC)) ||
+        (rc0 = encode_rows(&maps.k, const_cast<void *>(k), true, T, n_k_heads, 64, 2 * kC)) ||
+        (rc0 = encode_rows(&maps.q, const_cast<void *>(q), true, T, n_k_heads, 64, 2 * kC)) ||
+        (rc0 = encode_rows(&maps.v, const_cast<void *>(v), true, T, n_v_heads, 64, 2 * kC)))
+        return rc0;
     const cudaStream_t s = (cudaStream_t)stream;
-    gdr_prep_kernel<<<dim3((unsigned)((a.n_chunks + 1) / 2), (unsigned)n_v_heads), 256, kPrepSmem, s>>>(a);
+    gdr_prep_kernel<<<dim3((unsigned)((a.n_chunks + 1) / 2), (unsigned)n_v_heads), 256, kPrepSmem, s>>>(a, maps);
     int rc = launch_status();
     if (rc) return rc;
     gdr_state_kernel<<<(unsigned)n_v_heads, 288, kStateSmem, s>>>(a, tmO);

@@ -109,6 +109,19 @@ __host__ __device__ __forceinline__ uint32_t sw128_off(int m, int g) {
     return (uint32_t)((m >> 3) * 1024 + (m & 7) * 128 + ((g ^ (m & 7)) << 4));
 }
 
+// Shared-memory matrix descriptor: MN-major, 128-byte swizzle. The matrix is
+// stored as K-rows of 64 MN-contiguous 16-bit elements (128 B, swizzled like
+// the K-major tile: an [k][64] tile with sw128_off(k, mn / 8)); 8 K-rows form
+// a 1024-byte group and consecutive groups are contiguous (SBO = 1024); the
+// next 64-wide MN block starts `lbo` bytes further. One 16-deep K step of the
+// same operand starts 2048 bytes later. The MMA selects this layout for B
+// with kIdescBMajorMN.
+__device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t saddr, uint32_t lbo) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+constexpr uint32_t kIdescBMajorMN = 1u << 16;
+
 // Instruction descriptor, kind::f16: fp32 accumulate, A and B K-major, both
 // f16 (bf16 = false) or both bf16 (bf16 = true), M x N.
 __host__ __device__ constexpr uint32_t idesc_kf16(int m, int n, bool bf16) {
