@@ -90,7 +90,7 @@ constexpr uint32_t kPrepKt = 0, kPrepQt = 32768, kPrepVt = 65536, kPrepTk = 9830
                    kPrepPs = 163840, kPrepAf = 180224;
 constexpr int kAS = 68;   // row stride of the fp32 A matrix (16-byte rows; float4 row writes are conflict-free)
 constexpr uint32_t kPrepMisc = kPrepAf + 2 * 64 * kAS * 4;
-constexpr size_t kPrepSmem = kPrepMisc + 4096 + 1024;
+constexpr size_t kPrepSmem = kPrepMisc + 8192 + 1024;
 
 __device__ __forceinline__ void st_bf16_granules(uint8_t *tile_base, int row, int k0, const uint32_t (&r)[32]) {
     // 32 values of `row` (columns k0 .. k0+31, k0 a multiple of 32) into [rows][64] tiles by 64 columns
@@ -114,55 +114,59 @@ __device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *m
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_addr(smem_dst)), "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ void bulk_s2g(void *gdst, const void *ssrc, uint32_t bytes) {
     asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
                  ::"l"(gdst), "r"(smem_addr(ssrc)), "r"(bytes) : "memory");
 }
 
-// Column j of T = (I + A)^-1 for one chunk by forward substitution, in
-// registers: x_i = [i == j] - sum_{k<i} A[i][k] x_k. Rows below SB and columns
-// k < SB are skipped (every column this is called for has j >= SB, so those x
-// are zero). A rows are zero from the diagonal on, so the float4 steps past
-// k = i - 1 add zeros. Writes T[i][j] beta_j gamma_j and T[i][j] beta_j.
-template <int SB>
-__device__ __forceinline__ void solve_column(const float *Ac, int j, float fk, float fv, uint8_t *tk, uint8_t *tv,
-                                             int row0) {
-    float x[64];
+__device__ __forceinline__ void fma4(float4 &acc, float x, const float4 &y) {
+    acc.x = fmaf(x, y.x, acc.x);
+    acc.y = fmaf(x, y.y, acc.y);
+    acc.z = fmaf(x, y.z, acc.z);
+    acc.w = fmaf(x, y.w, acc.w);
+}
+__device__ __forceinline__ float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+__device__ __forceinline__ float f4get(const float4 &v, int e) { return e == 0 ? v.x : e == 1 ? v.y : e == 2 ? v.z : v.w; }
+
+// acc[0..n4) += sum_{k in [k0, k1)} X[k] * Y[k][4 e ..], k0 and k1 multiples of 4;
+// X a row (16-byte aligned), Y rows `ys` floats apart (16-byte aligned)
+template <int N4>
+__device__ __forceinline__ void row_times_rows(float4 (&acc)[N4], const float *X, const float *Y, int ys, int k0,
+                                               int k1) {
+#pragma unroll 1
+    for (int k = k0; k < k1; k += 4) {
+        const float4 x4 = ld4(X + k);
 #pragma unroll
-    for (int i = 0; i < 64; ++i) x[i] = 0.f;
+        for (int kk = 0; kk < 4; ++kk) {
+            const float xv = f4get(x4, kk);
 #pragma unroll
-    for (int i = SB; i < 64; ++i) {
-        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll
-        for (int k = SB; k < i; k += 4) {
-            const float4 a4 = *reinterpret_cast<const float4 *>(Ac + i * kAS + k);
-            s0 = fmaf(a4.x, x[k], s0);
-            s1 = fmaf(a4.y, x[k + 1], s1);
-            s2 = fmaf(a4.z, x[k + 2], s2);
-            s3 = fmaf(a4.w, x[k + 3], s3);
-        }
-        const float t = -((s0 + s1) + (s2 + s3));
-        x[i] = i < j ? 0.f : (i == j ? 1.f : t);
-    }
-    const uint32_t cb = (uint32_t)(j & 7) * 2;
-#pragma unroll
-    for (int i = SB; i < 64; ++i) {
-        const uint32_t off = sw128_off(row0 + i, j >> 3) + cb;
-        *reinterpret_cast<__nv_bfloat16 *>(tk + off) = __float2bfloat16_rn(x[i] * fk);
-        *reinterpret_cast<__nv_bfloat16 *>(tv + off) = __float2bfloat16_rn(x[i] * fv);
-    }
-    if (SB > 0) {
-#pragma unroll
-        for (int i = 0; i < SB; ++i) {
-            const uint32_t off = sw128_off(row0 + i, j >> 3) + cb;
-            *reinterpret_cast<__nv_bfloat16 *>(tk + off) = __float2bfloat16_rn(0.f);
-            *reinterpret_cast<__nv_bfloat16 *>(tv + off) = __float2bfloat16_rn(0.f);
+            for (int e = 0; e < N4; ++e) fma4(acc[e], xv, ld4(Y + (k + kk) * ys + 4 * e));
         }
     }
 }
 
+// 4 consecutive columns (j0 % 4 == 0) of row i of the bf16 copies of T: T x fk -> tk, T x fv -> tv
+__device__ __forceinline__ void put_t4(uint8_t *tk, uint8_t *tv, int i, int j0, float4 t, const float *fk,
+                                       const float *fv) {
+    const uint32_t off = sw128_off(i, j0 >> 3) + (uint32_t)(j0 & 7) * 2;
+    *reinterpret_cast<uint2 *>(tk + off) =
+        make_uint2(pack_bf16x2(t.x * fk[j0], t.y * fk[j0 + 1]), pack_bf16x2(t.z * fk[j0 + 2], t.w * fk[j0 + 3]));
+    *reinterpret_cast<uint2 *>(tv + off) =
+        make_uint2(pack_bf16x2(t.x * fv[j0], t.y * fv[j0 + 1]), pack_bf16x2(t.z * fv[j0 + 2], t.w * fv[j0 + 3]));
+}
+
 struct PrepMaps {
     CUtensorMap k, q, v;   // [T][H][128] bf16 as (d, head, token), box [128 t][64 d], 128B swizzle
+    CUtensorMap g, beta;   // [T][Hv] fp32 as (head, token), box [128 t][4 heads]
+    int gb_tma;            // g and beta by TMA (Hv % 4 == 0), else plain loads
 };
 
 __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a, const __grid_constant__ PrepMaps maps) {
@@ -170,12 +174,15 @@ __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a, const _
     uint8_t *sm = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     uint8_t *Kt = sm + kPrepKt, *Qt = sm + kPrepQt, *Vt = sm + kPrepVt, *Tk = sm + kPrepTk, *Tv = sm + kPrepTv;
     uint8_t *Ps = sm + kPrepPs;                              // P image tiles of both chunks
+    float *Tf = reinterpret_cast<float *>(Qt);               // [2][64][64] fp32 T, once the Q image has left
+    float *Mb = reinterpret_cast<float *>(Ps), *Mc = Mb + 1024;   // block-merge temporaries, once P has left
     uint8_t *Ws = Vt, *Us = Tk;                              // W, U staging once V, T are consumed
     float *Af = reinterpret_cast<float *>(sm + kPrepAf);    // [2][64][kAS] strictly lower A
-    float *gc = reinterpret_cast<float *>(sm + kPrepMisc);  // [128] log gamma
-    float *gam = gc + 128, *bet = gam + 128, *fkd = bet + 128, *wsum = fkd + 128;   // wsum [8]
-    uint64_t *bar = reinterpret_cast<uint64_t *>(wsum + 8);   // [3]: loads, K K^T + Q K^T, W + U
-    uint32_t *holder = reinterpret_cast<uint32_t *>(bar + 3);
+    float *gbox = reinterpret_cast<float *>(sm + kPrepMisc), *bbox = gbox + 512;   // [128 t][4 heads] g, beta (TMA)
+    float *gc = bbox + 512;                                   // [128] log gamma
+    float *gam = gc + 128, *bet = gam + 128, *fkd = bet + 128, *fbg = fkd + 128, *wsum = fbg + 128;   // wsum [8]
+    uint64_t *bar = reinterpret_cast<uint64_t *>(wsum + 8);   // [4]: rows, K K^T + Q K^T, W + U, g + beta
+    uint32_t *holder = reinterpret_cast<uint32_t *>(bar + 4);
 
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
     const int h = blockIdx.y, pair = blockIdx.x;
@@ -187,8 +194,13 @@ __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a, const _
     constexpr int kStoreThread = 128;                // issues every bulk store of the CTA
 
     if (tid == 0) {
-        for (int b = 0; b < 3; ++b) mbar_init(&bar[b], 1);
+        for (int b = 0; b < 4; ++b) mbar_init(&bar[b], 1);
         fence_mbar_init();
+        if (maps.gb_tma) {
+            mbar_arrive_expect_tx(&bar[3], 2 * 2048);
+            tma_load_2d(gbox, &maps.g, h & ~3, t0, &bar[3]);
+            tma_load_2d(bbox, &maps.beta, h & ~3, t0, &bar[3]);
+        }
         mbar_arrive_expect_tx(&bar[0], 6 * 16384);
         for (int hh = 0; hh < 2; ++hh) {
             tma_load_3d(Kt + hh * 16384, &maps.k, hh * 64, hk, t0, &bar[0]);
@@ -197,13 +209,21 @@ __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a, const _
         }
     }
     if (warp == 1) tmem_alloc(holder, 512);
+    __syncthreads();   // the barriers are initialised before anyone waits on them
 
     // 1. decay prefix sums (per 64-token chunk), beta
+    const bool gb_ok = !maps.gb_tma || mbar_wait(&bar[3], 0);
     if (tid < 128) {
         const int t = t0 + tid;
         const bool ok = t < a.T;
-        float gv = ok ? a.g[(size_t)t * a.Hv + h] : 0.f;
-        bet[tid] = ok ? a.beta[(size_t)t * a.Hv + h] : 0.f;
+        float gv;
+        if (maps.gb_tma) {
+            gv = gbox[tid * 4 + (h & 3)];
+            bet[tid] = bbox[tid * 4 + (h & 3)];
+        } else {
+            gv = ok ? a.g[(size_t)t * a.Hv + h] : 0.f;
+            bet[tid] = ok ? a.beta[(size_t)t * a.Hv + h] : 0.f;
+        }
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const float y = __shfl_up_sync(0xffffffffu, gv, o);
@@ -217,14 +237,17 @@ __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a, const _
         if (warp & 1) gc[tid] += wsum[warp - 1];   // second warp of each chunk
         gam[tid] = expf(gc[tid]);
         fkd[tid] = expf(gc[(tid & 64) + 63] - gc[tid]);   // gamma_C / gamma_t
+        fbg[tid] = bet[tid] * gam[tid];
     }
+    // both bf16 copies of T start as zeros (only the lower blocks get written)
+    for (int e = tid; e < 4096; e += 256) reinterpret_cast<uint4 *>(Tk)[e] = make_uint4(0, 0, 0, 0);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *holder;
     const uint32_t idesc = idesc_kf16(128, 128, true);
     // 2. K K^T -> cols [0,128), Q K^T -> cols [128,256)
-    bool ok = mbar_wait(&bar[0], 0);
+    bool ok = mbar_wait(&bar[0], 0) && gb_ok;
     if (tid == 0 && ok) {
         tc_fence_after();
         for (int kb = 0; kb < 2; ++kb) {
@@ -295,23 +318,81 @@ __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a, const _
         }
         asm volatile("cp.async.bulk.commit_group;" ::: "memory");
     }
-    // 4. T = (I + A)^-1 of each chunk, one column per thread (warps 0-3);
-    // warps 4-7 zero the off-diagonal blocks of the two bf16 copies of T
+    // 4. T = (I + A)^-1 of each chunk, by blocks: the four 16x16 diagonal
+    // blocks by forward substitution (one column per thread), then the 32-wide
+    // diagonal blocks T_10 = -T_11 (A_10 T_00), then the 64-wide one the same
+    // way. fp32 T goes to Tf (over the Q tiles, once their image copy has been
+    // read); each finished block also goes to the two bf16 copies.
+    float x[16];
+    if (tid < 128) {
+        const int b = tid >> 4, c = b >> 2, I = b & 3, jj = tid & 15;
+        const float *Ab = Af + (c * 64 + 16 * I) * kAS + 16 * I;
+#pragma unroll
+        for (int ii = 0; ii < 16; ++ii) x[ii] = 0.f;
+#pragma unroll
+        for (int ii = 0; ii < 16; ++ii) {
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int kk = 0; kk < ii; kk += 4) {
+                const float4 a4 = ld4(Ab + ii * kAS + kk);   // zeros from the diagonal on
+                s0 = fmaf(a4.x, x[kk], s0);
+                s1 = fmaf(a4.y, x[kk + 1], s1);
+                s0 = fmaf(a4.z, x[kk + 2], s0);
+                s1 = fmaf(a4.w, x[kk + 3], s1);
+            }
+            x[ii] = ii < jj ? 0.f : (ii == jj ? 1.f : -(s0 + s1));
+        }
+    }
+    if (tid == kStoreThread) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    __syncthreads();   // the Q and P tiles have been read: Tf and the temporaries may overwrite them
     if (ok) {
-        if (warp < 4) {
-            const int cc = warp >> 1, j = 32 * (warp & 1) + lane, rr = cc * 64 + j;
-            const float fk = bet[rr] * gam[rr], fv = bet[rr];
-            uint8_t *tk = Tk + cc * 16384, *tv = Tv + cc * 16384;
-            if (warp & 1)
-                solve_column<32>(Af + cc * 64 * kAS, j, fk, fv, tk, tv, cc * 64);
-            else
-                solve_column<0>(Af + cc * 64 * kAS, j, fk, fv, tk, tv, cc * 64);
-        } else {
-            // rows of chunk cc, columns of the other chunk: tile (1 - cc), rows 64 cc ..
-            for (int e = tid - 128; e < 2 * 2 * 512; e += 128) {
-                const int which = e >> 10, cc = (e >> 9) & 1, g = e & 511;
-                uint8_t *t = (which ? Tv : Tk) + (1 - cc) * 16384 + cc * 8192;
-                reinterpret_cast<uint4 *>(t)[g] = make_uint4(0, 0, 0, 0);
+        if (tid < 128) {
+            const int b = tid >> 4, c = b >> 2, I = b & 3, jj = tid & 15, j = 16 * I + jj;
+            float *tcol = Tf + (c * 64 + 16 * I) * 64 + j;
+            const uint32_t cb = (uint32_t)(j & 7) * 2;
+            const float fk = fbg[64 * c + j], fv = bet[64 * c + j];
+#pragma unroll
+            for (int ii = 0; ii < 16; ++ii) {
+                tcol[ii * 64] = x[ii];
+                const uint32_t off = c * 16384 + sw128_off(64 * c + 16 * I + ii, j >> 3) + cb;
+                *reinterpret_cast<__nv_bfloat16 *>(Tk + off) = __float2bfloat16_rn(x[ii] * fk);
+                *reinterpret_cast<__nv_bfloat16 *>(Tv + off) = __float2bfloat16_rn(x[ii] * fv);
+            }
+        }
+        __syncthreads();
+        // 32-wide: block q = (chunk, pair p): I = 2p + 1, J = 2p; thread: row r, columns c0 .. c0+3
+        {
+            const int q = tid >> 6, c = q >> 1, I = 2 * (q & 1) + 1, J = I - 1;
+            const int r = (tid >> 2) & 15, c0 = (tid & 3) * 4;
+            float4 m[1] = {make_float4(0.f, 0.f, 0.f, 0.f)};
+            row_times_rows<1>(m, Af + (c * 64 + 16 * I + r) * kAS + 16 * J, Tf + (c * 64 + 16 * J) * 64 + 16 * J + c0,
+                              64, 0, 16);
+            *reinterpret_cast<float4 *>(Mb + q * 256 + r * 16 + c0) = m[0];
+            __syncthreads();
+            float4 t[1] = {make_float4(0.f, 0.f, 0.f, 0.f)};
+            row_times_rows<1>(t, Tf + (c * 64 + 16 * I + r) * 64 + 16 * I, Mb + q * 256 + c0, 16, 0, 16);
+            t[0] = make_float4(-t[0].x, -t[0].y, -t[0].z, -t[0].w);
+            *reinterpret_cast<float4 *>(Tf + (c * 64 + 16 * I + r) * 64 + 16 * J + c0) = t[0];
+            put_t4(Tk + c * 16384, Tv + c * 16384, 64 * c + 16 * I + r, 16 * J + c0, t[0], fbg + 64 * c,
+                   bet + 64 * c);
+        }
+        __syncthreads();
+        // 64-wide: T_[23][01] = -T_[23][23] (A_[23][01] T_[01][01]); thread: chunk c, row r, columns c0 .. c0+7
+        {
+            const int c = tid >> 7, r = (tid >> 2) & 31, c0 = (tid & 3) * 8;
+            float4 m[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+            // T_[01][01][k][c0 ..] is zero for k < c0
+            row_times_rows<2>(m, Af + (c * 64 + 32 + r) * kAS, Tf + c * 64 * 64 + c0, 64, c0, 32);
+            *reinterpret_cast<float4 *>(Mc + c * 1024 + r * 32 + c0) = m[0];
+            *reinterpret_cast<float4 *>(Mc + c * 1024 + r * 32 + c0 + 4) = m[1];
+            __syncthreads();
+            float4 t[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+            // T_[23][23][r][k] is zero for k >= 16 when r < 16 (warp-uniform)
+            row_times_rows<2>(t, Tf + (c * 64 + 32 + r) * 64 + 32, Mc + c * 1024 + c0, 32, 0, r < 16 ? 16 : 32);
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                t[e] = make_float4(-t[e].x, -t[e].y, -t[e].z, -t[e].w);
+                put_t4(Tk + c * 16384, Tv + c * 16384, 64 * c + 32 + r, c0 + 4 * e, t[e], fbg + 64 * c, bet + 64 * c);
             }
         }
     }
@@ -387,6 +468,7 @@ __global__ void __launch_bounds__(256, 1) gdr_prep_kernel(PrefillArgs a, const _
     if (!ok && tid == 0) {
         // a wait gave up: let the copies and MMAs in flight finish (bounded) before the TMEM is freed
         mbar_wait(&bar[0], 0);
+        if (maps.gb_tma) mbar_wait(&bar[3], 0);
         mbar_wait(&bar[1], 0);
         mbar_wait(&bar[2], 0);
     }
@@ -653,6 +735,20 @@ int encode_rows(CUtensorMap *m, void *base, bool bf16, int T, int H, int box_d, 
     return r == CUDA_SUCCESS ? 0 : LI_ERR_BAD_SHAPE;
 }
 
+// [T][Hv] fp32 per-head scalars as a 2-D tensor (head, token), box [2 chunks of tokens][4 heads]
+int encode_heads(CUtensorMap *m, float *base, int T, int Hv) {
+    EncodeTiledFn fn = encoder();
+    if (!fn) return LI_ERR_UNSUPPORTED;
+    const cuuint64_t dims[2] = {(cuuint64_t)Hv, (cuuint64_t)T};
+    const cuuint64_t strides[1] = {(cuuint64_t)Hv * 4};
+    const cuuint32_t box[2] = {4, (cuuint32_t)(2 * kC)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : LI_ERR_BAD_SHAPE;
+}
+
 template <typename K>
 int set_smem(K kern, size_t bytes) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
@@ -705,6 +801,11 @@ int li_launch_deltanet_chunk_prefill_bf16(const void *q, const void *k, const vo
         (rc0 = encode_rows(&maps.k, const_cast<void *>(k), true, T, n_k_heads, 64, 2 * kC)) ||
         (rc0 = encode_rows(&maps.q, const_cast<void *>(q), true, T, n_k_heads, 64, 2 * kC)) ||
         (rc0 = encode_rows(&maps.v, const_cast<void *>(v), true, T, n_v_heads, 64, 2 * kC)))
+        return rc0;
+    maps.gb_tma = n_v_heads % 4 == 0 && aligned16(g) && aligned16(beta);
+    if (maps.gb_tma &&
+        ((rc0 = encode_heads(&maps.g, const_cast<float *>(g), T, n_v_heads)) ||
+         (rc0 = encode_heads(&maps.beta, const_cast<float *>(beta), T, n_v_heads))))
         return rc0;
     const cudaStream_t s = (cudaStream_t)stream;
     gdr_prep_kernel<<<dim3((unsigned)((a.n_chunks + 1) / 2), (unsigned)n_v_heads), 256, kPrepSmem, s>>>(a, maps);
