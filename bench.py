@@ -47,6 +47,20 @@ NCU_TRAFFIC = {64: 262_778_000}
 UNIT = "tokens/s"
 
 
+# Batch rows from which the layer's projections run on the tensor cores, and
+# up to which they use the X-stationary kernel (each projection is then a GEMM
+# launch plus a reduce launch).
+TC_MIN_ROWS, TCX_MAX_ROWS = 3, 32
+
+
+def kernels_per_step(batch: int) -> int:
+    if batch < TC_MIN_ROWS:
+        return 3      # in-projection GEMV, recurrence, out-projection GEMV
+    if batch <= TCX_MAX_ROWS:
+        return 6      # x prep, in-projection GEMM + reduce, recurrence, out-projection GEMM + reduce
+    return 4          # x prep, in-projection GEMM, recurrence, out-projection GEMM
+
+
 def algorithmic_bytes(batch: int) -> int:
     """Bytes a step must move at least once: both weight matrices (Q4_K), the
     conv weights, and per sequence the recurrent state and conv state read
@@ -252,7 +266,7 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
                    "parallelism": f"sequence-sharded x{world}, no collectives",
                    "l2": f"inputs larger than L2: rotating {n_inst} layer instances of {per_inst / 1e6:.1f} MB"},
         "roofline": {"bound": "hbm", "kernel": "deltanet layer decode step: " + (
-                         "x prep + tcgen05 in-projection + recurrence + tcgen05 out-projection" if B >= 8 else
+                         "x prep + tcgen05 in-projection + recurrence + tcgen05 out-projection" if B >= TC_MIN_ROWS else
                          "in-projection GEMV + recurrence + out-projection GEMV") + " (PDL-chained)",
                      "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
@@ -260,7 +274,7 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
                      "traffic": args.traffic if args.traffic is not None else NCU_TRAFFIC.get(B)},
         "e2e": {"value": round(world * B * e_steps / (e2e_ms / 1e3), 1), "unit": UNIT,
                 "h2d_bytes_per_step": B * HIDDEN * 4, "d2h_bytes_per_step": B * HIDDEN * 4},
-        "gpu_launches": (4 if B >= 8 else 3) * args.steps,
+        "gpu_launches": kernels_per_step(B) * args.steps,
         "clocks": clocks,
     }
     if not args.no_cpu_baseline:

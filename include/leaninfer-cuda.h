@@ -54,9 +54,10 @@ enum li_wtype {
                                        library's static scratch array holds */
 
 /* Size of the library's own device scratch used by
- * li_launch_deltanet_layer_decode_noalloc (8 MiB: up to 127 sequences of a
- * layer with hidden 4096, 16 k-heads, 32 v-heads, head_dim 128). */
-#define LI_DELTANET_STATIC_SCRATCH_BYTES (8u << 20)
+ * li_launch_deltanet_layer_decode_noalloc (32 MiB: every batch the tensor-core
+ * decode path takes, up to 256 sequences, of a layer with hidden 4096,
+ * 16 k-heads, 32 v-heads, head_dim 128). */
+#define LI_DELTANET_STATIC_SCRATCH_BYTES (32u << 20)
 
 /*
  * Recurrent DeltaNet layer for the fused decode entry. One layer's weights

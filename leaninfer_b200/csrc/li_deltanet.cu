@@ -67,6 +67,7 @@ struct RecArgs {
     float l2_eps, norm_eps;
     float *o_gated;         // [B][Hv*D] fp32, or
     __half *o_gated16;      // [B][Hv*D] f16 (the tensor-core out-projection's operand)
+    int og16_npad;          // > 0: o_gated16 tiled for the X-stationary out-projection
     float *zero_out;        // layer output to clear for a K-split out-projection, or nullptr
     int64_t zero_len;       // floats in zero_out
 };
@@ -260,7 +261,9 @@ recurrent_kernel(RecArgs a) {
                 const float z = a.proj[(size_t)seq * a.NI + a.C + h * D + row0 + r];
                 const float og = silu(z) * (o * a.norm_w[row0 + r] * rs);
                 const size_t oi = ((size_t)seq * a.n_heads + h) * D + row0 + r;
-                if (a.o_gated16) a.o_gated16[oi] = __float2half_rn(og);
+                if (a.o_gated16)
+                    a.o_gated16[a.og16_npad ? tiled_x_offset(seq, h * D + row0 + r, a.og16_npad) : oi] =
+                        __float2half_rn(og);
                 else a.o_gated[oi] = og;
             }
         }
@@ -426,12 +429,24 @@ void li_launch_fused_deltanet_recurrent_out_f32(const float *q, const float *k, 
 //                                       xscale f32 [B] | og16 f16 [B][Hv*D]
 static size_t al256(size_t v) { return (v + 255) / 256 * 256; }
 
+// partial sums of the X-stationary projections (the in- and out-projection
+// run one after the other and share the region)
+static size_t layer_partials_bytes(const li_deltanet_layer *L, int n_seqs) {
+    const int D = L->head_dim, Hk = L->n_k_heads, Hv = L->n_v_heads;
+    const int NI = 2 * Hk * D + 2 * Hv * D + 2 * Hv;
+    const size_t pin = li::tc_gemm_partials_bytes(L->w_in_type, li::kTcConv, L->hidden, NI, n_seqs);
+    const size_t pout = li::tc_gemm_partials_bytes(L->w_out_type, li::kTcStore, Hv * D, L->hidden, n_seqs);
+    return pin > pout ? pin : pout;
+}
+
 size_t li_deltanet_layer_workspace_size(const li_deltanet_layer *L, int n_seqs) {
     if (!L || n_seqs <= 0) return 0;
     const size_t D = L->head_dim, Hk = L->n_k_heads, Hv = L->n_v_heads, n = (size_t)n_seqs;
     const size_t NI = 2 * Hk * D + 2 * Hv * D + 2 * Hv;
     if (n_seqs < li::kTcMinRows) return al256(NI * n * 4) + al256(Hv * D * n * 4);
-    return al256(NI * n * 4) + al256((size_t)L->hidden * n * 2) + al256(n * 4) + al256(Hv * D * n * 2);
+    const size_t nx = (n + 31) / 32 * 32;   // tiled X operands are padded to 32 rows
+    return al256(NI * n * 4) + al256((size_t)L->hidden * nx * 2) + al256(n * 4) + al256(Hv * D * nx * 2) +
+           al256(layer_partials_bytes(L, n_seqs));
 }
 
 int li_launch_deltanet_layer_decode(const li_deltanet_layer *L, const float *x, float *y,
@@ -493,26 +508,34 @@ int li_launch_deltanet_layer_decode(const li_deltanet_layer *L, const float *x, 
 
     // tensor-core path: x -> f16, in-projection GEMM (+conv), recurrence
     // (gated heads written as f16), out-projection GEMM
+    const size_t nx = (n + 31) / 32 * 32;
     size_t off = al256((size_t)NI * n * 4);
     __half *x16 = (__half *)(ws + off);
-    off += al256((size_t)L->hidden * n * 2);
+    off += al256((size_t)L->hidden * nx * 2);
     float *xscale = (float *)(ws + off);
     off += al256(n * 4);
     __half *og16 = (__half *)(ws + off);
-    if ((rc = tc_prep_launch(x, L->hidden, L->in_norm_w, L->in_norm_eps, n_seqs, L->hidden, x16, xscale, s,
-                             false)))
-        return rc;
+    off += al256(Hv * D * nx * 2);
+    float *partials = layer_partials_bytes(L, n_seqs) ? (float *)(ws + off) : nullptr;
     TcArgs in = {};
     in.wtype = L->w_in_type; in.epi = kTcConv; in.K = L->hidden; in.total_rows = NI; in.B = n_seqs;
     in.W[0] = L->w_in; in.n_seg = 1; in.seg_rows[0] = NI; in.dst[0] = proj; in.dst_stride[0] = NI;
     in.X16 = x16; in.xscale = xscale;
     in.conv_w = L->conv_w; in.conv_state = conv_state; in.conv_channels = C;
+    in.partials = partials;
+    in.x_npad = tc_gemm_x_npad(in);
+    if ((rc = tc_prep_launch(x, L->hidden, L->in_norm_w, L->in_norm_eps, n_seqs, L->hidden, x16, xscale, s,
+                             false, in.x_npad)))
+        return rc;
     if ((rc = tc_gemm_launch(in, s, true))) return rc;
     TcArgs out = {};
     out.wtype = L->w_out_type; out.epi = kTcStore; out.K = Hv * D; out.total_rows = L->hidden; out.B = n_seqs;
     out.W[0] = L->w_out; out.n_seg = 1; out.seg_rows[0] = L->hidden; out.dst[0] = y;
     out.dst_stride[0] = L->hidden; out.X16 = og16; out.xscale = nullptr;
+    out.partials = partials;
+    out.x_npad = tc_gemm_x_npad(out);
     a.o_gated16 = og16;
+    a.og16_npad = out.x_npad;
     if (tc_gemm_splits_k(out)) {
         a.zero_out = y;
         a.zero_len = (int64_t)n_seqs * L->hidden;

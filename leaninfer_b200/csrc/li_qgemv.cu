@@ -615,14 +615,26 @@ int li_launch_fused_rms_norm_swiglu_q(int wtype, const float *x, const float *ga
 
 // Workspace regions, 256-byte aligned: h f32 [n_rows][N]; and for
 // n_rows >= kTcMinRows (tensor-core path) also x16 f16 [n_rows][K],
-// xscale [n_rows], h16 f16 [n_rows][N], hscale [n_rows].
+// xscale [n_rows], h16 f16 [n_rows][N], hscale [n_rows], and the partial
+// sums of the X-stationary projections (gate/up, then down, share them).
 static size_t al256(size_t v) { return (v + 255) / 256 * 256; }
+
+static size_t ffn_partials_bytes(int wtype, int K, int N, int n_rows) {
+    const size_t pg = tc_gemm_partials_bytes(wtype, kTcSwiGLU, K, N, n_rows);
+    const size_t pd = tc_gemm_partials_bytes(wtype, kTcStore, N, K, n_rows);
+    return pg > pd ? pg : pd;
+}
 
 size_t li_fused_ffn_workspace_size(int K, int N, int n_rows) {
     if (K <= 0 || N <= 0 || n_rows <= 0) return 0;
     const size_t n = (size_t)n_rows;
     size_t b = al256((size_t)N * n * 4);
-    if (n_rows >= kTcMinRows) b += al256((size_t)K * n * 2) + al256(n * 4) + al256((size_t)N * n * 2) + al256(n * 4);
+    const size_t nx = (n + 31) / 32 * 32;   // tiled X operands are padded to 32 rows
+    if (n_rows >= kTcMinRows)
+        b += al256((size_t)K * nx * 2) + al256(n * 4) + al256((size_t)N * nx * 2) + al256(n * 4) +
+             al256(ffn_partials_bytes(LI_WTYPE_Q4_K, K, N, n_rows) > ffn_partials_bytes(LI_WTYPE_Q8_0, K, N, n_rows)
+                       ? ffn_partials_bytes(LI_WTYPE_Q4_K, K, N, n_rows)
+                       : ffn_partials_bytes(LI_WTYPE_Q8_0, K, N, n_rows));
     return b;
 }
 
@@ -642,27 +654,30 @@ int li_launch_fused_ffn_q(int wtype, const float *x, const float *gamma, const v
     float *h = (float *)ws;
     if (n_rows >= kTcMinRows && n_rows <= 256 && K % 256 == 0 && N % 256 == 0) {
         // tensor-core path: x -> f16, gate/up GEMM + SwiGLU, h -> f16, down GEMM
-        const size_t n = (size_t)n_rows;
+        const size_t n = (size_t)n_rows, nx = (n + 31) / 32 * 32;
         size_t off = al256((size_t)N * n * 4);
-        __half *x16 = (__half *)(ws + off); off += al256((size_t)K * n * 2);
+        __half *x16 = (__half *)(ws + off); off += al256((size_t)K * nx * 2);
         float *xs = (float *)(ws + off);    off += al256(n * 4);
-        __half *h16 = (__half *)(ws + off); off += al256((size_t)N * n * 2);
-        float *hs = (float *)(ws + off);
+        __half *h16 = (__half *)(ws + off); off += al256((size_t)N * nx * 2);
+        float *hs = (float *)(ws + off);    off += al256(n * 4);
+        float *partials = ffn_partials_bytes(wtype, K, N, n_rows) ? (float *)(ws + off) : nullptr;
         TcArgs d = {};
         d.wtype = wtype; d.epi = kTcStore; d.K = N; d.total_rows = K; d.B = n_rows;
         d.W[0] = Wd; d.n_seg = 1; d.seg_rows[0] = K; d.dst[0] = y; d.dst_stride[0] = K;
-        d.X16 = h16; d.xscale = hs;
+        d.X16 = h16; d.xscale = hs; d.partials = partials;
+        d.x_npad = tc_gemm_x_npad(d);
         if (tc_gemm_splits_k(d)) {   // the down projection adds K-split partials into y
             const cudaError_t e = cudaMemsetAsync(y, 0, (size_t)n_rows * K * sizeof(float), s);
             if (e != cudaSuccess) return (int)e;
         }
-        if ((rc = tc_prep_launch(x, K, gamma, eps, n_rows, K, x16, xs, s, false))) return rc;
         TcArgs g = {};
         g.wtype = wtype; g.epi = kTcSwiGLU; g.K = K; g.total_rows = N; g.B = n_rows;
         g.W[0] = Wg; g.W[1] = Wu; g.n_seg = 1; g.seg_rows[0] = N; g.dst[0] = h; g.dst_stride[0] = N;
-        g.X16 = x16; g.xscale = xs;
+        g.X16 = x16; g.xscale = xs; g.partials = partials;
+        g.x_npad = tc_gemm_x_npad(g);
+        if ((rc = tc_prep_launch(x, K, gamma, eps, n_rows, K, x16, xs, s, false, g.x_npad))) return rc;
         if ((rc = tc_gemm_launch(g, s, true))) return rc;
-        if ((rc = tc_prep_launch(h, N, nullptr, 0.f, n_rows, N, h16, hs, s, true))) return rc;
+        if ((rc = tc_prep_launch(h, N, nullptr, 0.f, n_rows, N, h16, hs, s, true, d.x_npad))) return rc;
         return tc_gemm_launch(d, s, true);
     }
     QGemvArgs a = {};

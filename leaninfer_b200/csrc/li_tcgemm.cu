@@ -195,6 +195,7 @@ __device__ __forceinline__ void store_row(uint8_t *a_tile, int m, const uint32_t
 
 // Bounded wait that gives up at once when the CTA has already aborted.
 __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;   // a completed phase needs no abort check
     if (*abort_flag) return false;
     if (!mbar_wait(bar, parity)) {
         *abort_flag = 1;
@@ -484,11 +485,331 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
 }
 
 // ---------------------------------------------------------------------------
+// X-stationary variant (batch up to 64 rows): CTA (chunk c, j) keeps k-chunk c
+// of X resident in shared memory (one bulk copy of up to 128 KB; the producer
+// of X writes it tiled, so a chunk is contiguous) and runs row tiles j,
+// j + cpc, ... of that chunk, so X crosses into the SM once instead of once
+// per tile. Each tile's fp32 partial sum goes to partials[c][w][b][row];
+// tcx_reduce_kernel adds the chunks in order and applies the epilogue.
+// 23 warps:
+//   warps 0-15  dequant, set s = w / 4 takes k-blocks s*SB .. s*SB+SB-1 of
+//               every raw stage (SB 256-value columns = 4*SB k-blocks) into
+//               one A slot in tensor memory (one tile row per thread, its
+//               TMEM lane), so one handover carries SB k-blocks;
+//   warps 16-17 MMA issuers (lane 0): issuer i takes sets 2i and 2i+1 into
+//               its own accumulator per tile, double-buffered across tiles
+//               (one issuing thread keeps the tensor pipe about half busy at
+//               N = 64; two overlap their per-MMA issue work);
+//   warp 18     producer: lane 0 the raw weight stages of the CTA's tiles,
+//               lane 1 the X chunk;
+//   warps 19-22 epilogue: both issuers' accumulators (lane quarter w % 4)
+//               added in issuer order -> partials, while the next tile's
+//               MMAs run into the other buffers.
+// ---------------------------------------------------------------------------
+constexpr int kXSets = 4, kXIssuers = 2;
+constexpr int kXIssuer = 4 * kXSets, kXProducer = kXIssuer + kXIssuers, kXEpi0 = kXProducer + 1;
+constexpr int kXThreads = (kXEpi0 + 4) * kWarp;
+
+struct TcxPlan {
+    int NW, CB, Npad;
+    int nchunk, KC, nkb;        // K chunks, values per chunk, 64-value k-blocks per chunk
+    int tiles, cpc;             // row tiles over all segments, CTAs per chunk
+    int seg_tiles[3], seg_off[3];
+    int rows_total;
+    int SB, RB, RS, spt;        // raw stages: SB 256-value columns each, spt per tile chunk
+    int AG;                     // A slots per set (SB k-blocks each)
+    int tmem_cols;
+    uint32_t x_bytes, off_raw, off_bar;
+    size_t smem;
+};
+
+template <int WT, int EPI, int KI>
+__global__ void __launch_bounds__(kXThreads, 1)
+tcx_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__ CUtensorMap tmW1,
+                const __grid_constant__ CUtensorMap tmW2, TcArgs a, TcxPlan p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    constexpr int NW = EPI == kTcSwiGLU ? 2 : 1;
+    const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+    const int chunk = (int)blockIdx.x / p.cpc, j0 = (int)blockIdx.x % p.cpc;
+    const int n_my = j0 < p.tiles ? (p.tiles - 1 - j0) / p.cpc + 1 : 0;
+
+    uint8_t *x_ring = smem;                // [nkb][Npad][128 B], 128B-swizzled
+    uint8_t *raw_ring = smem + p.off_raw;  // [RS][NW][128 * RB]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + p.off_bar);
+    uint64_t *raw_full = bars, *raw_empty = raw_full + p.RS;
+    uint64_t *a_full = raw_empty + p.RS, *a_empty = a_full + kXSets * p.AG;
+    uint64_t *x_full = a_empty + kXSets * p.AG, *acc_full = x_full + 1, *acc_empty = acc_full + 2;
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(acc_empty + 2);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+    const uint32_t stage_bytes = (uint32_t)(kBM * p.RB);
+    const uint32_t xkb_bytes = (uint32_t)(p.Npad * 128);
+    constexpr int kpr = 4 * KI;                            // k-blocks per raw stage (KI == p.SB per set)
+    const uint32_t acc_cols = (uint32_t)(NW * p.Npad);     // one accumulator
+    // accumulator of issuer i, buffer ab: columns (2*ab + i)*acc_cols; A slot
+    // (set s, i), matrix w, k-block e of the set's share: column
+    // a_col0 + (((s*AG + i)*NW + w)*KI + e)*32
+    const uint32_t a_col0 = 2 * kXIssuers * acc_cols;
+
+    // tile ti of this CTA -> (segment, first row in the segment)
+    auto tile_of = [&](int ti) -> int2 {
+        int t = j0 + ti * p.cpc, seg = 0;
+        if (a.n_seg > 1 && t >= p.seg_tiles[0]) {
+            t -= p.seg_tiles[0];
+            seg = 1;
+            if (a.n_seg > 2 && t >= p.seg_tiles[1]) { t -= p.seg_tiles[1]; seg = 2; }
+        }
+        return make_int2(seg, t * kBM);
+    };
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < p.RS; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 4 * kXSets); }
+        for (int i = 0; i < kXSets * p.AG; ++i) { mbar_init(&a_full[i], 4); mbar_init(&a_empty[i], 1); }
+        mbar_init(x_full, 1);
+        for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], kXIssuers); mbar_init(&acc_empty[i], 4); }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == kXProducer) tmem_alloc(tmem_holder, (uint32_t)p.tmem_cols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+    grid_dep_launch_dependents();
+
+    // Ring positions advance incrementally (no divisions in the loops): a
+    // ring slot's fill parity flips each time the ring wraps; each A slot
+    // keeps its own parity bit.
+    if (warp == kXProducer) {
+        if (lane == 0) {
+            // weight stages (independent of the previous kernel)
+            const int n_st = n_my * p.spt;
+            int issued = 0, rs = 0, ti = 0, r = 0;
+            uint32_t rpar = 0;
+            for (int gs = 0; gs < n_st; ++gs) {
+                if (gs >= p.RS && !wait_or_abort(&raw_empty[rs], rpar ^ 1u, abort_flag)) break;
+                const int2 sr = tile_of(ti);
+                const CUtensorMap *tmA = sr.x == 0 ? &tmW0 : (sr.x == 1 ? &tmW1 : &tmW2);
+                mbar_arrive_expect_tx(&raw_full[rs], (uint32_t)NW * stage_bytes);
+                uint8_t *dst = raw_ring + (size_t)rs * NW * stage_bytes;
+                const int xcol = (chunk * p.spt + r) * (p.RB / 4);
+                tma_load_2d(dst, tmA, xcol, sr.y, &raw_full[rs]);
+                if (NW == 2) tma_load_2d(dst + stage_bytes, &tmW1, xcol, sr.y, &raw_full[rs]);
+                issued = gs + 1;
+                if (++r == p.spt) { r = 0; ++ti; }
+                if (++rs == p.RS) { rs = 0; rpar ^= 1u; }
+            }
+            // drain: every copy issued has landed before the CTA exits
+            for (int gs = issued - p.RS < 0 ? 0 : issued - p.RS; gs < issued; ++gs)
+                mbar_wait(&raw_full[gs % p.RS], (uint32_t)((gs / p.RS) & 1));
+        } else if (lane == 1 && n_my > 0) {
+            grid_dep_wait();   // X is written by the previous kernel
+            mbar_arrive_expect_tx(x_full, p.x_bytes);
+            bulk_g2s(x_ring, reinterpret_cast<const uint8_t *>(a.X16) + (size_t)chunk * p.x_bytes, p.x_bytes, x_full);
+            mbar_wait(x_full, 0u);
+        }
+    } else if (warp >= kXIssuer && warp < kXIssuer + kXIssuers) {
+        // MMA issue is serial in the issuing thread, so the loop keeps the
+        // work between MMAs to a minimum: descriptors advance by constants.
+        const int ii = warp - kXIssuer;
+        if (lane == 0 && n_my > 0) {
+            const uint32_t idesc = idesc_f16(p.Npad);
+            const uint64_t xdesc0 = sw128_desc(smem_addr(x_ring));
+            const uint32_t xstep = xkb_bytes >> 4;     // descriptor units per k-block
+            int sl[2] = {0, 0};          // next A slot of each of this issuer's sets
+            uint32_t fpar[2] = {0, 0};   // a_full parity bit per slot
+            bool ok = wait_or_abort(x_full, 0u, abort_flag);
+            for (int ti = 0; ok && ti < n_my; ++ti) {
+                const int ab = ti & 1;
+                if (ti >= 2 && !wait_or_abort(&acc_empty[ab], (uint32_t)(((ti >> 1) - 1) & 1), abort_flag)) break;
+                const uint32_t d_tmem = tmem + (uint32_t)(2 * ab + ii) * acc_cols;
+                for (int st = 0; ok && st < p.spt; ++st) {
+#pragma unroll
+                    for (int s2 = 0; s2 < 2; ++s2) {
+                        const int s = 2 * ii + s2;
+                        const int kb0 = st * kpr + s * KI, slot = s * p.AG + sl[s2];
+                        if (!wait_or_abort(&a_full[slot], (fpar[s2] >> sl[s2]) & 1u, abort_flag)) { ok = false; break; }
+                        fpar[s2] ^= 1u << sl[s2];
+                        tc_fence_after();
+                        const uint64_t bd = xdesc0 + (uint64_t)(kb0 * xstep);
+                        const uint32_t at = tmem + a_col0 + (uint32_t)(slot * NW * KI * 32);
+                        // this issuer's first MMA of the tile (per matrix) overwrites its accumulator
+                        const uint32_t acc0 = (st > 0 || s2 > 0) ? 1u : 0u;
+#pragma unroll
+                        for (int e = 0; e < KI; ++e)
+#pragma unroll
+                            for (int w = 0; w < NW; ++w)
+#pragma unroll
+                                for (int jj = 0; jj < 4; ++jj)
+                                    umma_f16_ta(d_tmem + (uint32_t)(w * p.Npad), at + (uint32_t)((w * KI + e) * 32 + 8 * jj),
+                                                bd + (uint64_t)(e * xstep + 2 * jj), idesc, (e > 0 || jj > 0) ? 1u : acc0);
+                        umma_commit(&a_empty[slot]);
+                        sl[s2] = sl[s2] + 1 == p.AG ? 0 : sl[s2] + 1;
+                    }
+                }
+                if (ok) umma_commit(&acc_full[ab]);
+            }
+        }
+    } else if (warp < kXIssuer) {
+        // ---------------- dequant ----------------
+        // every raw stage holds this set's share (KI k-blocks), one A slot per stage
+        const int s = warp >> 2, q = warp & 3;
+        const int m = 32 * q + lane;
+        const uint32_t lane_addr = tmem + ((uint32_t)(32 * q) << 16);
+        int sl = 0, rs = 0;
+        uint32_t epar = 0, rpar = 0;   // a_empty parity bit per slot; raw ring fill parity
+        bool ok = true;
+        const int n_st = n_my * p.spt;
+        for (int gs = 0; ok && gs < n_st; ++gs) {
+            if (!warp_wait_or_abort(&raw_full[rs], rpar, abort_flag)) break;
+            const uint8_t *stg = raw_ring + (size_t)rs * NW * stage_bytes + (size_t)m * p.RB;
+            const int slot = s * p.AG + sl;
+            const uint32_t at = lane_addr + a_col0 + (uint32_t)(slot * NW * KI * 32);
+            for (int e = 0; e < KI; ++e) {
+                const int sub = s * KI + e;   // k-block within the stage
+                const uint8_t *row = stg + (size_t)(sub >> 2) * p.CB;
+                uint32_t o[32], o2[32];
+                dequant_regs<WT>(row, sub & 3, o);
+                if (NW == 2) dequant_regs<WT>(row + stage_bytes, sub & 3, o2);
+                if (e == KI - 1) {   // this warp's rows of the stage are read
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&raw_empty[rs]);
+                }
+                if (e == 0) {
+                    if (gs >= p.AG) {
+                        if (!warp_wait_or_abort(&a_empty[slot], (epar >> sl) & 1u, abort_flag)) { ok = false; break; }
+                        epar ^= 1u << sl;
+                    }
+                    tc_fence_after();
+                }
+                tmem_st32(at + (uint32_t)(e * 32), o);
+                if (NW == 2) tmem_st32(at + (uint32_t)((KI + e) * 32), o2);
+            }
+            if (!ok) break;
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&a_full[slot]);
+            sl = sl + 1 == p.AG ? 0 : sl + 1;
+            if (++rs == p.RS) { rs = 0; rpar ^= 1u; }
+        }
+    } else {
+        // ---------------- epilogue: accumulators -> partials ----------------
+        const int q = warp & 3;
+        grid_dep_wait();   // the partials may still be read by the previous kernel
+        const uint32_t lane_addr = tmem + ((uint32_t)(32 * q) << 16);
+        for (int ti = 0; ti < n_my; ++ti) {
+            const int ab = ti & 1;
+            if (!warp_wait_or_abort(&acc_full[ab], (uint32_t)((ti >> 1) & 1), abort_flag)) break;
+            tc_fence_after();
+            const int2 sr = tile_of(ti);
+            const int seg = sr.x, row0 = sr.y;
+            const int grow0 = (seg == 0 ? p.seg_off[0] : seg == 1 ? p.seg_off[1] : p.seg_off[2]) + row0;
+            const int seg_rows = seg == 0 ? a.seg_rows[0] : (seg == 1 ? a.seg_rows[1] : a.seg_rows[2]);
+            const bool row_ok = row0 + 32 * q + lane < seg_rows;
+            const size_t grow = (size_t)grow0 + 32 * q + lane;
+            const uint32_t acc0 = lane_addr + (uint32_t)(2 * ab) * acc_cols;   // issuer 0; issuer 1 follows
+#pragma unroll
+            for (int w = 0; w < NW; ++w) {
+                float *pw = a.partials + (size_t)(chunk * NW + w) * a.B * p.rows_total + grow;
+                for (int c0 = 0; c0 < p.Npad; c0 += 32) {
+                    uint32_t v[32], u[32];
+                    tmem_ld32_nowait(acc0 + (uint32_t)(w * p.Npad + c0), v);
+                    tmem_ld32_nowait(acc0 + acc_cols + (uint32_t)(w * p.Npad + c0), u);
+                    tmem_wait_ld();
+                    if (row_ok) {
+#pragma unroll
+                        for (int t = 0; t < 32; ++t)
+                            if (c0 + t < a.B)
+                                pw[(size_t)(c0 + t) * p.rows_total] = __uint_as_float(v[t]) + __uint_as_float(u[t]);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[ab]);
+        }
+    }
+
+    if (*abort_flag && threadIdx.x == 0) atomicExch(&g_device_error, LI_ERR_TIMEOUT);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kXProducer) {
+        // an aborted CTA may have MMAs in flight: wait (bounded) for the last commits
+        if (*abort_flag && lane == 0 && n_my > 0) {
+            mbar_wait(&acc_full[(n_my - 1) & 1], (uint32_t)(((n_my - 1) >> 1) & 1));
+        }
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, (uint32_t)p.tmem_cols);
+    }
+}
+
+// The chunks' partial sums added in chunk order, scaled by the X row scale,
+// then the epilogue; four consecutive rows per thread.
+template <int EPI>
+__global__ void __launch_bounds__(256) tcx_reduce_kernel(TcArgs a, int nchunk, int rows_total, int seg_off1,
+                                                         int seg_off2) {
+    constexpr int NW = EPI == kTcSwiGLU ? 2 : 1;
+    grid_dep_wait();
+    grid_dep_launch_dependents();
+    const int nq = rows_total / 4;
+    const int it = (int)blockIdx.x * 256 + (int)threadIdx.x;
+    if (it >= a.B * nq) return;
+    const int b = it / nq, gr = 4 * (it % nq);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f), u = v;
+    for (int c = 0; c < nchunk; ++c) {
+        const float4 t = *reinterpret_cast<const float4 *>(a.partials + ((size_t)(c * NW) * a.B + b) * rows_total + gr);
+        v.x += t.x; v.y += t.y; v.z += t.z; v.w += t.w;
+        if (NW == 2) {
+            const float4 t2 =
+                *reinterpret_cast<const float4 *>(a.partials + ((size_t)(c * NW + 1) * a.B + b) * rows_total + gr);
+            u.x += t2.x; u.y += t2.y; u.z += t2.z; u.w += t2.w;
+        }
+    }
+    const float sc = a.xscale ? a.xscale[b] : 1.0f;
+    float r[4] = {v.x * sc, v.y * sc, v.z * sc, v.w * sc};
+    const int seg = gr >= seg_off2 && a.n_seg > 2 ? 2 : (gr >= seg_off1 && a.n_seg > 1 ? 1 : 0);
+    const int row = gr - (seg == 0 ? 0 : seg == 1 ? seg_off1 : seg_off2);
+    float *dst = (seg == 0 ? a.dst[0] : seg == 1 ? a.dst[1] : a.dst[2]) +
+                 (size_t)b * (seg == 0 ? a.dst_stride[0] : seg == 1 ? a.dst_stride[1] : a.dst_stride[2]) + row;
+    if (EPI == kTcSwiGLU) {
+        const float g[4] = {u.x * sc, u.y * sc, u.z * sc, u.w * sc};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) r[e] = silu(r[e]) * g[e];
+    } else if (EPI == kTcConv && row < a.conv_channels) {
+        // rows row .. row+3 are all conv channels (conv_channels is a multiple of 4)
+        float *cs = a.conv_state + ((size_t)b * a.conv_channels + row) * 3;
+        float4 s4[3];
+#pragma unroll
+        for (int e = 0; e < 3; ++e) s4[e] = reinterpret_cast<const float4 *>(cs)[e];
+        const float st[12] = {s4[0].x, s4[0].y, s4[0].z, s4[0].w, s4[1].x, s4[1].y,
+                              s4[1].z, s4[1].w, s4[2].x, s4[2].y, s4[2].z, s4[2].w};
+        float ns[12];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float4 cw = *reinterpret_cast<const float4 *>(a.conv_w + 4 * (size_t)(row + e));
+            const float x = r[e];
+            const float acc = fmaf(cw.x, st[3 * e], fmaf(cw.y, st[3 * e + 1], fmaf(cw.z, st[3 * e + 2], cw.w * x)));
+            ns[3 * e] = st[3 * e + 1];
+            ns[3 * e + 1] = st[3 * e + 2];
+            ns[3 * e + 2] = x;
+            r[e] = silu(acc);
+        }
+#pragma unroll
+        for (int e = 0; e < 3; ++e)
+            reinterpret_cast<float4 *>(cs)[e] = make_float4(ns[4 * e], ns[4 * e + 1], ns[4 * e + 2], ns[4 * e + 3]);
+    }
+    *reinterpret_cast<float4 *>(dst) = make_float4(r[0], r[1], r[2], r[3]);
+}
+
+// ---------------------------------------------------------------------------
 // x -> f16 with optional RMSNorm and a per-row power-of-two scale
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256)
 tc_prep_kernel(const float *__restrict__ x, int x_stride, const float *__restrict__ gamma, float eps, int K,
-               __half *__restrict__ X16, float *__restrict__ xscale) {
+               __half *__restrict__ X16, float *__restrict__ xscale, int x_npad) {
     __shared__ float s_sq[8], s_mx[8];
     const int b = blockIdx.x, t = threadIdx.x;
     grid_dep_wait();
@@ -515,12 +836,15 @@ tc_prep_kernel(const float *__restrict__ x, int x_stride, const float *__restric
     if (m > 0.f) { frexpf(m, &e); e -= 14; }
     const float s = ldexpf(1.0f, e), inv = ldexpf(1.0f, -e) * r;
     if (t == 0) xscale[b] = s;
-    __half2 *o2 = reinterpret_cast<__half2 *>(X16 + (size_t)b * K);
     for (int i = t; i < K / 4; i += 256) {
         const float4 v = x4[i];
         const float4 g = gamma ? g4[i] : make_float4(1.f, 1.f, 1.f, 1.f);
-        o2[2 * i] = __floats2half2_rn(v.x * g.x * inv, v.y * g.y * inv);
-        o2[2 * i + 1] = __floats2half2_rn(v.z * g.z * inv, v.w * g.w * inv);
+        const __half2 lo = __floats2half2_rn(v.x * g.x * inv, v.y * g.y * inv);
+        const __half2 hi = __floats2half2_rn(v.z * g.z * inv, v.w * g.w * inv);
+        // four consecutive k stay together in either layout (8 bytes)
+        __half *dst = X16 + (x_npad ? tiled_x_offset(b, 4 * i, x_npad) : (size_t)b * K + 4 * i);
+        *reinterpret_cast<uint2 *>(dst) = make_uint2(*reinterpret_cast<const uint32_t *>(&lo),
+                                                     *reinterpret_cast<const uint32_t *>(&hi));
     }
 }
 
@@ -645,6 +969,113 @@ int plan(const TcArgs &a, TcPlan *p) {
     return LI_ERR_BAD_SHAPE;
 }
 
+// X-stationary plan: needs partials (unless sizing), batch <= 32, rows and
+// strides in multiples of 4 (the reduce kernel moves four rows at a time).
+// Measured on B200 (DeltaNet layer step, hidden 4096): 3-32 rows gain (8
+// rows 54 us vs 58, 3 rows 48 vs 52); at 64 rows the K split's partial sums
+// and their reduce cost more than the shorter X stream saves (112 us vs 105).
+constexpr int kTcxMaxRows = 32;
+
+int planx(const TcArgs &a, TcxPlan *p, bool sizing) {
+    if (a.wtype != LI_WTYPE_Q4_K && a.wtype != LI_WTYPE_Q8_0) return LI_ERR_UNSUPPORTED;
+    if (a.K <= 0 || a.K % 256 || a.B <= 0 || a.B > kTcxMaxRows || a.n_seg < 1 || a.n_seg > 3) return LI_ERR_BAD_SHAPE;
+    if (a.epi == kTcSwiGLU && a.n_seg != 1) return LI_ERR_BAD_SHAPE;
+    p->NW = a.epi == kTcSwiGLU ? 2 : 1;
+    p->CB = a.wtype == LI_WTYPE_Q4_K ? 144 : 272;
+    p->Npad = (a.B + 31) / 32 * 32;
+    p->tiles = 0;
+    p->rows_total = 0;
+    for (int s = 0; s < 3; ++s) {
+        const int rows = s < a.n_seg ? a.seg_rows[s] : 0;
+        if (rows % 4) return LI_ERR_BAD_SHAPE;
+        p->seg_off[s] = p->rows_total;
+        p->seg_tiles[s] = (rows + kBM - 1) / kBM;
+        p->tiles += p->seg_tiles[s];
+        p->rows_total += rows;
+    }
+    if (!sizing) {
+        if (!a.partials || !aligned16(a.partials) || !aligned16(a.X16)) return LI_ERR_MISALIGNED;
+        for (int s = 0; s < a.n_seg; ++s)
+            if (a.dst_stride[s] % 4 || !aligned16(a.dst[s])) return LI_ERR_MISALIGNED;
+        if (a.epi == kTcConv && (a.conv_channels % 4 || !aligned16(a.conv_state) || !aligned16(a.conv_w)))
+            return LI_ERR_MISALIGNED;
+    }
+    int sms = 148;
+    {
+        int dev = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    for (int xb : {128 * 1024, 64 * 1024}) {
+        int kc = a.K;
+        while (kc > 256 && ((size_t)p->Npad * kc * 2 > (size_t)xb || a.K % kc || kc % 256)) kc -= 256;
+        if ((size_t)p->Npad * kc * 2 > (size_t)xb || a.K % kc) continue;
+        p->KC = kc;
+        p->nchunk = a.K / kc;
+        p->nkb = kc / 64;
+        if (p->nkb > 4 * 256 || p->nkb % 4) continue;
+        p->x_bytes = (uint32_t)((size_t)p->Npad * kc * 2);
+        for (int sb : {2, 1}) {
+            if ((kc / 256) % sb) continue;
+            // TMEM: two accumulator buffers, then 4 sets x AG slots of SB k-blocks per matrix
+            const int accs = 2 * kXIssuers * p->NW * p->Npad;   // two buffers per issuer
+            const int ag = accs + 4 * 2 * p->NW * sb * 32 <= 512 ? 2 : 1;
+            const int tcols = accs + 4 * ag * p->NW * sb * 32;
+            if (tcols > 512) continue;
+            p->AG = ag;
+            p->tmem_cols = 32;
+            while (p->tmem_cols < tcols) p->tmem_cols <<= 1;
+            p->SB = sb;
+            p->RB = sb * p->CB;
+            p->spt = kc / (256 * sb);
+            const size_t stage = (size_t)p->NW * kBM * p->RB;
+            for (int rs : {3, 2}) {
+                p->RS = rs;
+                p->off_raw = (p->x_bytes + 1023u) / 1024u * 1024u;
+                p->off_bar = p->off_raw + (uint32_t)(rs * stage);
+                p->smem = p->off_bar + 8 * (2 * rs + 2 * 4 * ag + 1 + 4) + 16 + 1024;
+                if (p->smem <= (size_t)kMaxSmem) {
+                    p->cpc = sms / p->nchunk;
+                    if (p->cpc < 1) p->cpc = 1;
+                    if (p->cpc > p->tiles) p->cpc = p->tiles;
+                    return 0;
+                }
+            }
+        }
+    }
+    return LI_ERR_BAD_SHAPE;
+}
+
+template <int WT, int EPI, int KI>
+int launch_x(const CUtensorMap *maps, const TcArgs &a, const TcxPlan &p, cudaStream_t stream, bool pdl) {
+    auto kern = tcx_gemm_kernel<WT, EPI, KI>;
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [&] {
+        attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+    });
+    if (attr_err != cudaSuccess) return (int)attr_err;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(p.nchunk * p.cpc));
+    cfg.blockDim = dim3((unsigned)kXThreads);
+    cfg.dynamicSmemBytes = p.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], a, p);
+    if (e != cudaSuccess) return (int)e;
+    const int items = a.B * (p.rows_total / 4);
+    return (int)launch_pdl(tcx_reduce_kernel<EPI>, dim3((unsigned)((items + 255) / 256)), dim3(256), 0, stream, true,
+                           a, p.nchunk, p.rows_total, p.seg_off[1], p.seg_off[2]);
+}
+
+template <int WT, int EPI>
+int launch_x(const CUtensorMap *maps, const TcArgs &a, const TcxPlan &p, cudaStream_t stream, bool pdl) {
+    return p.SB == 2 ? launch_x<WT, EPI, 2>(maps, a, p, stream, pdl) : launch_x<WT, EPI, 1>(maps, a, p, stream, pdl);
+}
+
 template <int WT, int EPI, bool ATM>
 int launch_kernel(const CUtensorMap *maps, const TcArgs &a, const TcPlan &p, cudaStream_t stream, bool pdl) {
     auto kern = tc_gemm_kernel<WT, EPI, ATM>;
@@ -676,18 +1107,73 @@ int launch_kernel(const CUtensorMap *maps, const TcArgs &a, const TcPlan &p, cud
 }  // namespace
 
 int tc_prep_launch(const float *x, int x_stride, const float *gamma, float eps, int B, int K, __half *X16,
-                   float *xscale, cudaStream_t stream, bool pdl) {
+                   float *xscale, cudaStream_t stream, bool pdl, int x_npad) {
     if (K % 8 || !aligned16(x) || (gamma && !aligned16(gamma)) || !aligned16(X16)) return LI_ERR_MISALIGNED;
+    if (x_npad && (x_npad < B || x_npad % 8 || K % 64)) return LI_ERR_BAD_SHAPE;
     return (int)launch_pdl(tc_prep_kernel, dim3((unsigned)B), dim3(256), 0, stream, pdl, x, x_stride, gamma, eps,
-                           K, X16, xscale);
+                           K, X16, xscale, x_npad);
 }
 
 bool tc_gemm_splits_k(const TcArgs &a) {
+    if (tc_gemm_x_npad(a)) return false;
     TcPlan p;
     return plan(a, &p) == 0 && p.ks > 1;
 }
 
+int tc_gemm_x_npad(const TcArgs &a) {
+    TcArgs c = a;
+    if (!c.X16) c.X16 = reinterpret_cast<const __half *>(c.partials);   // alignment of a pointer to come
+    TcxPlan p;
+    return planx(c, &p, false) == 0 ? p.Npad : 0;
+}
+
+size_t tc_gemm_partials_bytes(int wtype, int epi, int K, int rows_total, int B) {
+    TcArgs a = {};
+    a.wtype = wtype; a.epi = epi; a.K = K; a.total_rows = rows_total; a.B = B;
+    a.n_seg = 1; a.seg_rows[0] = rows_total;
+    TcxPlan p;
+    if (planx(a, &p, true)) return 0;
+    return (size_t)p.nchunk * p.NW * B * p.rows_total * sizeof(float);
+}
+
+namespace {
+int launch_tcx(const TcArgs &a, const TcxPlan &p, cudaStream_t stream, bool pdl) {
+    const size_t rb = li_row_bytes(a.wtype, a.K);
+    CUtensorMap maps[4];
+    memset(maps, 0, sizeof(maps));
+    int rc;
+    const int nw = a.epi == kTcSwiGLU ? 2 : a.n_seg;
+    for (int s = 0; s < 3; ++s) {
+        const int src = s < nw ? s : 0;
+        const int rows = a.epi == kTcSwiGLU ? a.seg_rows[0] : a.seg_rows[src];
+        if (!aligned16(a.W[src])) return LI_ERR_MISALIGNED;
+        rc = encode_2d(&maps[s], CU_TENSOR_MAP_DATA_TYPE_UINT32, a.W[src], rb / 4, (uint64_t)rows, rb,
+                       (uint32_t)(p.RB / 4), kBM, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (rc) return rc;
+    }
+    if (!aligned16(a.X16)) return LI_ERR_MISALIGNED;   // X comes by one bulk copy (no tensor map)
+    const bool q4 = a.wtype == LI_WTYPE_Q4_K;
+    switch (a.epi) {
+    case kTcStore: return q4 ? launch_x<LI_WTYPE_Q4_K, kTcStore>(maps, a, p, stream, pdl)
+                              : launch_x<LI_WTYPE_Q8_0, kTcStore>(maps, a, p, stream, pdl);
+    case kTcSwiGLU: return q4 ? launch_x<LI_WTYPE_Q4_K, kTcSwiGLU>(maps, a, p, stream, pdl)
+                               : launch_x<LI_WTYPE_Q8_0, kTcSwiGLU>(maps, a, p, stream, pdl);
+    case kTcConv: return q4 ? launch_x<LI_WTYPE_Q4_K, kTcConv>(maps, a, p, stream, pdl)
+                             : launch_x<LI_WTYPE_Q8_0, kTcConv>(maps, a, p, stream, pdl);
+    default: return LI_ERR_BAD_ARG;
+    }
+}
+}  // namespace
+
 int tc_gemm_launch(const TcArgs &a, cudaStream_t stream, bool pdl) {
+    {
+        TcxPlan px;
+        if (planx(a, &px, false) == 0) {
+            if (a.x_npad != px.Npad) return LI_ERR_BAD_ARG;   // X16 must be tiled for this kernel
+            return launch_tcx(a, px, stream, pdl);
+        }
+    }
+    if (a.x_npad) return LI_ERR_BAD_ARG;                  // the one-tile kernel reads row-major X
     TcPlan p;
     int rc = plan(a, &p);
     if (rc) return rc;

@@ -27,22 +27,45 @@ struct TcArgs {
     int seg_rows[3];
     float *dst[3];
     int dst_stride[3];
-    const __half *X16;     // [B][K] f16 operand (K-major)
+    const __half *X16;     // [B][K] f16 operand (K-major), or tiled (x_npad > 0)
+    int x_npad;            // > 0: X16 is tiled for the X-stationary kernel (tiled_x_offset)
     const float *xscale;   // [B] output multiplier per batch row, or nullptr (1)
     const float *conv_w;   // kTcConv
     float *conv_state;
     int conv_channels;
+    // fp32 scratch of tc_gemm_partials_bytes() for the X-stationary kernel
+    // (batch <= 64); nullptr keeps the one-tile-per-CTA kernel
+    float *partials;
 };
+
+// Tiled X for the X-stationary kernel: [K/64][npad rows][64 k] f16, each
+// [npad][64] k-block in the 128-byte-swizzled K-major MMA layout (16-byte
+// granule g of row b at granule g ^ (b % 8)), so a k-chunk is one contiguous
+// block; rows B .. npad-1 are never written (their products are discarded).
+// Element offset of (b, k):
+__host__ __device__ inline size_t tiled_x_offset(int b, int k, int npad) {
+    return (size_t)(k >> 6) * npad * 64 + (size_t)(b >> 3) * 512 + (b & 7) * 64 + ((((k & 63) >> 3) ^ (b & 7)) << 3) +
+           (k & 7);
+}
 
 // x[b] (fp32) -> X16[b] = f16(rmsnorm?(x[b]) / s_b), xscale[b] = s_b (a power
 // of two that keeps the row inside f16 range). gamma == nullptr: no norm.
+// x_npad > 0 writes X16 tiled (tiled_x_offset), else row-major [B][K].
 int tc_prep_launch(const float *x, int x_stride, const float *gamma, float eps, int B, int K,
-                   __half *X16, float *xscale, cudaStream_t stream, bool pdl);
+                   __half *X16, float *xscale, cudaStream_t stream, bool pdl, int x_npad = 0);
 
 // One launch covers all batch rows (up to 256); returns LI_ERR_* / cudaError_t.
 // kTcStore launches may split K over several CTAs per tile and then ADD into
 // dst: the caller zeroes dst first when tc_gemm_splits_k(a) is true.
 int tc_gemm_launch(const TcArgs &a, cudaStream_t stream, bool pdl);
 bool tc_gemm_splits_k(const TcArgs &a);
+
+// Scratch for the per-chunk partial sums of the X-stationary kernel (0 when
+// that kernel does not apply to this shape; then partials stay unused).
+size_t tc_gemm_partials_bytes(int wtype, int epi, int K, int rows_total, int B);
+
+// Rows of the tiled X (x_npad) the launch with these arguments (X16 and
+// x_npad aside) will use the X-stationary kernel with, or 0 when it will not.
+int tc_gemm_x_npad(const TcArgs &a);
 
 }  // namespace li

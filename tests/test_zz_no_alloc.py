@@ -70,8 +70,10 @@ def test_noalloc_rejects_batches_beyond_the_scratch(cuda):
 
     lib = _lib.load()
     L = DeltaNetLayer(hidden=4096, n_k_heads=16, n_v_heads=32, head_dim=128, conv_kernel=4)
-    # 127 sequences of this shape fit in the 8 MiB array; 128 do not
-    assert lib.li_deltanet_layer_workspace_size(ctypes.byref(L), 127) <= 8 << 20
-    assert lib.li_deltanet_layer_workspace_size(ctypes.byref(L), 128) > 8 << 20
+    L.w_in_type = L.w_out_type = 12   # Q4_K
+    # every batch of the tensor-core path (up to 256 sequences) of this shape
+    # fits in the 32 MiB array; 600 sequences do not
+    assert max(lib.li_deltanet_layer_workspace_size(ctypes.byref(L), b) for b in range(1, 257)) <= 32 << 20
+    assert lib.li_deltanet_layer_workspace_size(ctypes.byref(L), 600) > 32 << 20
     p = ctypes.c_void_p(256)
-    assert lib.li_launch_deltanet_layer_decode_noalloc(ctypes.byref(L), p, p, p, p, 128, None) == 2008
+    assert lib.li_launch_deltanet_layer_decode_noalloc(ctypes.byref(L), p, p, p, p, 600, None) == 2008
