@@ -8,9 +8,9 @@
 //   warp 5G producer: allocates TMEM; lane 0 streams 2-D tiled TMA boxes of
 //           raw weight blocks ([128 rows] x SB 256-value columns: 144 B Q4_K /
 //           272 B Q8_0 per row and column) into a ring of raw stages, lane 1
-//           3-D boxes of G*XM f16 X k-blocks (64 k x N rows each, 128-byte
-//           swizzle) into a ring of X slots. The TMA engine's cost per copy
-//           is high for small copies, so both streams move 16-72 KB per copy;
+//           bulk copies of G*XM f16 X k-blocks (64 k x N rows each, 128-byte
+//           swizzle: X arrives tiled, see tiled_x_offset) into a ring of X
+//           slots. Both streams move 16-72 KB per copy;
 //   warps 4g..4g+3 (group g) dequant: take k-blocks g, g+G, ... and write
 //           them as f16 into the group's A slots, one tile row per thread:
 //           into tensor memory (tcgen05.st, the row's 64 k in 32 columns of
@@ -84,15 +84,6 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *m
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
         " [%0], [%1, {%2, %3}], [%4];"
         ::"r"(smem_addr(smem_dst)), "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *map, int x, int y, int z,
-                                            uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3, %4}], [%5];"
-        ::"r"(smem_addr(smem_dst)), "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
         : "memory");
 }
 
@@ -213,8 +204,7 @@ __device__ __forceinline__ bool warp_wait_or_abort(uint64_t *bar, uint32_t parit
 template <int WT, int EPI, bool ATM>
 __global__ void __launch_bounds__(kMaxThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__ CUtensorMap tmW1,
-               const __grid_constant__ CUtensorMap tmW2, const __grid_constant__ CUtensorMap tmX,
-               TcArgs a, TcPlan p) {
+               const __grid_constant__ CUtensorMap tmW2, TcArgs a, TcPlan p) {
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte aligned base for the swizzled tiles
     uint8_t *smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
@@ -275,37 +265,42 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
     const uint32_t tmem = *tmem_holder;
     grid_dep_launch_dependents();
 
+    // Ring positions advance incrementally (no divisions in the loops): a
+    // ring slot's fill parity flips each time its ring wraps; each A slot
+    // keeps its own parity bit.
     if (warp == producer_warp) {
         if (lane == 0) {
             // weight stages: they do not depend on the previous kernel, so no
             // griddepcontrol.wait here
-            int issued = 0;
+            int issued = 0, s = 0;
+            uint32_t par = 0;
             for (int r = 0; r < n_raw; ++r) {
-                const int s = r % p.RS;
-                if (r >= p.RS && !wait_or_abort(&raw_empty[s], (uint32_t)(((r / p.RS) - 1) & 1), abort_flag))
-                    break;
+                if (r >= p.RS && !wait_or_abort(&raw_empty[s], par ^ 1u, abort_flag)) break;
                 mbar_arrive_expect_tx(&raw_full[s], (uint32_t)NW * raw_stage_bytes);
                 uint8_t *dst = raw_ring + (size_t)s * NW * raw_stage_bytes;
                 tma_load_2d(dst, tmA, (r_base + r) * (p.RB / 4), row0, &raw_full[s]);
                 if (NW == 2) tma_load_2d(dst + raw_stage_bytes, tmB, (r_base + r) * (p.RB / 4), row0, &raw_full[s]);
                 issued = r + 1;
+                if (++s == p.RS) { s = 0; par ^= 1u; }
             }
             // drain: every copy issued has landed before the CTA exits
             for (int r = issued - p.RS < 0 ? 0 : issued - p.RS; r < issued; ++r)
                 mbar_wait(&raw_full[r % p.RS], (uint32_t)((r / p.RS) & 1));
         } else if (lane == 1) {
-            // X slots of XK consecutive k-blocks, one 3-D TMA box each; slot j
-            // is free again when every group has committed its MMAs on it
+            // X slots of XK consecutive k-blocks: the tiled X keeps them
+            // contiguous, one bulk copy each; slot j is free again when every
+            // group has committed its MMAs on it
             grid_dep_wait();                      // X is written by the previous kernel
+            const uint8_t *xg = reinterpret_cast<const uint8_t *>(a.X16) + (size_t)r_base * kpr * xkb_bytes;
             const int n_xs = nkb / XK;
-            int issued = 0;
+            int issued = 0, s = 0;
+            uint32_t par = 0;
             for (int j = 0; j < n_xs; ++j) {
-                const int s = j % p.XS;
-                if (j >= p.XS && !wait_or_abort(&x_empty[s], (uint32_t)(((j / p.XS) - 1) & 1), abort_flag))
-                    break;
+                if (j >= p.XS && !wait_or_abort(&x_empty[s], par ^ 1u, abort_flag)) break;
                 mbar_arrive_expect_tx(&x_full[s], x_slot_bytes);
-                tma_load_3d(x_ring + (size_t)s * x_slot_bytes, &tmX, 0, 0, r_base * kpr + j * XK, &x_full[s]);
+                bulk_g2s(x_ring + (size_t)s * x_slot_bytes, xg + (size_t)j * x_slot_bytes, x_slot_bytes, &x_full[s]);
                 issued = j + 1;
+                if (++s == p.XS) { s = 0; par ^= 1u; }
             }
             for (int j = issued - p.XS < 0 ? 0 : issued - p.XS; j < issued; ++j)
                 mbar_wait(&x_full[j % p.XS], (uint32_t)((j / p.XS) & 1));
@@ -315,23 +310,27 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
         // Issues the group's MMAs (k-blocks grp, grp+G, ...) into its own
         // accumulators (TMEM columns [grp*acc_cols, (grp+1)*acc_cols)),
         // releases A slots, X slots (after its last k-block in the slot) and
-        // raw stages (after its dequant warps are past them).
+        // raw stages (after its dequant warps are past them). The MMA issue
+        // is serial in this thread, so descriptors advance by constants.
         const int grp = warp - issuer0;
         if (lane == 0) {
             const int n_it = nkb / G;
             const uint32_t idesc = idesc_f16(p.Npad);
             const uint32_t d_tmem = tmem + (uint32_t)grp * acc_cols;
+            const uint64_t xdesc0 = sw128_desc(smem_addr(x_ring));
+            const uint32_t xstep = xkb_bytes >> 4;     // descriptor units per X k-block
+            int ai = 0, xm = 0, xs = 0, kx = grp, kin = grp, rst = 0;
+            uint32_t apar = 0, xpar = 0;
             for (int i = 0; i < n_it; ++i) {
-                const int kb = grp + i * G;
-                const int slot = grp * p.AG + i % p.AG;
-                const int xj = i / p.XM, xs = xj % p.XS;
-                if (!wait_or_abort(&a_full[slot], (uint32_t)((i / p.AG) & 1), abort_flag)) break;
+                const int slot = grp * p.AG + ai;
+                if (!wait_or_abort(&a_full[slot], (apar >> ai) & 1u, abort_flag)) break;
+                apar ^= 1u << ai;
                 // the dequant warps have read this group's last k-block of the raw stage
-                if ((kb % kpr) + G >= kpr) mbar_arrive(&raw_empty[(kb / kpr) % p.RS]);
-                if (!wait_or_abort(&x_full[xs], (uint32_t)((xj / p.XS) & 1), abort_flag)) break;
+                if (kin + G >= kpr) mbar_arrive(&raw_empty[rst]);
+                if (xm == 0 && !wait_or_abort(&x_full[xs], xpar, abort_flag)) break;
                 tc_fence_after();
-                const uint64_t bdesc =
-                    sw128_desc(smem_addr(x_ring + (size_t)xs * x_slot_bytes + (size_t)(kb % XK) * xkb_bytes));
+                const uint64_t bdesc = xdesc0 + (uint64_t)((xs * XK + kx) * xstep);
+                const uint32_t acc0 = i > 0 ? 1u : 0u;
 #pragma unroll
                 for (int w = 0; w < NW; ++w) {
                     if constexpr (ATM) {
@@ -339,18 +338,30 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
 #pragma unroll
                         for (int j = 0; j < 4; ++j)
                             umma_f16_ta(d_tmem + (uint32_t)(w * p.Npad), at + (uint32_t)(8 * j), bdesc + 2 * j, idesc,
-                                        (i > 0 || j > 0) ? 1u : 0u);
+                                        j > 0 ? 1u : acc0);
                     } else {
                         const uint64_t adesc =
                             sw128_desc(smem_addr(a_ring + ((size_t)slot * NW + w) * 16384));
 #pragma unroll
                         for (int j = 0; j < 4; ++j)
                             umma_f16(d_tmem + (uint32_t)(w * p.Npad), adesc + 2 * j, bdesc + 2 * j, idesc,
-                                     (i > 0 || j > 0) ? 1u : 0u);
+                                     j > 0 ? 1u : acc0);
                     }
                 }
                 umma_commit(&a_empty[slot]);
-                if (i % p.XM == p.XM - 1) umma_commit(&x_empty[xs]);
+                if (xm == p.XM - 1) umma_commit(&x_empty[xs]);
+                ai = ai + 1 == p.AG ? 0 : ai + 1;
+                if (++xm == p.XM) {
+                    xm = 0;
+                    if (++xs == p.XS) { xs = 0; xpar ^= 1u; }
+                }
+                kx += G;
+                if (kx >= XK) kx -= XK;
+                kin += G;
+                if (kin >= kpr) {
+                    kin -= kpr;
+                    if (++rst == p.RS) rst = 0;
+                }
             }
             // every MMA this group issued has finished when acc_full sees this commit
             umma_commit(acc_full);
@@ -362,28 +373,30 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
         // the slot is known free, so the wait overlaps the arithmetic.
         const int grp = warp / 4;
         const int m = threadIdx.x % kBM;          // tile row
-        int r_have = -1;
+        int ai = 0, kin = grp, rst = 0;
+        uint32_t epar = 0, rpar = 0;
+        bool new_stage = true;
         for (int i = 0; i < nkb / G; ++i) {
-            const int kb = grp + i * G;
-            const int r = kb / kpr, sub = kb % kpr;   // column sub/4, pair (Q8_0: blocks) sub%4
-            const int rs = r % p.RS;
-            const int slot = grp * p.AG + i % p.AG;
-            if (r != r_have) {
-                if (!warp_wait_or_abort(&raw_full[rs], (uint32_t)((r / p.RS) & 1), abort_flag)) break;
-                r_have = r;
+            const int slot = grp * p.AG + ai;
+            if (new_stage) {
+                if (!warp_wait_or_abort(&raw_full[rst], rpar, abort_flag)) break;
+                new_stage = false;
             }
-            const uint8_t *row = raw_ring + (size_t)rs * NW * raw_stage_bytes + (size_t)m * p.RB + (size_t)(sub >> 2) * p.CB;
+            // super-block column kin/4, sub-block pair (Q8_0: blocks) kin%4
+            const uint8_t *row = raw_ring + (size_t)rst * NW * raw_stage_bytes + (size_t)m * p.RB + (size_t)(kin >> 2) * p.CB;
             uint32_t o[32];
-            dequant_regs<WT>(row, sub & 3, o);
-            if (i >= p.AG && !warp_wait_or_abort(&a_empty[slot], (uint32_t)(((i / p.AG) - 1) & 1), abort_flag))
-                break;
+            dequant_regs<WT>(row, kin & 3, o);
+            if (i >= p.AG) {
+                if (!warp_wait_or_abort(&a_empty[slot], (epar >> ai) & 1u, abort_flag)) break;
+                epar ^= 1u << ai;
+            }
             if constexpr (ATM) {
                 // this thread's row = its TMEM lane; the 64 k of the block fill 32 columns
                 tc_fence_after();                 // the MMAs that read the slot before have finished
                 const uint32_t at = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + a_col0 + (uint32_t)(slot * NW * 32);
                 tmem_st32(at, o);
                 if (NW == 2) {
-                    dequant_regs<WT>(row + raw_stage_bytes, sub & 3, o);
+                    dequant_regs<WT>(row + raw_stage_bytes, kin & 3, o);
                     tmem_st32(at + 32u, o);
                 }
                 tmem_wait_st();
@@ -392,13 +405,20 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
                 uint8_t *at0 = a_ring + (size_t)slot * NW * 16384;
                 store_row(at0, m, o);
                 if (NW == 2) {
-                    dequant_regs<WT>(row + raw_stage_bytes, sub & 3, o);
+                    dequant_regs<WT>(row + raw_stage_bytes, kin & 3, o);
                     store_row(at0 + 16384, m, o);
                 }
                 fence_proxy_async_shared();       // generic-proxy writes -> tensor core reads
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&a_full[slot]);
+            ai = ai + 1 == p.AG ? 0 : ai + 1;
+            kin += G;
+            if (kin >= kpr) {
+                kin -= kpr;
+                if (++rst == p.RS) { rst = 0; rpar ^= 1u; }
+                new_stage = true;
+            }
         }
 
         // ---------------- epilogue ----------------
@@ -882,19 +902,6 @@ int encode_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64
     return r == CUDA_SUCCESS ? 0 : LI_ERR_BAD_SHAPE;
 }
 
-int encode_x(CUtensorMap *map, const void *x16, int K, int B, uint32_t box_rows, uint32_t box_kb) {
-    EncodeTiledFn fn = encoder();
-    if (!fn) return LI_ERR_UNSUPPORTED;
-    const cuuint64_t dims[3] = {64, (cuuint64_t)B, (cuuint64_t)(K / 64)};
-    const cuuint64_t strides[2] = {(cuuint64_t)K * 2, 128};
-    const cuuint32_t box[3] = {64, box_rows, box_kb};
-    const cuuint32_t estr[3] = {1, 1, 1};
-    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(x16), dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS ? 0 : LI_ERR_BAD_SHAPE;
-}
-
 // Columns per raw stage to try first.
 int tc_default_sb() { return 2; }
 
@@ -1095,7 +1102,7 @@ int launch_kernel(const CUtensorMap *maps, const TcArgs &a, const TcPlan &p, cud
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return (int)cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], maps[3], a, p);
+    return (int)cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], a, p);
 }
 
 template <int WT, int EPI>
@@ -1115,7 +1122,10 @@ int tc_prep_launch(const float *x, int x_stride, const float *gamma, float eps, 
 }
 
 bool tc_gemm_splits_k(const TcArgs &a) {
-    if (tc_gemm_x_npad(a)) return false;
+    TcArgs c = a;
+    if (!c.X16) c.X16 = reinterpret_cast<const __half *>(c.partials);
+    TcxPlan px;
+    if (planx(c, &px, false) == 0) return false;   // the X-stationary kernel stores whole sums
     TcPlan p;
     return plan(a, &p) == 0 && p.ks > 1;
 }
@@ -1123,8 +1133,10 @@ bool tc_gemm_splits_k(const TcArgs &a) {
 int tc_gemm_x_npad(const TcArgs &a) {
     TcArgs c = a;
     if (!c.X16) c.X16 = reinterpret_cast<const __half *>(c.partials);   // alignment of a pointer to come
-    TcxPlan p;
-    return planx(c, &p, false) == 0 ? p.Npad : 0;
+    TcxPlan px;
+    if (planx(c, &px, false) == 0) return px.Npad;
+    TcPlan p;
+    return plan(c, &p) == 0 ? p.Npad : 0;
 }
 
 size_t tc_gemm_partials_bytes(int wtype, int epi, int K, int rows_total, int B) {
@@ -1173,10 +1185,10 @@ int tc_gemm_launch(const TcArgs &a, cudaStream_t stream, bool pdl) {
             return launch_tcx(a, px, stream, pdl);
         }
     }
-    if (a.x_npad) return LI_ERR_BAD_ARG;                  // the one-tile kernel reads row-major X
     TcPlan p;
     int rc = plan(a, &p);
     if (rc) return rc;
+    if (a.x_npad != p.Npad) return LI_ERR_BAD_ARG;       // X16 must be tiled with the kernel's row padding
     const size_t rb = li_row_bytes(a.wtype, a.K);
     CUtensorMap maps[4];
     memset(maps, 0, sizeof(maps));
@@ -1189,11 +1201,7 @@ int tc_gemm_launch(const TcArgs &a, cudaStream_t stream, bool pdl) {
                        (uint32_t)(p.RB / 4), kBM, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (rc) return rc;
     }
-    if (!aligned16(a.X16)) return LI_ERR_MISALIGNED;
-    // X as [k-block][row][64 k]: one box brings G*XM consecutive k-blocks,
-    // each a [Npad rows][128 B] 128B-swizzled tile (rows past B read as zeros)
-    rc = encode_x(&maps[3], a.X16, a.K, a.B, (uint32_t)p.Npad, (uint32_t)(p.G * p.XM));
-    if (rc) return rc;
+    if (!aligned16(a.X16)) return LI_ERR_MISALIGNED;   // X slots come by bulk copies (no tensor map)
     const bool q4 = a.wtype == LI_WTYPE_Q4_K;
     switch (a.epi) {
     case kTcStore: return q4 ? launch_kernel<LI_WTYPE_Q4_K, kTcStore>(maps, a, p, stream, pdl)
