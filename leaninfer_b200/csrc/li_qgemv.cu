@@ -33,6 +33,9 @@
 //   * The grid is persistent (SM count x resident CTAs); CTAs stride over
 //     stages. A launch may be a programmatic dependent launch: weight stages
 //     are requested before griddepcontrol.wait, x after it.
+//   * One x row with K a multiple of 32 units (at most 2 Q4_K / 4 Q8_0
+//     units per lane) takes qgemv_row_kernel instead: no staging, a warp
+//     per group of adjacent rows, weights loaded straight into registers.
 #include "li_common.cuh"
 #include "li_qgemv.cuh"
 #include "li_tcgemm.cuh"
@@ -53,17 +56,11 @@ constexpr int kSmemBudget = 112 * 1024;   // stages per CTA (two CTAs per SM)
 // Weights per unit.
 __host__ __device__ constexpr int unit_weights(int wt) { return wt == LI_WTYPE_Q8_0 ? 32 : 64; }
 
-// Q8_0 block u of a row whose shared-memory copy starts at `srow` (4-byte
-// aligned); xq[k] = int16 pair (x[2k], x[2k+1]) of the block, xscale its
-// quantization step. Reads 9 aligned words: even blocks start on a 4-byte
-// boundary (scale in the low half of word 0), odd blocks 2 bytes past one.
-__device__ __forceinline__ float dot_q8_0(const uint8_t *srow, int u, const int *xq, float xscale) {
-    const uint32_t off = 34u * (uint32_t)u;
-    const uint32_t *w = reinterpret_cast<const uint32_t *>(srow + (off & ~3u));
-    uint32_t v[9];
-#pragma unroll
-    for (int i = 0; i < 9; ++i) v[i] = w[i];
-    const bool odd = (off & 2u) != 0;                  // odd block: quants start at word 1
+// Q8_0 block dot product from the block's 9 aligned words (starting at the
+// 4-byte boundary at or below the block): even blocks start on the boundary
+// (scale in the low half of word 0), odd blocks 2 bytes past it. xq[k] =
+// int16 pair (x[2k], x[2k+1]) of the block, xscale its quantization step.
+__device__ __forceinline__ float dot_q8_0_words(const uint32_t (&v)[9], bool odd, const int *xq, float xscale) {
     const uint32_t sh = odd ? 32u : 16u;
     const float d = half_bits_to_float(odd ? (v[0] >> 16) : v[0]);
     int acc = 0;
@@ -76,13 +73,33 @@ __device__ __forceinline__ float dot_q8_0(const uint8_t *srow, int u, const int 
     return d * xscale * (float)acc;
 }
 
-// Q4_K sub-block pair i of a super-block: header h = {d | dmin<<16, scale
-// bytes 0-3, 4-7, 8-11}, nibble bytes q0 (0-15) and q1 (16-31) of the pair.
-// xq0/xq1 = int16 pairs of sub-blocks 2i / 2i+1, xs0/xs1 their steps,
-// sum0/sum1 their fp32 sums of x.
-__device__ __forceinline__ float dot_q4_k(uint4 h, uint4 q0, uint4 q1, int i, const int *xq0,
-                                          const int *xq1, float xs0, float xs1, float sum0,
-                                          float sum1) {
+// Q8_0 block u of a row whose shared-memory copy starts at `srow` (4-byte aligned).
+__device__ __forceinline__ float dot_q8_0(const uint8_t *srow, int u, const int *xq, float xscale) {
+    const uint32_t off = 34u * (uint32_t)u;
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(srow + (off & ~3u));
+    uint32_t v[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) v[i] = w[i];
+    return dot_q8_0_words(v, (off & 2u) != 0, xq, xscale);
+}
+
+// Integer dot of the 32 nibbles of one sub-block of a pair (low nibbles of
+// the pair's 8 words for sub-block 2i, shift 0; high nibbles for 2i+1,
+// shift 4) with its int16 x pairs.
+__device__ __forceinline__ int q4k_nibble_dot(const uint32_t (&w)[8], uint32_t shift, const int *xq) {
+    int acc = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int q = (int)((w[j] >> shift) & 0x0f0f0f0fu);   // positions 4j..4j+3
+        acc = __dp2a_lo(xq[2 * j], q, acc);
+        acc = __dp2a_hi(xq[2 * j + 1], q, acc);
+    }
+    return acc;
+}
+
+// Value of pair i from its two integer dots acc0 / acc1 and the header h.
+__device__ __forceinline__ float q4k_combine(uint4 h, int i, int acc0, int acc1, float xs0, float xs1,
+                                             float sum0, float sum1) {
     const uint32_t bsh = 16u * (uint32_t)(i & 1);
     const uint32_t a0 = h.y >> bsh, a1 = h.z >> bsh, a2 = h.w >> bsh;
     uint32_t sc0, sc1, m0, m1;
@@ -94,20 +111,20 @@ __device__ __forceinline__ float dot_q4_k(uint4 h, uint4 q0, uint4 q1, int i, co
         m0 = ((a2 >> 4) & 15u) | ((a1 >> 2) & 48u);
         m1 = ((a2 >> 12) & 15u) | ((a1 >> 10) & 48u);
     }
-    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-    int acc0 = 0, acc1 = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const int lo = (int)(w[j] & 0x0f0f0f0fu);          // sub-block 2i, positions 4j..4j+3
-        const int hi = (int)((w[j] >> 4) & 0x0f0f0f0fu);   // sub-block 2i+1
-        acc0 = __dp2a_lo(xq0[2 * j], lo, acc0);
-        acc0 = __dp2a_hi(xq0[2 * j + 1], lo, acc0);
-        acc1 = __dp2a_lo(xq1[2 * j], hi, acc1);
-        acc1 = __dp2a_hi(xq1[2 * j + 1], hi, acc1);
-    }
     const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
     return d * fmaf((float)sc0 * xs0, (float)acc0, (float)sc1 * xs1 * (float)acc1) -
            dmin * fmaf((float)m0, sum0, (float)m1 * sum1);
+}
+
+// Q4_K sub-block pair i of a super-block: header h = {d | dmin<<16, scale
+// bytes 0-3, 4-7, 8-11}, nibble bytes q0 (0-15) and q1 (16-31) of the pair.
+// xq0/xq1 = int16 pairs of sub-blocks 2i / 2i+1, xs0/xs1 their steps,
+// sum0/sum1 their fp32 sums of x.
+__device__ __forceinline__ float dot_q4_k(uint4 h, uint4 q0, uint4 q1, int i, const int *xq0,
+                                          const int *xq1, float xs0, float xs1, float sum0,
+                                          float sum1) {
+    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    return q4k_combine(h, i, q4k_nibble_dot(w, 0, xq0), q4k_nibble_dot(w, 4, xq1), xs0, xs1, sum0, sum1);
 }
 
 // Quantize 32 fp32 values to int16 pairs with step max|v|/32767; returns
@@ -362,6 +379,246 @@ qgemv_kernel(QGemvArgs a) {
     }
 }
 
+
+// ---------------------------------------------------------------------------
+// One batch row: a warp owns whole output rows and lane l handles units l,
+// l+32, ... (UPL of them) of each. The CTA quantizes x once into shared
+// memory (int16 pairs in [sub-block][16-byte chunk][unit] order, so a
+// warp's 16-byte reads of one chunk are conflict-free), and lanes read their
+// weight units straight from global memory (the warp's loads of a row cover
+// one contiguous range). A warp holds the weights of R adjacent rows (one
+// contiguous range of the matrix) in registers:
+// the first R rows are loaded before the wait on the previous kernel
+// (weights are constant), the next R rows as soon as the current ones are
+// multiplied, so the loads overlap the reductions and epilogues; each x
+// sub-block is read from shared memory once per R rows. Lane r finishes
+// row r; in the in-projection epilogue it fetches its row's conv state and
+// taps one iteration ahead. Same quantization and unit dot products as
+// qgemv_kernel.
+// ---------------------------------------------------------------------------
+constexpr int kRowThreads = 512;
+
+// Read-only weight loads.
+__device__ __forceinline__ uint4 ldg_nc16(const uint8_t *p) {
+    uint4 v;
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint32_t ldg_nc4(const uint8_t *p) {
+    uint32_t v;
+    asm("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+
+// 32-bit words a lane holds per unit of one weight row.
+__host__ __device__ constexpr int row_unit_words(int wt) { return wt == LI_WTYPE_Q8_0 ? 9 : 12; }
+
+// Rows a warp keeps in flight: about 72 registers of weights, at most 4.
+__host__ __device__ constexpr int row_batch(int wt, int nw, int upl) {
+    return 72 / (row_unit_words(wt) * upl * nw) < 1 ? 1
+         : 72 / (row_unit_words(wt) * upl * nw) > 4 ? 4
+         : 72 / (row_unit_words(wt) * upl * nw);
+}
+
+// Shared memory of the one-row kernel: padded fp32 x, then the int16 pairs
+// (K/2 words), then per-sub-block steps and sums (2 x K/32 floats).
+__host__ __device__ constexpr size_t row_smem_bytes(int wt, int K) {
+    return ((size_t)K + K / unit_weights(wt)) * 4 + (size_t)K / 2 * 4 + (size_t)K / 32 * 8;
+}
+
+template <int WT, int EPI, int UPL>
+__global__ void __launch_bounds__(kRowThreads, 1) qgemv_row_kernel(QGemvArgs a) {
+    constexpr int NW = EPI == kEpiSwiGLU ? 2 : 1;
+    constexpr int UW = unit_weights(WT);
+    constexpr int NSUB = UW / 32;
+    constexpr int NWD = row_unit_words(WT);
+    constexpr int R = row_batch(WT, NW, UPL);
+    constexpr int U = UPL * kWarp;                      // units of a row
+    extern __shared__ __align__(16) uint8_t smem[];
+    float *xs = reinterpret_cast<float *>(smem);                      // x, one pad float per unit
+    uint4 *xq4 = reinterpret_cast<uint4 *>(smem + ((size_t)a.K + a.K / UW) * 4);
+    float *xst = reinterpret_cast<float *>(xq4 + (size_t)NSUB * 4 * U);   // [sb][u] steps
+    float *xsm = xst + NSUB * U;                                          // [sb][u] sums
+    __shared__ float sred[kRowThreads / kWarp];
+    const int t = threadIdx.x, lane = t % kWarp, warp = t / kWarp;
+    const size_t rb = a.plan.row_bytes;
+    const int total = a.plan.total_rows;
+    const int nwarps = (int)gridDim.x * (kRowThreads / kWarp);
+    const int step = nwarps * R;
+    int base = ((int)blockIdx.x * (kRowThreads / kWarp) + warp) * R;   // rows base .. base + R - 1
+
+    uint32_t wq[R][NW][UPL][NWD];
+    auto load_rows = [&](int b0) {
+#pragma unroll
+        for (int rr = 0; rr < R; ++rr) {
+            int row = b0 + rr;
+            if (row >= total) row = total - 1;           // loaded, never stored
+            int m = 0, lr = row;
+            while (m < a.n_seg - 1 && lr >= a.seg_rows[m]) lr -= a.seg_rows[m++];
+#pragma unroll
+            for (int w = 0; w < NW; ++w) {
+                const uint8_t *src = reinterpret_cast<const uint8_t *>(a.W[w == 0 ? m : 1]) + (size_t)lr * rb;
+#pragma unroll
+                for (int i = 0; i < UPL; ++i) {
+                    const uint32_t u = (uint32_t)(lane + kWarp * i);
+                    if constexpr (WT == LI_WTYPE_Q8_0) {
+                        const uint8_t *q = src + ((34u * u) & ~3u);
+#pragma unroll
+                        for (int k = 0; k < 9; ++k) wq[rr][w][i][k] = ldg_nc4(q + 4 * k);
+                    } else {
+                        const uint8_t *blk = src + 144 * (u >> 2);
+                        const uint4 h = ldg_nc16(blk);
+                        const uint4 qa = ldg_nc16(blk + 16 + 32 * (u & 3));
+                        const uint4 qb = ldg_nc16(blk + 32 + 32 * (u & 3));
+                        wq[rr][w][i][0] = h.x;  wq[rr][w][i][1] = h.y;  wq[rr][w][i][2] = h.z;  wq[rr][w][i][3] = h.w;
+                        wq[rr][w][i][4] = qa.x; wq[rr][w][i][5] = qa.y; wq[rr][w][i][6] = qa.z; wq[rr][w][i][7] = qa.w;
+                        wq[rr][w][i][8] = qb.x; wq[rr][w][i][9] = qb.y; wq[rr][w][i][10] = qb.z; wq[rr][w][i][11] = qb.w;
+                    }
+                }
+            }
+        }
+    };
+    // in-projection epilogue inputs of row base + lane (lanes < R)
+    float c0 = 0.f, c1 = 0.f, c2 = 0.f;
+    float4 cw = make_float4(0.f, 0.f, 0.f, 0.f);
+    auto load_conv = [&](int b0) {
+        if constexpr (EPI == kEpiConv) {
+            const int row = b0 + lane;
+            if (lane < R && row < total && row < a.conv_channels) {
+                const float *cs = a.conv_state + (size_t)row * 3;
+                c0 = cs[0]; c1 = cs[1]; c2 = cs[2];
+                cw = *reinterpret_cast<const float4 *>(a.conv_w + 4 * (size_t)row);
+            }
+        }
+    };
+
+    if (base < total) load_rows(base);
+    grid_dep_launch_dependents();
+    grid_dep_wait();   // x and the conv state may be written by earlier kernels
+    {
+        const float4 *x4 = reinterpret_cast<const float4 *>(a.x);
+        const float4 *g4 = reinterpret_cast<const float4 *>(a.gamma);
+        float sq = 0.f;
+        for (int i = t; i < a.K / 4; i += kRowThreads) {
+            float4 v = x4[i];
+            sq = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, sq))));
+            if (a.gamma) {
+                const float4 g = g4[i];
+                v.x *= g.x; v.y *= g.y; v.z *= g.z; v.w *= g.w;
+            }
+            const int k = 4 * i, kp = k + k / UW;
+            xs[kp] = v.x; xs[kp + 1] = v.y; xs[kp + 2] = v.z; xs[kp + 3] = v.w;
+        }
+        sq = warp_sum(sq);
+        if (lane == 0) sred[warp] = sq;
+        __syncthreads();
+        float rnorm = 1.0f;
+        if (a.gamma) {
+            float tot = 0.f;
+            for (int w = 0; w < kRowThreads / kWarp; ++w) tot += sred[w];
+            rnorm = rsqrtf(tot / (float)a.K + a.eps);
+        }
+        for (int q = t; q < NSUB * U; q += kRowThreads) {   // q = sb * U + u
+            const int sb = q / U, u = q % U;
+            const float *xu = xs + (size_t)u * (UW + 1) + 32 * sb;
+            float v[32];
+            float sm = 0.f;
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+                v[k] = xu[k] * rnorm;
+                sm += v[k];
+            }
+            int xq[16];
+            xst[q] = quantize32_s16(v, xq);
+            xsm[q] = sm;
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                xq4[(size_t)(sb * 4 + c) * U + u] = make_uint4(xq[4 * c], xq[4 * c + 1], xq[4 * c + 2], xq[4 * c + 3]);
+        }
+        __syncthreads();
+    }
+    load_conv(base);
+
+    for (; base < total; base += step) {
+        float acc[R][NW];
+#pragma unroll
+        for (int rr = 0; rr < R; ++rr)
+#pragma unroll
+            for (int w = 0; w < NW; ++w) acc[rr][w] = 0.f;
+#pragma unroll
+        for (int i = 0; i < UPL; ++i) {
+            const int u = lane + kWarp * i;
+            int ia[R][NW][NSUB];
+            float xsv[NSUB], xmv[NSUB];
+#pragma unroll
+            for (int sb = 0; sb < NSUB; ++sb) {
+                int xq[16];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const uint4 v = xq4[(size_t)(sb * 4 + c) * U + u];
+                    xq[4 * c] = (int)v.x; xq[4 * c + 1] = (int)v.y; xq[4 * c + 2] = (int)v.z; xq[4 * c + 3] = (int)v.w;
+                }
+                xsv[sb] = xst[sb * U + u];
+                xmv[sb] = xsm[sb * U + u];
+#pragma unroll
+                for (int rr = 0; rr < R; ++rr)
+#pragma unroll
+                    for (int w = 0; w < NW; ++w) {
+                        if constexpr (WT == LI_WTYPE_Q8_0) {
+                            acc[rr][w] += dot_q8_0_words(*reinterpret_cast<const uint32_t(*)[9]>(wq[rr][w][i]),
+                                                         ((34u * (uint32_t)u) & 2u) != 0, xq, xsv[0]);
+                        } else {
+                            ia[rr][w][sb] = q4k_nibble_dot(*reinterpret_cast<const uint32_t(*)[8]>(wq[rr][w][i] + 4),
+                                                           4u * (uint32_t)sb, xq);
+                        }
+                    }
+            }
+            if constexpr (WT == LI_WTYPE_Q4_K) {
+#pragma unroll
+                for (int rr = 0; rr < R; ++rr)
+#pragma unroll
+                    for (int w = 0; w < NW; ++w) {
+                        const uint32_t *v = wq[rr][w][i];
+                        acc[rr][w] += q4k_combine(make_uint4(v[0], v[1], v[2], v[3]), u & 3, ia[rr][w][0],
+                                                  ia[rr][w][NSUB - 1], xsv[0], xsv[NSUB - 1], xmv[0], xmv[NSUB - 1]);
+                    }
+            }
+        }
+        if (base + step < total) load_rows(base + step);
+        float s0 = 0.f, s1 = 0.f;   // lane r: sums of row base + r
+#pragma unroll
+        for (int rr = 0; rr < R; ++rr) {
+            const float v0 = warp_sum(acc[rr][0]);
+            const float v1 = NW == 2 ? warp_sum(acc[rr][NW - 1]) : 0.f;
+            if (lane == rr) { s0 = v0; s1 = v1; }
+        }
+        const int row = base + lane;
+        if (lane < R && row < total) {
+            if (EPI == kEpiSwiGLU) {
+                a.dst[0][row] = silu(s0) * s1;
+            } else if (EPI == kEpiStore) {
+                int m = 0, lr = row;
+                while (m < a.n_seg - 1 && lr >= a.seg_rows[m]) lr -= a.seg_rows[m++];
+                float *d = m == 0 ? a.dst[0] : (m == 1 ? a.dst[1] : a.dst[2]);
+                d[lr] = s0;
+            } else {   // kEpiConv: DeltaNet in-projection epilogue
+                float out = s0;
+                if (row < a.conv_channels) {
+                    float *cs = a.conv_state + (size_t)row * 3;
+                    const float accv = fmaf(cw.x, c0, fmaf(cw.y, c1, fmaf(cw.z, c2, cw.w * s0)));
+                    cs[0] = c1;
+                    cs[1] = c2;
+                    cs[2] = s0;
+                    out = silu(accv);
+                }
+                a.dst[0][row] = out;
+            }
+        }
+        load_conv(base + step);
+    }
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
@@ -472,8 +729,77 @@ static int launch_t(const QGemvArgs &a, int n_rows, cudaStream_t stream, bool pd
     return (int)cudaLaunchKernelExC(&cfg, kern, params);
 }
 
+// The one-row kernel: K a multiple of 32 units (so every lane has UPL whole
+// units) with at most 4 units per lane (x stays in registers).
+template <int WT, int EPI, int UPL>
+static int launch_row_t(const QGemvArgs &a, cudaStream_t stream, bool pdl) {
+    auto kern = qgemv_row_kernel<WT, EPI, UPL>;
+    const size_t smem = row_smem_bytes(WT, a.K);
+    const int per_sm = resident_ctas((const void *)kern, kRowThreads, smem);
+    if (per_sm < 0) return -per_sm;
+    if (per_sm < 1) return LI_ERR_BAD_SHAPE;
+    const int rows_per_cta = kRowThreads / kWarp * row_batch(WT, EPI == kEpiSwiGLU ? 2 : 1, UPL);
+    int grid = num_sms() * per_sm;
+    const int need = (a.plan.total_rows + rows_per_cta - 1) / rows_per_cta;
+    if (grid > need) grid = need;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kRowThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void *params[] = {const_cast<QGemvArgs *>(&a)};
+    return (int)cudaLaunchKernelExC(&cfg, (const void *)kern, params);
+}
+
+template <int WT, int EPI>
+static int launch_row(const QGemvArgs &a, int upl, cudaStream_t stream, bool pdl) {
+    switch (upl) {
+    case 1: return launch_row_t<WT, EPI, 1>(a, stream, pdl);
+    case 2: return launch_row_t<WT, EPI, 2>(a, stream, pdl);
+    default:
+        if constexpr (WT == LI_WTYPE_Q8_0) {
+            if (upl == 3) return launch_row_t<WT, EPI, 3>(a, stream, pdl);
+            if (upl == 4) return launch_row_t<WT, EPI, 4>(a, stream, pdl);
+        }
+        return LI_ERR_BAD_SHAPE;
+    }
+}
+
+// Units per lane of the one-row kernel for this shape, or 0 when it does not apply.
+static int row_kernel_upl(const QGemvArgs &a, int n_rows) {
+    if (n_rows != 1) return 0;
+    const int per_warp = unit_weights(a.wtype) * kWarp;
+    if (a.K % per_warp) return 0;
+    const int upl = a.K / per_warp;
+    const int max_upl = a.wtype == LI_WTYPE_Q8_0 ? 4 : 2;
+    if (upl < 1 || upl > max_upl) return 0;
+    if (a.gamma && !aligned16(a.gamma)) return 0;
+    if (!aligned16(a.x)) return 0;
+    return upl;
+}
+
 int qgemv_launch(const QGemvArgs &a, int n_rows, cudaStream_t stream, bool pdl) {
     const int wt = a.wtype;
+    if (const int upl = row_kernel_upl(a, n_rows)) {
+        switch (a.epi) {
+        case kEpiStore:
+            return wt == LI_WTYPE_Q8_0 ? launch_row<LI_WTYPE_Q8_0, kEpiStore>(a, upl, stream, pdl)
+                                       : launch_row<LI_WTYPE_Q4_K, kEpiStore>(a, upl, stream, pdl);
+        case kEpiSwiGLU:
+            return wt == LI_WTYPE_Q8_0 ? launch_row<LI_WTYPE_Q8_0, kEpiSwiGLU>(a, upl, stream, pdl)
+                                       : launch_row<LI_WTYPE_Q4_K, kEpiSwiGLU>(a, upl, stream, pdl);
+        case kEpiConv:
+            return wt == LI_WTYPE_Q8_0 ? launch_row<LI_WTYPE_Q8_0, kEpiConv>(a, upl, stream, pdl)
+                                       : launch_row<LI_WTYPE_Q4_K, kEpiConv>(a, upl, stream, pdl);
+        default:
+            return LI_ERR_BAD_ARG;
+        }
+    }
     switch (a.epi) {
     case kEpiStore:
         return wt == LI_WTYPE_Q8_0 ? launch_t<LI_WTYPE_Q8_0, kEpiStore>(a, n_rows, stream, pdl)
