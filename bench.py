@@ -47,10 +47,11 @@ NCU_TRAFFIC = {64: 262_778_000}
 UNIT = "tokens/s"
 
 
-# Batch rows from which the layer's projections run on the tensor cores, and
-# up to which they use the X-stationary kernel (each projection is then a GEMM
-# launch plus a reduce launch).
-TC_MIN_ROWS, TCX_MAX_ROWS = 3, 32
+# Batch rows from which the layer's projections run on the tensor cores (up
+# to 3 rows they are SIMT GEMVs at this layer shape), and up to which they use
+# the X-stationary kernel (each projection is then a GEMM launch plus a reduce
+# launch).
+TC_MIN_ROWS, TCX_MAX_ROWS = 4, 32
 
 
 def kernels_per_step(batch: int) -> int:

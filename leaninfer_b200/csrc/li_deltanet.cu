@@ -424,10 +424,25 @@ void li_launch_fused_deltanet_recurrent_out_f32(const float *q, const float *k, 
 }
 
 // Workspace regions, each 256-byte aligned:
-//   SIMT path (n_seqs < kTcMinRows):   proj f32 [B][NI] | og f32 [B][Hv*D]
-//   tensor path (n_seqs >= kTcMinRows): proj f32 [B][NI] | x16 f16 [B][hidden] |
-//                                       xscale f32 [B] | og16 f16 [B][Hv*D]
+//   SIMT path:   proj f32 [B][NI] | og f32 [B][Hv*D]
+//   tensor path: proj f32 [B][NI] | x16 f16 [B][hidden] | xscale f32 [B] |
+//                og16 f16 [B][Hv*D] | partial sums
 static size_t al256(size_t v) { return (v + 255) / 256 * 256; }
+
+// The projections run on the SIMT GEMV kernels below kTcMinRows sequences,
+// and up to kLayerFewRowsMax when both projection shapes suit the few-row
+// kernel (weights read once into registers, no f16 operand and no partial
+// sums); on the tensor cores otherwise. Measured on B200 at hidden 4096,
+// Q4_K, layer step: 2 sequences 30 us (staged SIMT 44), 3: 37.5 (tensor
+// cores 43), 4: 44 either way, 6: 63 (tensor cores 46; the few-row kernel
+// reads every x row from shared memory once per weight row pair). Decided
+// from shapes alone, so the workspace size and the launch agree.
+constexpr int kLayerFewRowsMax = 3;
+static bool layer_simt(const li_deltanet_layer *L, int n_seqs) {
+    if (n_seqs < li::kTcMinRows) return true;
+    return n_seqs <= kLayerFewRowsMax && li::qgemv_few_rows(L->w_in_type, L->hidden, n_seqs) &&
+           li::qgemv_few_rows(L->w_out_type, L->n_v_heads * L->head_dim, n_seqs);
+}
 
 // partial sums of the X-stationary projections (the in- and out-projection
 // run one after the other and share the region)
@@ -443,7 +458,7 @@ size_t li_deltanet_layer_workspace_size(const li_deltanet_layer *L, int n_seqs) 
     if (!L || n_seqs <= 0) return 0;
     const size_t D = L->head_dim, Hk = L->n_k_heads, Hv = L->n_v_heads, n = (size_t)n_seqs;
     const size_t NI = 2 * Hk * D + 2 * Hv * D + 2 * Hv;
-    if (n_seqs < li::kTcMinRows) return al256(NI * n * 4) + al256(Hv * D * n * 4);
+    if (layer_simt(L, n_seqs)) return al256(NI * n * 4) + al256(Hv * D * n * 4);
     const size_t nx = (n + 31) / 32 * 32;   // tiled X operands are padded to 32 rows
     return al256(NI * n * 4) + al256((size_t)L->hidden * nx * 2) + al256(n * 4) + al256(Hv * D * nx * 2) +
            al256(layer_partials_bytes(L, n_seqs));
@@ -469,7 +484,7 @@ int li_launch_deltanet_layer_decode(const li_deltanet_layer *L, const float *x, 
     char *ws = (char *)workspace;
     float *proj = (float *)ws;
     const cudaStream_t s = (cudaStream_t)stream;
-    const bool tc = n_seqs >= kTcMinRows;
+    const bool tc = !layer_simt(L, n_seqs);
     int rc;
 
     RecArgs a = {};

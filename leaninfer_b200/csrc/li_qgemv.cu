@@ -33,9 +33,10 @@
 //   * The grid is persistent (SM count x resident CTAs); CTAs stride over
 //     stages. A launch may be a programmatic dependent launch: weight stages
 //     are requested before griddepcontrol.wait, x after it.
-//   * One x row with K a multiple of 32 units (at most 2 Q4_K / 4 Q8_0
-//     units per lane) takes qgemv_row_kernel instead: no staging, a warp
-//     per group of adjacent rows, weights loaded straight into registers.
+//   * Up to 8 x rows with K a multiple of 32 units (at most 2 units per
+//     lane; 4 Q8_0 units for one x row) take qgemv_row_kernel instead: no
+//     staging, a warp per group of adjacent rows, weights loaded straight
+//     into registers and multiplied with every x row.
 #include "li_common.cuh"
 #include "li_qgemv.cuh"
 #include "li_tcgemm.cuh"
@@ -381,22 +382,23 @@ qgemv_kernel(QGemvArgs a) {
 
 
 // ---------------------------------------------------------------------------
-// One batch row: a warp owns whole output rows and lane l handles units l,
-// l+32, ... (UPL of them) of each. The CTA quantizes x once into shared
-// memory (int16 pairs in [sub-block][16-byte chunk][unit] order, so a
-// warp's 16-byte reads of one chunk are conflict-free), and lanes read their
-// weight units straight from global memory (the warp's loads of a row cover
-// one contiguous range). A warp holds the weights of R adjacent rows (one
-// contiguous range of the matrix) in registers:
-// the first R rows are loaded before the wait on the previous kernel
-// (weights are constant), the next R rows as soon as the current ones are
-// multiplied, so the loads overlap the reductions and epilogues; each x
-// sub-block is read from shared memory once per R rows. Lane r finishes
-// row r; in the in-projection epilogue it fetches its row's conv state and
+// A few batch rows (nb <= NB <= 8): a warp owns whole weight rows and lane l
+// handles units l, l+32, ... (UPL of them) of each. The CTA quantizes the nb
+// x rows once into shared memory (int16 pairs in [row][sub-block][16-byte
+// chunk][unit] order, so a warp's 16-byte reads of one chunk are
+// conflict-free), and lanes read their weight units straight from global
+// memory (the warp's loads of a row cover one contiguous range). A warp
+// holds the weights of R adjacent rows (one contiguous range of the matrix)
+// in registers and multiplies them with every x row: the first R rows are
+// loaded before the wait on the previous kernel (weights are constant), the
+// next R rows as soon as the current ones are multiplied, so the loads
+// overlap the reductions and epilogues. Lane rr * NB + b finishes (row rr,
+// x row b); in the in-projection epilogue it fetches its conv state and
 // taps one iteration ahead. Same quantization and unit dot products as
 // qgemv_kernel.
 // ---------------------------------------------------------------------------
 constexpr int kRowThreads = 512;
+constexpr int kRowMaxBatch = 8;
 
 // Read-only weight loads.
 __device__ __forceinline__ uint4 ldg_nc16(const uint8_t *p) {
@@ -414,33 +416,43 @@ __device__ __forceinline__ uint32_t ldg_nc4(const uint8_t *p) {
 // 32-bit words a lane holds per unit of one weight row.
 __host__ __device__ constexpr int row_unit_words(int wt) { return wt == LI_WTYPE_Q8_0 ? 9 : 12; }
 
-// Rows a warp keeps in flight: about 72 registers of weights, at most 4.
-__host__ __device__ constexpr int row_batch(int wt, int nw, int upl) {
-    return 72 / (row_unit_words(wt) * upl * nw) < 1 ? 1
-         : 72 / (row_unit_words(wt) * upl * nw) > 4 ? 4
-         : 72 / (row_unit_words(wt) * upl * nw);
+// Rows a warp keeps in flight: about 72 registers of weights for one x
+// row; for several, about 60 registers of weights and accumulators (40 with
+// one unit per lane, where more rows share each x read). At least 1, at
+// most 4, and R * NB <= 32 lanes.
+__host__ __device__ constexpr int row_batch_raw(int wt, int nw, int upl, int nb) {
+    return nb > 1 ? (upl > 1 ? 60 : 40) / (row_unit_words(wt) * upl * nw + nb * nw)
+                  : 72 / (row_unit_words(wt) * upl * nw);
+}
+__host__ __device__ constexpr int row_batch(int wt, int nw, int upl, int nb) {
+    return row_batch_raw(wt, nw, upl, nb) < 1 ? 1
+         : row_batch_raw(wt, nw, upl, nb) > 32 / nb ? 32 / nb
+         : row_batch_raw(wt, nw, upl, nb) > 4 ? 4
+         : row_batch_raw(wt, nw, upl, nb);
 }
 
-// Shared memory of the one-row kernel: padded fp32 x, then the int16 pairs
-// (K/2 words), then per-sub-block steps and sums (2 x K/32 floats).
+// Shared memory of the kernel per x row: padded fp32 x, the int16 pairs
+// (K/2 words), per-sub-block steps and sums (2 x K/32 floats).
 __host__ __device__ constexpr size_t row_smem_bytes(int wt, int K) {
     return ((size_t)K + K / unit_weights(wt)) * 4 + (size_t)K / 2 * 4 + (size_t)K / 32 * 8;
 }
 
-template <int WT, int EPI, int UPL>
-__global__ void __launch_bounds__(kRowThreads, 1) qgemv_row_kernel(QGemvArgs a) {
+template <int WT, int EPI, int UPL, int NB>
+__global__ void __launch_bounds__(kRowThreads, 1) qgemv_row_kernel(QGemvArgs a, int nb) {
     constexpr int NW = EPI == kEpiSwiGLU ? 2 : 1;
     constexpr int UW = unit_weights(WT);
     constexpr int NSUB = UW / 32;
     constexpr int NWD = row_unit_words(WT);
-    constexpr int R = row_batch(WT, NW, UPL);
+    constexpr int R = row_batch(WT, NW, UPL, NB);
     constexpr int U = UPL * kWarp;                      // units of a row
+    constexpr int XQ = NSUB * 4 * U;                    // 16-byte chunks of one quantized x row
     extern __shared__ __align__(16) uint8_t smem[];
-    float *xs = reinterpret_cast<float *>(smem);                      // x, one pad float per unit
-    uint4 *xq4 = reinterpret_cast<uint4 *>(smem + ((size_t)a.K + a.K / UW) * 4);
-    float *xst = reinterpret_cast<float *>(xq4 + (size_t)NSUB * 4 * U);   // [sb][u] steps
-    float *xsm = xst + NSUB * U;                                          // [sb][u] sums
-    __shared__ float sred[kRowThreads / kWarp];
+    const int XF = a.K + a.K / UW;                      // padded floats of one x row
+    float *xs = reinterpret_cast<float *>(smem);                                 // [NB][XF]
+    uint4 *xq4 = reinterpret_cast<uint4 *>(smem + (size_t)NB * XF * 4);          // [NB][sb][c][u]
+    float *xst = reinterpret_cast<float *>(xq4 + (size_t)NB * XQ);               // [NB][sb][u] steps
+    float *xsm = xst + NB * NSUB * U;                                            // [NB][sb][u] sums
+    __shared__ float sred[NB][kRowThreads / kWarp];
     const int t = threadIdx.x, lane = t % kWarp, warp = t / kWarp;
     const size_t rb = a.plan.row_bytes;
     const int total = a.plan.total_rows;
@@ -479,14 +491,17 @@ __global__ void __launch_bounds__(kRowThreads, 1) qgemv_row_kernel(QGemvArgs a) 
             }
         }
     };
-    // in-projection epilogue inputs of row base + lane (lanes < R)
+    // this lane's output: row base + lane / NB, x row lane % NB (lanes < R * NB)
+    const int my_rr = lane / NB, my_b = lane % NB;
+    const bool my_lane = lane < R * NB && my_b < nb;
+    // in-projection epilogue inputs of this lane's output
     float c0 = 0.f, c1 = 0.f, c2 = 0.f;
     float4 cw = make_float4(0.f, 0.f, 0.f, 0.f);
     auto load_conv = [&](int b0) {
         if constexpr (EPI == kEpiConv) {
-            const int row = b0 + lane;
-            if (lane < R && row < total && row < a.conv_channels) {
-                const float *cs = a.conv_state + (size_t)row * 3;
+            const int row = b0 + my_rr;
+            if (my_lane && row < total && row < a.conv_channels) {
+                const float *cs = a.conv_state + ((size_t)my_b * a.conv_channels + row) * 3;
                 c0 = cs[0]; c1 = cs[1]; c2 = cs[2];
                 cw = *reinterpret_cast<const float4 *>(a.conv_w + 4 * (size_t)row);
             }
@@ -497,31 +512,39 @@ __global__ void __launch_bounds__(kRowThreads, 1) qgemv_row_kernel(QGemvArgs a) 
     grid_dep_launch_dependents();
     grid_dep_wait();   // x and the conv state may be written by earlier kernels
     {
-        const float4 *x4 = reinterpret_cast<const float4 *>(a.x);
         const float4 *g4 = reinterpret_cast<const float4 *>(a.gamma);
-        float sq = 0.f;
-        for (int i = t; i < a.K / 4; i += kRowThreads) {
-            float4 v = x4[i];
-            sq = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, sq))));
-            if (a.gamma) {
-                const float4 g = g4[i];
-                v.x *= g.x; v.y *= g.y; v.z *= g.z; v.w *= g.w;
+        float sq[NB];
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            sq[b] = 0.f;
+            if (b >= nb) continue;
+            const float4 *x4 = reinterpret_cast<const float4 *>(a.x + (size_t)b * a.x_stride);
+            for (int i = t; i < a.K / 4; i += kRowThreads) {
+                float4 v = x4[i];
+                sq[b] = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, sq[b]))));
+                if (a.gamma) {
+                    const float4 g = g4[i];
+                    v.x *= g.x; v.y *= g.y; v.z *= g.z; v.w *= g.w;
+                }
+                const int k = 4 * i, kp = b * XF + k + k / UW;
+                xs[kp] = v.x; xs[kp + 1] = v.y; xs[kp + 2] = v.z; xs[kp + 3] = v.w;
             }
-            const int k = 4 * i, kp = k + k / UW;
-            xs[kp] = v.x; xs[kp + 1] = v.y; xs[kp + 2] = v.z; xs[kp + 3] = v.w;
         }
-        sq = warp_sum(sq);
-        if (lane == 0) sred[warp] = sq;
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            const float v = warp_sum(sq[b]);
+            if (lane == 0) sred[b][warp] = v;
+        }
         __syncthreads();
-        float rnorm = 1.0f;
-        if (a.gamma) {
-            float tot = 0.f;
-            for (int w = 0; w < kRowThreads / kWarp; ++w) tot += sred[w];
-            rnorm = rsqrtf(tot / (float)a.K + a.eps);
-        }
-        for (int q = t; q < NSUB * U; q += kRowThreads) {   // q = sb * U + u
-            const int sb = q / U, u = q % U;
-            const float *xu = xs + (size_t)u * (UW + 1) + 32 * sb;
+        for (int q = t; q < nb * NSUB * U; q += kRowThreads) {   // q = (b * NSUB + sb) * U + u
+            const int b = q / (NSUB * U), sb = (q / U) % NSUB, u = q % U;
+            float rnorm = 1.0f;
+            if (a.gamma) {
+                float tot = 0.f;
+                for (int w = 0; w < kRowThreads / kWarp; ++w) tot += sred[b][w];
+                rnorm = rsqrtf(tot / (float)a.K + a.eps);
+            }
+            const float *xu = xs + (size_t)b * XF + (size_t)u * (UW + 1) + 32 * sb;
             float v[32];
             float sm = 0.f;
 #pragma unroll
@@ -534,85 +557,98 @@ __global__ void __launch_bounds__(kRowThreads, 1) qgemv_row_kernel(QGemvArgs a) 
             xsm[q] = sm;
 #pragma unroll
             for (int c = 0; c < 4; ++c)
-                xq4[(size_t)(sb * 4 + c) * U + u] = make_uint4(xq[4 * c], xq[4 * c + 1], xq[4 * c + 2], xq[4 * c + 3]);
+                xq4[(size_t)b * XQ + (size_t)(sb * 4 + c) * U + u] =
+                    make_uint4(xq[4 * c], xq[4 * c + 1], xq[4 * c + 2], xq[4 * c + 3]);
         }
         __syncthreads();
     }
     load_conv(base);
 
     for (; base < total; base += step) {
-        float acc[R][NW];
+        float acc[R][NW][NB];
 #pragma unroll
         for (int rr = 0; rr < R; ++rr)
 #pragma unroll
-            for (int w = 0; w < NW; ++w) acc[rr][w] = 0.f;
+            for (int w = 0; w < NW; ++w)
+#pragma unroll
+                for (int b = 0; b < NB; ++b) acc[rr][w][b] = 0.f;
 #pragma unroll
         for (int i = 0; i < UPL; ++i) {
             const int u = lane + kWarp * i;
-            int ia[R][NW][NSUB];
-            float xsv[NSUB], xmv[NSUB];
 #pragma unroll
-            for (int sb = 0; sb < NSUB; ++sb) {
-                int xq[16];
+            for (int b = 0; b < NB; ++b) {
+                if (b >= nb) break;
+                int ia[R][NW][NSUB];
+                float xsv[NSUB], xmv[NSUB];
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const uint4 v = xq4[(size_t)(sb * 4 + c) * U + u];
-                    xq[4 * c] = (int)v.x; xq[4 * c + 1] = (int)v.y; xq[4 * c + 2] = (int)v.z; xq[4 * c + 3] = (int)v.w;
-                }
-                xsv[sb] = xst[sb * U + u];
-                xmv[sb] = xsm[sb * U + u];
+                for (int sb = 0; sb < NSUB; ++sb) {
+                    int xq[16];
+                    const uint4 *xp = xq4 + (size_t)b * XQ + (size_t)sb * 4 * U + u;
 #pragma unroll
-                for (int rr = 0; rr < R; ++rr)
+                    for (int c = 0; c < 4; ++c) {
+                        const uint4 v = xp[c * U];
+                        xq[4 * c] = (int)v.x; xq[4 * c + 1] = (int)v.y; xq[4 * c + 2] = (int)v.z; xq[4 * c + 3] = (int)v.w;
+                    }
+                    xsv[sb] = xst[(b * NSUB + sb) * U + u];
+                    xmv[sb] = xsm[(b * NSUB + sb) * U + u];
 #pragma unroll
-                    for (int w = 0; w < NW; ++w) {
-                        if constexpr (WT == LI_WTYPE_Q8_0) {
-                            acc[rr][w] += dot_q8_0_words(*reinterpret_cast<const uint32_t(*)[9]>(wq[rr][w][i]),
-                                                         ((34u * (uint32_t)u) & 2u) != 0, xq, xsv[0]);
-                        } else {
-                            ia[rr][w][sb] = q4k_nibble_dot(*reinterpret_cast<const uint32_t(*)[8]>(wq[rr][w][i] + 4),
-                                                           4u * (uint32_t)sb, xq);
+                    for (int rr = 0; rr < R; ++rr)
+#pragma unroll
+                        for (int w = 0; w < NW; ++w) {
+                            if constexpr (WT == LI_WTYPE_Q8_0) {
+                                acc[rr][w][b] += dot_q8_0_words(*reinterpret_cast<const uint32_t(*)[9]>(wq[rr][w][i]),
+                                                                ((34u * (uint32_t)u) & 2u) != 0, xq, xsv[0]);
+                            } else {
+                                ia[rr][w][sb] = q4k_nibble_dot(*reinterpret_cast<const uint32_t(*)[8]>(wq[rr][w][i] + 4),
+                                                               4u * (uint32_t)sb, xq);
+                            }
                         }
-                    }
-            }
-            if constexpr (WT == LI_WTYPE_Q4_K) {
+                }
+                if constexpr (WT == LI_WTYPE_Q4_K) {
 #pragma unroll
-                for (int rr = 0; rr < R; ++rr)
+                    for (int rr = 0; rr < R; ++rr)
 #pragma unroll
-                    for (int w = 0; w < NW; ++w) {
-                        const uint32_t *v = wq[rr][w][i];
-                        acc[rr][w] += q4k_combine(make_uint4(v[0], v[1], v[2], v[3]), u & 3, ia[rr][w][0],
-                                                  ia[rr][w][NSUB - 1], xsv[0], xsv[NSUB - 1], xmv[0], xmv[NSUB - 1]);
-                    }
+                        for (int w = 0; w < NW; ++w) {
+                            const uint32_t *v = wq[rr][w][i];
+                            acc[rr][w][b] += q4k_combine(make_uint4(v[0], v[1], v[2], v[3]), u & 3, ia[rr][w][0],
+                                                         ia[rr][w][NSUB - 1], xsv[0], xsv[NSUB - 1], xmv[0],
+                                                         xmv[NSUB - 1]);
+                        }
+                }
             }
         }
         if (base + step < total) load_rows(base + step);
-        float s0 = 0.f, s1 = 0.f;   // lane r: sums of row base + r
+        float s0 = 0.f, s1 = 0.f;   // this lane's sums
 #pragma unroll
-        for (int rr = 0; rr < R; ++rr) {
-            const float v0 = warp_sum(acc[rr][0]);
-            const float v1 = NW == 2 ? warp_sum(acc[rr][NW - 1]) : 0.f;
-            if (lane == rr) { s0 = v0; s1 = v1; }
-        }
-        const int row = base + lane;
-        if (lane < R && row < total) {
+        for (int rr = 0; rr < R; ++rr)
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                if (b >= nb) break;
+                const float v0 = warp_sum(acc[rr][0][b]);
+                const float v1 = NW == 2 ? warp_sum(acc[rr][NW - 1][b]) : 0.f;
+                if (lane == rr * NB + b) { s0 = v0; s1 = v1; }
+            }
+        const int row = base + my_rr;
+        if (my_lane && row < total) {
             if (EPI == kEpiSwiGLU) {
-                a.dst[0][row] = silu(s0) * s1;
+                a.dst[0][(size_t)my_b * a.dst_stride[0] + row] = silu(s0) * s1;
             } else if (EPI == kEpiStore) {
                 int m = 0, lr = row;
                 while (m < a.n_seg - 1 && lr >= a.seg_rows[m]) lr -= a.seg_rows[m++];
                 float *d = m == 0 ? a.dst[0] : (m == 1 ? a.dst[1] : a.dst[2]);
-                d[lr] = s0;
+                const int ds = m == 0 ? a.dst_stride[0] : (m == 1 ? a.dst_stride[1] : a.dst_stride[2]);
+                d[(size_t)my_b * ds + lr] = s0;
             } else {   // kEpiConv: DeltaNet in-projection epilogue
                 float out = s0;
                 if (row < a.conv_channels) {
-                    float *cs = a.conv_state + (size_t)row * 3;
+                    float *cs = a.conv_state + ((size_t)my_b * a.conv_channels + row) * 3;
                     const float accv = fmaf(cw.x, c0, fmaf(cw.y, c1, fmaf(cw.z, c2, cw.w * s0)));
                     cs[0] = c1;
                     cs[1] = c2;
                     cs[2] = s0;
                     out = silu(accv);
                 }
-                a.dst[0][row] = out;
+                a.dst[0][(size_t)my_b * a.dst_stride[0] + row] = out;
             }
         }
         load_conv(base + step);
@@ -729,16 +765,17 @@ static int launch_t(const QGemvArgs &a, int n_rows, cudaStream_t stream, bool pd
     return (int)cudaLaunchKernelExC(&cfg, kern, params);
 }
 
-// The one-row kernel: K a multiple of 32 units (so every lane has UPL whole
-// units) with at most 4 units per lane (x stays in registers).
-template <int WT, int EPI, int UPL>
-static int launch_row_t(const QGemvArgs &a, cudaStream_t stream, bool pdl) {
-    auto kern = qgemv_row_kernel<WT, EPI, UPL>;
-    const size_t smem = row_smem_bytes(WT, a.K);
+// The few-row kernel: K a multiple of 32 units (every lane has UPL whole
+// units), at most 4 units per lane for one x row (Q8_0) and 2 otherwise (x
+// and the weights stay in registers), n_rows <= 8.
+template <int WT, int EPI, int UPL, int NB>
+static int launch_row_t(const QGemvArgs &a, int n_rows, cudaStream_t stream, bool pdl) {
+    auto kern = qgemv_row_kernel<WT, EPI, UPL, NB>;
+    const size_t smem = NB * row_smem_bytes(WT, a.K);
     const int per_sm = resident_ctas((const void *)kern, kRowThreads, smem);
     if (per_sm < 0) return -per_sm;
     if (per_sm < 1) return LI_ERR_BAD_SHAPE;
-    const int rows_per_cta = kRowThreads / kWarp * row_batch(WT, EPI == kEpiSwiGLU ? 2 : 1, UPL);
+    const int rows_per_cta = kRowThreads / kWarp * row_batch(WT, EPI == kEpiSwiGLU ? 2 : 1, UPL, NB);
     int grid = num_sms() * per_sm;
     const int need = (a.plan.total_rows + rows_per_cta - 1) / rows_per_cta;
     if (grid > need) grid = need;
@@ -752,50 +789,73 @@ static int launch_row_t(const QGemvArgs &a, cudaStream_t stream, bool pdl) {
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    void *params[] = {const_cast<QGemvArgs *>(&a)};
+    int nb = n_rows;
+    void *params[] = {const_cast<QGemvArgs *>(&a), &nb};
     return (int)cudaLaunchKernelExC(&cfg, (const void *)kern, params);
 }
 
+template <int WT, int EPI, int UPL>
+static int launch_row_nb(const QGemvArgs &a, int n_rows, cudaStream_t stream, bool pdl) {
+    if (n_rows == 1) return launch_row_t<WT, EPI, UPL, 1>(a, n_rows, stream, pdl);
+    if constexpr (UPL <= 2) {
+        switch (n_rows) {
+        case 2: return launch_row_t<WT, EPI, UPL, 2>(a, n_rows, stream, pdl);
+        case 3: return launch_row_t<WT, EPI, UPL, 3>(a, n_rows, stream, pdl);
+        case 4: return launch_row_t<WT, EPI, UPL, 4>(a, n_rows, stream, pdl);
+        case 5:
+        case 6: return launch_row_t<WT, EPI, UPL, 6>(a, n_rows, stream, pdl);
+        default: return launch_row_t<WT, EPI, UPL, 8>(a, n_rows, stream, pdl);
+        }
+    }
+    return LI_ERR_BAD_SHAPE;
+}
+
 template <int WT, int EPI>
-static int launch_row(const QGemvArgs &a, int upl, cudaStream_t stream, bool pdl) {
+static int launch_row(const QGemvArgs &a, int upl, int n_rows, cudaStream_t stream, bool pdl) {
     switch (upl) {
-    case 1: return launch_row_t<WT, EPI, 1>(a, stream, pdl);
-    case 2: return launch_row_t<WT, EPI, 2>(a, stream, pdl);
+    case 1: return launch_row_nb<WT, EPI, 1>(a, n_rows, stream, pdl);
+    case 2: return launch_row_nb<WT, EPI, 2>(a, n_rows, stream, pdl);
     default:
         if constexpr (WT == LI_WTYPE_Q8_0) {
-            if (upl == 3) return launch_row_t<WT, EPI, 3>(a, stream, pdl);
-            if (upl == 4) return launch_row_t<WT, EPI, 4>(a, stream, pdl);
+            if (upl == 3) return launch_row_t<WT, EPI, 3, 1>(a, n_rows, stream, pdl);
+            if (upl == 4) return launch_row_t<WT, EPI, 4, 1>(a, n_rows, stream, pdl);
         }
         return LI_ERR_BAD_SHAPE;
     }
 }
 
-// Units per lane of the one-row kernel for this shape, or 0 when it does not apply.
-static int row_kernel_upl(const QGemvArgs &a, int n_rows) {
-    if (n_rows != 1) return 0;
-    const int per_warp = unit_weights(a.wtype) * kWarp;
-    if (a.K % per_warp) return 0;
-    const int upl = a.K / per_warp;
-    const int max_upl = a.wtype == LI_WTYPE_Q8_0 ? 4 : 2;
-    if (upl < 1 || upl > max_upl) return 0;
-    if (a.gamma && !aligned16(a.gamma)) return 0;
-    if (!aligned16(a.x)) return 0;
-    return upl;
+// Units per lane of the few-row kernel for this shape, or 0 when it does not apply.
+static int row_kernel_upl_shape(int wtype, int K, int n_rows) {
+    if (n_rows < 1 || n_rows > kRowMaxBatch) return 0;
+    if (wtype != LI_WTYPE_Q8_0 && wtype != LI_WTYPE_Q4_K) return 0;
+    const int per_warp = unit_weights(wtype) * kWarp;
+    if (K <= 0 || K % per_warp) return 0;
+    const int upl = K / per_warp;
+    const int max_upl = n_rows > 1 ? 2 : (wtype == LI_WTYPE_Q8_0 ? 4 : 2);
+    return upl <= max_upl ? upl : 0;
 }
+
+static int row_kernel_upl(const QGemvArgs &a, int n_rows) {
+    if (a.gamma && !aligned16(a.gamma)) return 0;
+    if (!aligned16(a.x) || (n_rows > 1 && a.x_stride % 4)) return 0;
+    return row_kernel_upl_shape(a.wtype, a.K, n_rows);
+}
+
+bool qgemv_few_rows(int wtype, int K, int n_rows) { return row_kernel_upl_shape(wtype, K, n_rows) != 0; }
 
 int qgemv_launch(const QGemvArgs &a, int n_rows, cudaStream_t stream, bool pdl) {
     const int wt = a.wtype;
     if (const int upl = row_kernel_upl(a, n_rows)) {
         switch (a.epi) {
         case kEpiStore:
-            return wt == LI_WTYPE_Q8_0 ? launch_row<LI_WTYPE_Q8_0, kEpiStore>(a, upl, stream, pdl)
-                                       : launch_row<LI_WTYPE_Q4_K, kEpiStore>(a, upl, stream, pdl);
+            return wt == LI_WTYPE_Q8_0 ? launch_row<LI_WTYPE_Q8_0, kEpiStore>(a, upl, n_rows, stream, pdl)
+                                       : launch_row<LI_WTYPE_Q4_K, kEpiStore>(a, upl, n_rows, stream, pdl);
         case kEpiSwiGLU:
-            return wt == LI_WTYPE_Q8_0 ? launch_row<LI_WTYPE_Q8_0, kEpiSwiGLU>(a, upl, stream, pdl)
-                                       : launch_row<LI_WTYPE_Q4_K, kEpiSwiGLU>(a, upl, stream, pdl);
+            return wt == LI_WTYPE_Q8_0 ? launch_row<LI_WTYPE_Q8_0, kEpiSwiGLU>(a, upl, n_rows, stream, pdl)
+                                       : launch_row<LI_WTYPE_Q4_K, kEpiSwiGLU>(a, upl, n_rows, stream, pdl);
         case kEpiConv:
-            return wt == LI_WTYPE_Q8_0 ? launch_row<LI_WTYPE_Q8_0, kEpiConv>(a, upl, stream, pdl)
-                                       : launch_row<LI_WTYPE_Q4_K, kEpiConv>(a, upl, stream, pdl);
+            return wt == LI_WTYPE_Q8_0 ? launch_row<LI_WTYPE_Q8_0, kEpiConv>(a, upl, n_rows, stream, pdl)
+                                       : launch_row<LI_WTYPE_Q4_K, kEpiConv>(a, upl, n_rows, stream, pdl);
         default:
             return LI_ERR_BAD_ARG;
         }

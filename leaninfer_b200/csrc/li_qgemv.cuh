@@ -39,5 +39,9 @@ struct QGemvArgs {
 
 int qgemv_plan(int wtype, int K, int total_rows, int epi, QGemvPlan *p);
 int qgemv_launch(const QGemvArgs &a, int n_rows, cudaStream_t stream, bool pdl);
+// True when n_rows x rows of this shape take the few-row kernel (weights in
+// registers, every x row per weight load; x and gamma 16-byte aligned, x
+// rows a multiple of 4 floats apart).
+bool qgemv_few_rows(int wtype, int K, int n_rows);
 
 }  // namespace li

@@ -978,6 +978,10 @@ int plan(const TcArgs &a, TcPlan *p) {
 
 // X-stationary plan: needs partials (unless sizing), batch <= 32, rows and
 // strides in multiples of 4 (the reduce kernel moves four rows at a time).
+// X chunks of 64 KB come first: they leave room for 4 raw stages (a stage's
+// load then overlaps the dequant of the ones before it) and give 2x the
+// (tile, chunk) items to spread over the SMs (layer step at hidden 4096, B =
+// 3-32: 3-3.5 us faster than with 128 KB chunks and 2-3 raw stages).
 // Measured on B200 (DeltaNet layer step, hidden 4096): 3-32 rows gain (8
 // rows 54 us vs 58, 3 rows 48 vs 52); at 64 rows the K split's partial sums
 // and their reduce cost more than the shorter X stream saves (112 us vs 105).
@@ -1012,7 +1016,7 @@ int planx(const TcArgs &a, TcxPlan *p, bool sizing) {
         int dev = 0;
         if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     }
-    for (int xb : {128 * 1024, 64 * 1024}) {
+    for (int xb : {64 * 1024, 128 * 1024}) {
         int kc = a.K;
         while (kc > 256 && ((size_t)p->Npad * kc * 2 > (size_t)xb || a.K % kc || kc % 256)) kc -= 256;
         if ((size_t)p->Npad * kc * 2 > (size_t)xb || a.K % kc) continue;
@@ -1035,7 +1039,7 @@ int planx(const TcArgs &a, TcxPlan *p, bool sizing) {
             p->RB = sb * p->CB;
             p->spt = kc / (256 * sb);
             const size_t stage = (size_t)p->NW * kBM * p->RB;
-            for (int rs : {3, 2}) {
+            for (int rs : {4, 3, 2}) {
                 p->RS = rs;
                 p->off_raw = (p->x_bytes + 1023u) / 1024u * 1024u;
                 p->off_bar = p->off_raw + (uint32_t)(rs * stage);

@@ -16,6 +16,11 @@ from conftest import GOLDEN, assert_close, max_rel_err, rng
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-3
+# Layer output y when the projections run on the tensor cores (f16 operands:
+# X and the dequantized weights each rounded to f16 once, fp32 accumulation;
+# about 4e-4 normwise per projection at hidden 4096, two projections composed
+# through the recurrence). States and conv states keep TOL on every path.
+TOL_Y_F16 = 2e-3
 
 
 def T(a, dev):
@@ -128,8 +133,10 @@ def test_qkv_q_config1_shapes(cuda, oracle_mod, wtype):
 
 
 @pytest.mark.parametrize("wtype", [8, 12])
-@pytest.mark.parametrize("n_rows", [1, 3])
+@pytest.mark.parametrize("n_rows", [1, 2, 3, 6, 8])
 def test_matmul_q_shapes(cuda, oracle_mod, wtype, n_rows):
+    """Up to 8 rows, K = 1024 (Q8_0) / 2048 (Q4_K) per unit per lane take the
+    few-row kernel (K = 4096 here), the others the staged kernel."""
     from leaninfer_b200 import ops, synth
     r = rng(200 + wtype + n_rows)
     for K, N_ in [(256, 5), (4096, 1037), (12288, 512), (5120, 333)]:
@@ -279,6 +286,8 @@ def _layer(cuda, w, repeat_type=0, in_norm_w=None):
     (12, 2, 1024, 4, 8, 0),
     (8, 3, 1024, 2, 8, 1),
     (12, 1, 4096, 16, 32, 0),      # the decode workload's layer shape
+    (12, 3, 4096, 16, 32, 1),      # few-row SIMT projections at the layer shape
+    (12, 8, 4096, 16, 32, 0),
     (12, 5, 1024, 4, 8, 0),        # tensor-core projections from 3 sequences on
     (12, 8, 1024, 4, 8, 0),
     (8, 16, 1024, 2, 8, 1),
@@ -300,7 +309,7 @@ def test_layer_decode_steps(cuda, oracle_mod, wtype, B, hidden, Hk, Hv, repeat_t
         y = torch.empty(B, hidden, device=cuda)
         layer.step(T(x, cuda), y, cs, st)
         y_ref = oracle_mod.deltanet_layer_decode(L, keep, x, cs_ref, st_ref)
-        assert_close(N(y), y_ref, TOL, f"y step {step}")
+        assert_close(N(y), y_ref, TOL_Y_F16 if B >= 3 else TOL, f"y step {step}")
         assert_close(N(cs), cs_ref, TOL, f"conv state step {step}")
         assert_close(N(st), st_ref, TOL, f"state step {step}")
 
