@@ -113,3 +113,30 @@ def test_layer_workspace_size(lib):
     need = lib.li_deltanet_layer_workspace_size(ctypes.byref(L), 64)
     assert need >= (NI + 32 * 128) * 64 * 4
     assert need % 256 == 0
+
+
+def test_layer_projection_path_by_shape(lib):
+    """The layer's projections are SIMT GEMVs up to 3 sequences when both
+    projection shapes suit the few-row kernel (Q4_K, K = 4096: 2 units per
+    lane), tensor-core GEMMs from 4 on; the workspace (proj + og fp32 for the
+    SIMT path, plus the f16 operands for the tensor path) shows the choice
+    without a GPU."""
+    from leaninfer_b200._lib import DeltaNetLayer
+
+    def al(v):
+        return (v + 255) // 256 * 256
+
+    L = DeltaNetLayer(hidden=4096, n_k_heads=16, n_v_heads=32, head_dim=128, conv_kernel=4,
+                      w_in_type=12, w_out_type=12)
+    NI = 2 * 16 * 128 + 2 * 32 * 128 + 64
+    for B in (1, 2, 3):
+        assert lib.li_deltanet_layer_workspace_size(ctypes.byref(L), B) == al(NI * B * 4) + al(4096 * B * 4)
+    for B in (4, 8, 64):
+        assert lib.li_deltanet_layer_workspace_size(ctypes.byref(L), B) > al(NI * B * 4) + al(4096 * B * 4)
+    # hidden 1024 with Q4_K: K is not a multiple of 32 units of 64 weights, so
+    # 3 sequences already take the tensor cores
+    L2 = DeltaNetLayer(hidden=1024, n_k_heads=4, n_v_heads=8, head_dim=128, conv_kernel=4,
+                       w_in_type=12, w_out_type=12)
+    NI2 = 2 * 4 * 128 + 2 * 8 * 128 + 16
+    assert lib.li_deltanet_layer_workspace_size(ctypes.byref(L2), 2) == al(NI2 * 2 * 4) + al(1024 * 2 * 4)
+    assert lib.li_deltanet_layer_workspace_size(ctypes.byref(L2), 3) > al(NI2 * 3 * 4) + al(1024 * 3 * 4)
