@@ -17,6 +17,11 @@ and states) so that consecutive uses of one instance are separated by more
 than 3x the L2 capacity of traffic.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl reference]
+
+Other workloads (`--workload`): `prefill` (one 8192-token chunked prefill +
+gated norm + bf16 out-projection), `qkv` (RMSNorm + Q/K/V Q8_0 GEMV, K = 2048,
+one token) and `ffn` (RMSNorm + SwiGLU FFN 4096 -> 12288 -> 4096, `--batch`
+rows, `--wtype` 12 = Q4_K or 8 = Q8_0).
 """
 from __future__ import annotations
 
@@ -132,6 +137,36 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------
+# timed replays: the steps of the rotating instances chained in CUDA graphs
+# --------------------------------------------------------------------------
+def chained_graphs(insts: list, launch, steps: int):
+    """One graph holding every instance's step in rotation order and one with
+    the first steps % len(insts) of them, so `steps` steps replay as whole
+    chains (a model replays its layers the same way) with no host launch
+    between consecutive steps. Returns a function that runs the steps."""
+    import torch
+
+    def capture(items):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for it in items:
+                launch(it)
+        return g
+    n = len(insts)
+    full = capture(insts)
+    rem = steps % n
+    part = capture(insts[:rem]) if rem else None
+    torch.cuda.synchronize()
+
+    def run():
+        for _ in range(steps // n):
+            full.replay()
+        if part is not None:
+            part.replay()
+    return run
+
+
+# --------------------------------------------------------------------------
 # our arm
 # --------------------------------------------------------------------------
 def build_instances(dev, batch: int, n_inst: int, seed: int):
@@ -195,6 +230,7 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
     def step(i: int):
         insts[i % n_inst]["graph"].replay()
 
+    timed = chained_graphs(insts, launch, args.steps)
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
@@ -209,8 +245,7 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
     t_wall0 = time.time()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(args.steps):
-        step(i)
+    timed()
     e1.record(stream)
     torch.cuda.synchronize()
     t_wall1 = time.time()
@@ -443,6 +478,199 @@ def cpu_baseline_prefill() -> dict:
             "seconds": round(dt, 3)}
 
 
+# --------------------------------------------------------------------------
+# quantized GEMV workloads: RMSNorm + Q/K/V (Q8_0, one token) and the SwiGLU
+# FFN (gate/up + down, Q4_K or Q8_0, B rows)
+# --------------------------------------------------------------------------
+QKV_K, QKV_N = 2048, (2048, 512, 512)
+FFN_K, FFN_N = 4096, 12288
+
+
+def gemv_bytes(kind: str, wtype: int, rows: int) -> int:
+    """Algorithmic bytes per step: every weight byte once, gamma, x in and
+    the outputs out."""
+    from leaninfer_b200 import _lib
+    rb = lambda n, k: n * int(_lib.load().li_row_bytes(wtype, k))
+    if kind == "qkv":
+        return sum(rb(n, QKV_K) for n in QKV_N) + 4 * QKV_K * (rows + 1) + 4 * rows * sum(QKV_N)
+    return 2 * rb(FFN_N, FFN_K) + rb(FFN_K, FFN_N) + 4 * FFN_K * (2 * rows + 1)
+
+
+# rows from which li_launch_fused_ffn_q runs on the tensor cores
+FFN_TC_MIN_ROWS = 3
+
+
+def gemv_launches(kind: str, rows: int) -> int:
+    if kind == "qkv":
+        return 1                                  # one GEMV over the three weight segments
+    if rows < FFN_TC_MIN_ROWS:
+        return 2                                  # gate/up GEMV + down GEMV
+    return 6 if rows <= TCX_MAX_ROWS else 4      # prep + GEMM (+ reduce) per projection
+
+
+def run_gemv(args, rank: int, world: int, dist) -> dict | None:
+    """qkv: li_launch_fused_rms_norm_qkv_q, K = 2048 -> 2048 / 512 / 512, Q8_0,
+    one token per step (rows = 1). ffn: li_launch_fused_ffn_q, 4096 -> 12288
+    -> 4096 (gate/up + down), `--wtype` Q4_K (12) or Q8_0 (8), `--batch` rows.
+    Steps replay one CUDA graph per weight instance and rotate over enough
+    instances that consecutive uses of one are separated by more than 3x the
+    L2 capacity of traffic."""
+    import torch
+    from leaninfer_b200 import _lib, ops, synth
+    from leaninfer_b200.shard import max_over_ranks
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    kind = args.workload
+    wtype = synth.Q8_0 if kind == "qkv" else args.wtype
+    rows = 1 if kind == "qkv" else args.batch
+    lib = _lib.load()
+    per = gemv_bytes(kind, wtype, rows)
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    n_inst = max(2, math.ceil(3 * l2 / per) + 1)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    K = QKV_K if kind == "qkv" else FFN_K
+    insts = []
+    for i in range(n_inst):
+        r = np.random.Generator(np.random.PCG64((rank + 1) * 1000 + i))
+        it = dict(x=t(r.standard_normal((rows, K)).astype(np.float32)),
+                  gamma=t(r.uniform(0.5, 1.5, K).astype(np.float32)))
+        if kind == "qkv":
+            it["W"] = [t(synth.random_weights(r, wtype, n, K)) for n in QKV_N]
+            it["out"] = [torch.empty(rows, n, device=dev) for n in QKV_N]
+        else:
+            it["W"] = [t(synth.random_weights(r, wtype, FFN_N, K)), t(synth.random_weights(r, wtype, FFN_N, K)),
+                       t(synth.random_weights(r, wtype, K, FFN_N))]
+            it["y"] = torch.empty(rows, K, device=dev)
+            it["ws"] = torch.empty(int(lib.li_fused_ffn_workspace_size(K, FFN_N, rows)), device=dev,
+                                   dtype=torch.uint8)
+        insts.append(it)
+    p = ops._p
+
+    def launch(it):
+        s = ops._stream()
+        if kind == "qkv":
+            rc = lib.li_launch_fused_rms_norm_qkv_q(wtype, p(it["x"]), p(it["gamma"]), *(p(w) for w in it["W"]),
+                                                     *(p(o) for o in it["out"]), K, *QKV_N, rows, 1e-6, s)
+        else:
+            rc = lib.li_launch_fused_ffn_q(wtype, p(it["x"]), p(it["gamma"]), *(p(w) for w in it["W"]),
+                                           p(it["y"]), K, FFN_N, rows, 1e-6, p(it["ws"]), it["ws"].numel(), s)
+        if rc:
+            raise RuntimeError(f"{kind} launch failed: {rc}")
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for it in insts:
+            launch(it)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    for it in insts:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            launch(it)
+        it["graph"] = g
+    torch.cuda.synchronize()
+    timed = chained_graphs(insts, launch, args.steps)
+    for i in range(args.warmup):
+        insts[i % n_inst]["graph"].replay()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    sampler = ClockSampler(dev.index)
+    sampler.start()
+    time.sleep(0.3)
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_wall0 = time.time()
+    e0.record(stream)
+    timed()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    ms = e0.elapsed_time(e1)
+    sampler.stop()
+    # e2e: x from pinned host memory, the outputs back, every step
+    outs = (lambda it: it["out"]) if kind == "qkv" else (lambda it: [it["y"]])
+    hx = [it["x"].cpu().pin_memory() for it in insts]
+    ho = [[o.cpu().pin_memory() for o in outs(it)] for it in insts]
+    e_steps = max(1, min(args.steps, 200))
+
+    def e2e_step(i: int):
+        it = insts[i % n_inst]
+        it["x"].copy_(hx[i % n_inst], non_blocking=True)
+        it["graph"].replay()
+        for h, o in zip(ho[i % n_inst], outs(it)):
+            h.copy_(o, non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(e_steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    status = ops.device_status()
+    if status:
+        raise RuntimeError(f"device status {status} after the timed region")
+    ms, e2e_ms = max_over_ranks([ms, e2e_ms], dist, device=dev)
+    if rank != 0:
+        return None
+    peaks = measured_peaks()
+    step_s = ms / 1e3 / args.steps
+    achieved = per / step_s / 1e9
+    wname = "Q8_0" if wtype == synth.Q8_0 else "Q4_K"
+    out_bytes = sum(o.numel() * 4 for o in outs(insts[0]))
+    line = {
+        "metric": "tokens/s", "value": round(world * rows * args.steps / (ms / 1e3), 1), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": f"f32 ({wname} weights)",
+        "data": "synthetic",
+        "config": {"workload": "rms_norm_qkv_q8_0" if kind == "qkv" else f"ffn_{wname.lower()}",
+                   "rows_per_gpu": rows, "K": K, "N": list(QKV_N) if kind == "qkv" else [FFN_N, FFN_N, FFN_K],
+                   "weights": wname, "parallelism": f"replicas x{world}, no collectives",
+                   "l2": f"inputs larger than L2: rotating {n_inst} weight instances of {per / 1e6:.1f} MB"},
+        "roofline": {"bound": "hbm", "kernel": "RMSNorm + Q/K/V GEMV" if kind == "qkv" else
+                     "RMSNorm + SwiGLU gate/up + down projection",
+                     "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
+                     "algorithmic_bytes_per_step": per, "traffic": None},
+        "e2e": {"value": round(world * rows * e_steps / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": rows * K * 4, "d2h_bytes_per_step": out_bytes},
+        "gpu_launches": gemv_launches(kind, rows) * args.steps,
+        "clocks": sampler.summary(t_wall0, t_wall1),
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_gemv(kind, wtype, rows)
+    return line
+
+
+def cpu_baseline_gemv(kind: str, wtype: int, rows: int) -> dict:
+    """The oracle (dequantize, double accumulation) on the same shapes: one
+    step of the qkv workload, one row of the FFN."""
+    from leaninfer_b200 import synth
+    from oracle import oracle
+    r = np.random.Generator(np.random.PCG64(13))
+    K = QKV_K if kind == "qkv" else FFN_K
+    x = r.standard_normal((1, K)).astype(np.float32)
+    gamma = r.uniform(0.5, 1.5, K).astype(np.float32)
+    if kind == "qkv":
+        Ws = [synth.random_weights(r, wtype, n, K) for n in QKV_N]
+        t0 = time.perf_counter()
+        for w, n in zip(Ws, QKV_N):
+            oracle.rms_norm_matmul(wtype, x, gamma, w, n, 1e-6)
+    else:
+        Wg, Wu = synth.random_weights(r, wtype, FFN_N, K), synth.random_weights(r, wtype, FFN_N, K)
+        Wd = synth.random_weights(r, wtype, K, FFN_N)
+        t0 = time.perf_counter()
+        oracle.ffn(wtype, x, gamma, Wg, Wu, Wd, FFN_N, 1e-6)
+    dt = time.perf_counter() - t0
+    return {"value": round(1 / dt, 2), "unit": "tokens/s", "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"one row of the {kind} workload (oracle/li_oracle.c, dequantize + double accumulation, "
+                      f"{oracle.num_threads()} host threads)", "seconds": round(dt, 3)}
+
+
 def run_reference(args, rank: int) -> dict | None:
     if rank != 0:
         return None
@@ -467,9 +695,12 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--traffic", type=float, default=None, help="ncu DRAM bytes per step, if captured")
-    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "qkv", "ffn"], default="decode",
                     help="decode: the fused DeltaNet layer decode step (the headline); prefill: one 8192-token "
-                         "chunked prefill + gated norm + bf16 out-projection")
+                         "chunked prefill + gated norm + bf16 out-projection; qkv: RMSNorm + Q/K/V Q8_0 GEMV "
+                         "(K=2048, one token); ffn: RMSNorm + SwiGLU FFN 4096 -> 12288 -> 4096 (--batch rows, "
+                         "--wtype)")
+    ap.add_argument("--wtype", type=int, choices=[8, 12], default=12, help="ffn weights: 12 = Q4_K, 8 = Q8_0")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -499,7 +730,12 @@ def main():
             dist.barrier()
     _lib.load()
     try:
-        line = run_prefill(args, rank, world, dist) if args.workload == "prefill" else run_ours(args, rank, world, dist)
+        if args.workload == "prefill":
+            line = run_prefill(args, rank, world, dist)
+        elif args.workload in ("qkv", "ffn"):
+            line = run_gemv(args, rank, world, dist)
+        else:
+            line = run_ours(args, rank, world, dist)
     finally:
         if dist:
             dist.destroy_process_group()

@@ -437,13 +437,15 @@ __host__ __device__ constexpr size_t row_smem_bytes(int wt, int K) {
     return ((size_t)K + K / unit_weights(wt)) * 4 + (size_t)K / 2 * 4 + (size_t)K / 32 * 8;
 }
 
-template <int WT, int EPI, int UPL, int NB>
+// R1: one row per warp (matrices with too few rows to give every SM a
+// CTA at the default row batch).
+template <int WT, int EPI, int UPL, int NB, bool R1>
 __global__ void __launch_bounds__(kRowThreads, 1) qgemv_row_kernel(QGemvArgs a, int nb) {
     constexpr int NW = EPI == kEpiSwiGLU ? 2 : 1;
     constexpr int UW = unit_weights(WT);
     constexpr int NSUB = UW / 32;
     constexpr int NWD = row_unit_words(WT);
-    constexpr int R = row_batch(WT, NW, UPL, NB);
+    constexpr int R = R1 ? 1 : row_batch(WT, NW, UPL, NB);
     constexpr int U = UPL * kWarp;                      // units of a row
     constexpr int XQ = NSUB * 4 * U;                    // 16-byte chunks of one quantized x row
     extern __shared__ __align__(16) uint8_t smem[];
@@ -768,14 +770,22 @@ static int launch_t(const QGemvArgs &a, int n_rows, cudaStream_t stream, bool pd
 // The few-row kernel: K a multiple of 32 units (every lane has UPL whole
 // units), at most 4 units per lane for one x row (Q8_0) and 2 otherwise (x
 // and the weights stay in registers), n_rows <= 8.
-template <int WT, int EPI, int UPL, int NB>
+template <int WT, int EPI, int UPL, int NB, bool R1 = false>
 static int launch_row_t(const QGemvArgs &a, int n_rows, cudaStream_t stream, bool pdl) {
-    auto kern = qgemv_row_kernel<WT, EPI, UPL, NB>;
+    constexpr int R = R1 ? 1 : row_batch(WT, EPI == kEpiSwiGLU ? 2 : 1, UPL, NB);
+    if constexpr (NB == 1 && !R1 && R > 1) {
+        // groups of R rows per warp would leave more than half the SMs idle:
+        // one row per warp (measured: the 3072-row Q8_0 QKV GEMV 9.8 -> 8.6 us;
+        // at 58% of the SMs busy, the 4096-row out-projection, no gain)
+        if (2 * a.plan.total_rows < kRowThreads / kWarp * R * num_sms())
+            return launch_row_t<WT, EPI, UPL, NB, true>(a, n_rows, stream, pdl);
+    }
+    auto kern = qgemv_row_kernel<WT, EPI, UPL, NB, R1>;
     const size_t smem = NB * row_smem_bytes(WT, a.K);
     const int per_sm = resident_ctas((const void *)kern, kRowThreads, smem);
     if (per_sm < 0) return -per_sm;
     if (per_sm < 1) return LI_ERR_BAD_SHAPE;
-    const int rows_per_cta = kRowThreads / kWarp * row_batch(WT, EPI == kEpiSwiGLU ? 2 : 1, UPL, NB);
+    const int rows_per_cta = kRowThreads / kWarp * R;
     int grid = num_sms() * per_sm;
     const int need = (a.plan.total_rows + rows_per_cta - 1) / rows_per_cta;
     if (grid > need) grid = need;
