@@ -688,7 +688,8 @@ def run_reference(args, rank: int) -> dict | None:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=500)
+    # 5000 decode steps at B = 64 are ~0.5 s of timed work: several clock samples (100 ms apart)
+    ap.add_argument("--steps", type=int, default=5000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
