@@ -672,8 +672,25 @@ def cpu_baseline_gemv(kind: str, wtype: int, rows: int) -> dict:
 
 
 def run_reference(args, rank: int) -> dict | None:
+    """The reference's CPU path for the workload (the oracle port: ggml's CPU
+    ops are not vendored), on the host cores with all threads; rank 0 only."""
     if rank != 0:
         return None
+    if args.workload != "decode":
+        if args.workload == "prefill":
+            cb, metric, cfg = cpu_baseline_prefill(), "chunked prefill tokens/s", {
+                "workload": "deltanet_chunk_prefill_bf16", "tokens_per_sequence": PF_T, "chunk": 64}
+        else:
+            wtype = 8 if args.workload == "qkv" else args.wtype
+            cb, metric = cpu_baseline_gemv(args.workload, wtype, 1), "tokens/s"
+            cfg = {"workload": "rms_norm_qkv_q8_0" if args.workload == "qkv" else
+                   f"ffn_{'q8_0' if wtype == 8 else 'q4_k'}", "rows_timed": 1}
+        cfg["note"] = "the reference's ggml CPU ops are not vendored; its CPU path is the C oracle port"
+        return {"impl": "reference", "metric": metric, "value": cb["value"], "unit": cb["unit"], "n_gpus": 0,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f64 accumulation", "data": "synthetic", "config": cfg,
+                "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     cb = cpu_baseline(args.batch, max(1, args.steps if args.steps <= 8 else 8))
     return {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": 0,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
