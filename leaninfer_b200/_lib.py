@@ -47,6 +47,16 @@ class DeltaNetLayer(ctypes.Structure):
     ]
 
 
+class GgmlTensor(ctypes.Structure):
+    """Mirror of ``li_ggml_tensor`` (include/leaninfer-ggml.h)."""
+
+
+GgmlTensor._fields_ = [
+    ("type", ctypes.c_int32), ("ne", c_int64 * 4), ("nb", c_size_t * 4), ("op", ctypes.c_int32),
+    ("op_params", ctypes.c_int32 * 16), ("src", POINTER(GgmlTensor) * 10), ("data", c_void_p),
+]
+
+
 # name -> (restype, argtypes)
 _SIGS = {
     # reference entries (void)
@@ -87,6 +97,9 @@ _SIGS = {
                 c_void_p, c_size_t, c_void_p]),
     "li_launch_deltanet_layer_decode_noalloc": (
         c_int, [POINTER(DeltaNetLayer), c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
+    # ggml-style node dispatch (include/leaninfer-ggml.h)
+    "li_ggml_workspace_size": (c_size_t, [c_void_p]),
+    "li_ggml_compute_forward": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
 }
 
 _lib = None
