@@ -11,6 +11,7 @@ from __future__ import annotations
 
 import ctypes
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -231,6 +232,19 @@ class DeltaNetLayerDecode:
             dt_bias=_p(dt_bias), norm_w=_p(norm_w), w_out=_p(w_out))
         self.device = w_in.device
         self._ws = None
+
+    @classmethod
+    def from_gguf(cls, path, il: int, *, n_k_heads: int, n_v_heads: int, head_dim: int = 128, names=None,
+                  device="cuda", **kw) -> "DeltaNetLayerDecode":
+        """Layer `il` of a GGUF checkpoint (leaninfer_b200.gguf_file: the
+        quantized rows are copied to the device as they are in the file)."""
+        from .gguf_file import GGUFFile, deltanet_layer
+        with GGUFFile(path) as g:
+            w = deltanet_layer(g, il, n_k_heads=n_k_heads, n_v_heads=n_v_heads, head_dim=head_dim, names=names)
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(device)
+        return cls(hidden=w["hidden"], n_k_heads=n_k_heads, n_v_heads=n_v_heads, head_dim=head_dim,
+                   w_in=t(w["w_in"]), conv_w=t(w["conv_w"]), a_log=t(w["a_log"]), dt_bias=t(w["dt_bias"]),
+                   norm_w=t(w["norm_w"]), w_out=t(w["w_out"]), w_in_type=w["wtype"], w_out_type=w["wtype"], **kw)
 
     @property
     def conv_channels(self) -> int:
