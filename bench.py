@@ -67,15 +67,15 @@ def kernels_per_step(batch: int) -> int:
     return 4          # x prep, in-projection GEMM, recurrence, out-projection GEMM
 
 
-def algorithmic_bytes(batch: int) -> int:
+def algorithmic_bytes(batch: int, state_bytes: int = 4) -> int:
     """Bytes a step must move at least once: both weight matrices (Q4_K), the
-    conv weights, and per sequence the recurrent state and conv state read
-    and written plus x in and y out."""
+    conv weights, and per sequence the recurrent state (state_bytes per
+    element) and conv state read and written plus x in and y out."""
     w_in = N_IN * (HIDDEN // 256) * 144
     w_out = HIDDEN * (HV * D // 256) * 144
     conv_w = CONV_CH * 4 * 4
     small = (2 * HV + D) * 4
-    per_seq = HV * D * D * 4 * 2 + CONV_CH * 3 * 4 * 2 + HIDDEN * 4 * 2
+    per_seq = HV * D * D * state_bytes * 2 + CONV_CH * 3 * 4 * 2 + HIDDEN * 4 * 2
     return w_in + w_out + conv_w + small + batch * per_seq
 
 
@@ -169,7 +169,7 @@ def chained_graphs(insts: list, launch, steps: int):
 # --------------------------------------------------------------------------
 # our arm
 # --------------------------------------------------------------------------
-def build_instances(dev, batch: int, n_inst: int, seed: int):
+def build_instances(dev, batch: int, n_inst: int, seed: int, state_dtype=None):
     import torch
     from leaninfer_b200 import ops, synth
     insts = []
@@ -181,7 +181,7 @@ def build_instances(dev, batch: int, n_inst: int, seed: int):
                                         conv_w=t(w["conv_w"]), a_log=t(w["a_log"]), dt_bias=t(w["dt_bias"]),
                                         norm_w=t(w["norm_w"]), w_out=t(w["w_out"]))
         inp = synth.deltanet_inputs(r, batch, w)
-        state = torch.empty(batch, HV, D, D, device=dev)
+        state = torch.empty(batch, HV, D, D, device=dev, dtype=state_dtype or torch.float32)
         # state ~ N(0, 0.02), drawn on the device (268 MB per instance at B=64)
         g = torch.Generator(device=dev)
         g.manual_seed(seed * 1000 + i)
@@ -201,10 +201,12 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
     # weak scaling: a global batch of batch x world sequences, one contiguous
     # shard of `batch` sequences per rank, no data exchange during a step
     _, B = shard_bounds(args.batch * world, world, rank)
+    sbytes = 2 if args.state == "f16" else 4
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size
-    per_inst = algorithmic_bytes(B)
+    per_inst = algorithmic_bytes(B, sbytes)
     n_inst = max(2, math.ceil(3 * l2 / per_inst) + 1)
-    insts = build_instances(dev, B, n_inst, seed=rank + 1)
+    insts = build_instances(dev, B, n_inst, seed=rank + 1,
+                            state_dtype=torch.float16 if sbytes == 2 else torch.float32)
     stream = torch.cuda.current_stream()
 
     def launch(it):
@@ -313,13 +315,15 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
 
     peaks = measured_peaks()
     step_s = ms / 1e3 / args.steps
-    achieved = algorithmic_bytes(B) / step_s / 1e9
+    achieved = algorithmic_bytes(B, sbytes) / step_s / 1e9
     value = world * B * args.steps / (ms / 1e3)
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (Q4_K weights)", "data": "synthetic",
-        "config": {"workload": "deltanet_layer_decode_q4k", "batch_per_gpu": B, "global_batch": B * world,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 (Q4_K weights" + (", f16 recurrent state)" if sbytes == 2 else ")"), "data": "synthetic",
+        "config": {"workload": "deltanet_layer_decode_q4k" + ("_f16state" if sbytes == 2 else ""),
+                   "batch_per_gpu": B, "global_batch": B * world,
                    "hidden": HIDDEN, "k_heads": HK, "v_heads": HV, "head_dim": D, "weights": "Q4_K",
                    "parallelism": f"sequence-sharded x{world}, no collectives",
                    "l2": f"inputs larger than L2: rotating {n_inst} layer instances of {per_inst / 1e6:.1f} MB"},
@@ -328,8 +332,9 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
                          "in-projection GEMV + recurrence + out-projection GEMV") + " (PDL-chained)",
                      "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
-                     "algorithmic_bytes_per_step": algorithmic_bytes(B),
-                     "traffic": args.traffic if args.traffic is not None else NCU_TRAFFIC.get(B)},
+                     "algorithmic_bytes_per_step": algorithmic_bytes(B, sbytes),
+                     "traffic": args.traffic if args.traffic is not None else
+                     (NCU_TRAFFIC.get(B) if sbytes == 4 else None)},
         "e2e": {"value": round(world * B * e_steps / (e2e_ms / 1e3), 1), "unit": UNIT,
                 "h2d_bytes_per_step": B * HIDDEN * 4, "d2h_bytes_per_step": B * HIDDEN * 4},
         "gpu_launches": kernels_per_step(B) * args.steps,
@@ -741,6 +746,8 @@ def main():
                          "(K=2048, one token); ffn: RMSNorm + SwiGLU FFN 4096 -> 12288 -> 4096 (--batch rows, "
                          "--wtype)")
     ap.add_argument("--wtype", type=int, choices=[8, 12], default=12, help="ffn weights: 12 = Q4_K, 8 = Q8_0")
+    ap.add_argument("--state", choices=["f32", "f16"], default="f32",
+                    help="decode: recurrent state storage (f16 = li_launch_deltanet_layer_decode_f16state)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -251,6 +251,17 @@ int li_launch_deltanet_layer_decode(const li_deltanet_layer * L,
         const float * x, float * y, float * conv_state, float * state,
         int n_seqs, void * workspace, size_t workspace_bytes, void * stream);
 
+/* The same step with the recurrent state stored as fp16 (`state` is
+ * __half [n_seqs][Hv][D][D], the fp32 entry's element order), computed in
+ * fp32 and rounded once per step when stored, saturating at +-65504 (the
+ * reference's +-1e6 clamp lies beyond the fp16 range). Half the state bytes
+ * of the fp32 entry. No counterpart among the reference's kernels: upstream's
+ * fp16 recurrent-state storage option (reference docs/RESULTS.md:37). Same
+ * workspace size. */
+int li_launch_deltanet_layer_decode_f16state(const li_deltanet_layer * L,
+        const float * x, float * y, float * conv_state, void * state,
+        int n_seqs, void * workspace, size_t workspace_bytes, void * stream);
+
 /* The same layer decode step for callers that cannot allocate device memory
  * for a workspace (for example a ggml graph whose buffers were all planned
  * before this op, or a host runtime that owns every device allocation and

@@ -95,6 +95,9 @@ _SIGS = {
     "li_launch_deltanet_layer_decode": (
         c_int, [POINTER(DeltaNetLayer), c_void_p, c_void_p, c_void_p, c_void_p, c_int,
                 c_void_p, c_size_t, c_void_p]),
+    "li_launch_deltanet_layer_decode_f16state": (
+        c_int, [POINTER(DeltaNetLayer), c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+                c_void_p, c_size_t, c_void_p]),
     "li_launch_deltanet_layer_decode_noalloc": (
         c_int, [POINTER(DeltaNetLayer), c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
     # ggml-style node dispatch (include/leaninfer-ggml.h)

@@ -70,6 +70,9 @@ struct RecArgs {
     int og16_npad;          // > 0: o_gated16 tiled for the X-stationary out-projection
     float *zero_out;        // layer output to clear for a K-split out-projection, or nullptr
     int64_t zero_len;       // floats in zero_out
+    // layer mode with the state stored as fp16 (same element order)
+    const __half *state_in16;
+    __half *state_out16;
 };
 
 template <int D>
@@ -104,7 +107,43 @@ __device__ __forceinline__ void vstore(float *dst, const float *src) {
     *reinterpret_cast<typename VecT<RPL>::T *>(dst) = v;
 }
 
-template <int D, bool LAYER, int RB>
+// The same for a state stored as fp16: one 2*RPL-byte access, fp32 in
+// registers; stores saturate at the fp16 maximum.
+template <int RPL>
+__device__ __forceinline__ void vload_h(float *dst, const __half *src) {
+    if constexpr (RPL == 4) {
+        const uint2 v = *reinterpret_cast<const uint2 *>(src);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&v.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&v.y));
+        dst[0] = a.x; dst[1] = a.y; dst[2] = b.x; dst[3] = b.y;
+    } else if constexpr (RPL == 2) {
+        const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(src));
+        dst[0] = a.x; dst[1] = a.y;
+    } else {
+        dst[0] = __half2float(*src);
+    }
+}
+
+template <int RPL>
+__device__ __forceinline__ void vstore_h(__half *dst, const float *src) {
+    float c[RPL];
+#pragma unroll
+    for (int r = 0; r < RPL; ++r) c[r] = fminf(fmaxf(src[r], -65504.0f), 65504.0f);
+    if constexpr (RPL == 4) {
+        const __half2 a = __floats2half2_rn(c[0], c[1]), b = __floats2half2_rn(c[2], c[3]);
+        uint2 v;
+        v.x = *reinterpret_cast<const uint32_t *>(&a);
+        v.y = *reinterpret_cast<const uint32_t *>(&b);
+        *reinterpret_cast<uint2 *>(dst) = v;
+    } else if constexpr (RPL == 2) {
+        *reinterpret_cast<__half2 *>(dst) = __floats2half2_rn(c[0], c[1]);
+    } else {
+        *dst = __float2half_rn(c[0]);
+    }
+}
+
+// SH: the state is stored as fp16 (layer mode only).
+template <int D, bool LAYER, int RB, bool SH = false>
 __global__ void __launch_bounds__(kRecThreads, kRecMinBlocks)
 recurrent_kernel(RecArgs a) {
     constexpr int RPL = RB / 32;                 // value rows per lane
@@ -128,10 +167,16 @@ recurrent_kernel(RecArgs a) {
     const float scale = rsqrtf((float)D);
 
     // ---- state slice -> registers (independent of the previous kernel) ----
-    const float *Sin = a.state_in + ((size_t)seq * a.n_heads + h) * D * D + row0;
     float S[CPW][RPL];
+    if constexpr (SH) {
+        const __half *Sin = a.state_in16 + ((size_t)seq * a.n_heads + h) * D * D + row0;
 #pragma unroll
-    for (int j = 0; j < CPW; ++j) vload<RPL>(S[j], Sin + (size_t)(warp + kRecWarps * j) * D + RPL * lane);
+        for (int j = 0; j < CPW; ++j) vload_h<RPL>(S[j], Sin + (size_t)(warp + kRecWarps * j) * D + RPL * lane);
+    } else {
+        const float *Sin = a.state_in + ((size_t)seq * a.n_heads + h) * D * D + row0;
+#pragma unroll
+        for (int j = 0; j < CPW; ++j) vload<RPL>(S[j], Sin + (size_t)(warp + kRecWarps * j) * D + RPL * lane);
+    }
 
     if (LAYER) {
         grid_dep_launch_dependents();
@@ -281,9 +326,15 @@ recurrent_kernel(RecArgs a) {
         __syncthreads();   // s_q/s_k/s_vp/s_red reused by the next token
     }
 
-    float *Sout = a.state_out + ((size_t)seq * a.n_heads + h) * D * D + row0;
+    if constexpr (SH) {
+        __half *Sout = a.state_out16 + ((size_t)seq * a.n_heads + h) * D * D + row0;
 #pragma unroll
-    for (int j = 0; j < CPW; ++j) vstore<RPL>(Sout + (size_t)(warp + kRecWarps * j) * D + RPL * lane, S[j]);
+        for (int j = 0; j < CPW; ++j) vstore_h<RPL>(Sout + (size_t)(warp + kRecWarps * j) * D + RPL * lane, S[j]);
+    } else {
+        float *Sout = a.state_out + ((size_t)seq * a.n_heads + h) * D * D + row0;
+#pragma unroll
+        for (int j = 0; j < CPW; ++j) vstore<RPL>(Sout + (size_t)(warp + kRecWarps * j) * D + RPL * lane, S[j]);
+    }
     if (LAYER && CS > 1) {
         // No CTA leaves while a cluster peer may still read its s_part. Only
         // shared-memory lifetime is at stake, so the arrive is relaxed: it
@@ -347,7 +398,7 @@ int launch_rec(const RecArgs &a, int64_t head_dim, cudaStream_t stream) {
 }
 
 // Layer-mode launch: a cluster of D/RB CTAs per head, programmatic dependent.
-template <int RB>
+template <int RB, bool SH = false>
 int launch_layer_rec(const RecArgs &a, cudaStream_t stream) {
     const int64_t heads = a.n_seqs * a.n_heads;
     cudaLaunchConfig_t cfg = {};
@@ -364,7 +415,13 @@ int launch_layer_rec(const RecArgs &a, cudaStream_t stream) {
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return (int)cudaLaunchKernelEx(&cfg, recurrent_kernel<128, true, RB>, a);
+    return (int)cudaLaunchKernelEx(&cfg, recurrent_kernel<128, true, RB, SH>, a);
+}
+
+int launch_layer_rec_any(const RecArgs &a, int rb, bool sh, cudaStream_t s) {
+    if (sh) return rb == 32 ? launch_layer_rec<32, true>(a, s) : rb == 64 ? launch_layer_rec<64, true>(a, s)
+                                                                       : launch_layer_rec<128, true>(a, s);
+    return rb == 32 ? launch_layer_rec<32>(a, s) : rb == 64 ? launch_layer_rec<64>(a, s) : launch_layer_rec<128>(a, s);
 }
 
 }  // namespace
@@ -464,10 +521,13 @@ size_t li_deltanet_layer_workspace_size(const li_deltanet_layer *L, int n_seqs) 
            al256(layer_partials_bytes(L, n_seqs));
 }
 
-int li_launch_deltanet_layer_decode(const li_deltanet_layer *L, const float *x, float *y,
-                                    float *conv_state, float *state, int n_seqs, void *workspace,
-                                    size_t workspace_bytes, void *stream) {
-    if (!L || !x || !y || !conv_state || !state || n_seqs < 0) return LI_ERR_BAD_ARG;
+}  // extern "C"
+
+// The layer step; the state is fp32 (`state`) or fp16 (`state16`).
+static int layer_decode(const li_deltanet_layer *L, const float *x, float *y, float *conv_state, float *state,
+                        __half *state16, int n_seqs, void *workspace, size_t workspace_bytes, void *stream) {
+    if (!L || !x || !y || !conv_state || (!state && !state16) || n_seqs < 0) return LI_ERR_BAD_ARG;
+    if (!state) state = reinterpret_cast<float *>(state16);   // alignment check below covers both
     if (n_seqs == 0) return 0;
     if (!L->w_in || !L->conv_w || !L->a_log || !L->dt_bias || !L->norm_w || !L->w_out)
         return LI_ERR_BAD_ARG;
@@ -488,7 +548,8 @@ int li_launch_deltanet_layer_decode(const li_deltanet_layer *L, const float *x, 
     int rc;
 
     RecArgs a = {};
-    a.state_in = state; a.state_out = state;
+    a.state_in = state16 ? nullptr : state; a.state_out = state16 ? nullptr : state;
+    a.state_in16 = state16; a.state_out16 = state16;
     a.n_tokens = 1; a.n_heads = Hv; a.gqa = Hv / Hk; a.n_seqs = n_seqs;
     a.repeat_type = L->repeat_type;
     a.proj = proj; a.NI = NI; a.Hk = Hk; a.C = C;
@@ -509,7 +570,7 @@ int li_launch_deltanet_layer_decode(const li_deltanet_layer *L, const float *x, 
         if ((rc = qgemv_launch(in, n_seqs, s, false))) return rc;
         // 2. recurrence + L2 norm + gated RMSNorm (dependent launch)
         a.o_gated = og;
-        rc = rb == 32 ? launch_layer_rec<32>(a, s) : rb == 64 ? launch_layer_rec<64>(a, s) : launch_layer_rec<128>(a, s);
+        rc = launch_layer_rec_any(a, rb, state16 != nullptr, s);
         if (rc) return rc;
         // 3. out-projection (dependent launch)
         QGemvArgs out = {};
@@ -555,9 +616,26 @@ int li_launch_deltanet_layer_decode(const li_deltanet_layer *L, const float *x, 
         a.zero_out = y;
         a.zero_len = (int64_t)n_seqs * L->hidden;
     }
-    rc = rb == 32 ? launch_layer_rec<32>(a, s) : rb == 64 ? launch_layer_rec<64>(a, s) : launch_layer_rec<128>(a, s);
+    rc = launch_layer_rec_any(a, rb, state16 != nullptr, s);
     if (rc) return rc;
     return tc_gemm_launch(out, s, true);
+}
+
+extern "C" {
+
+int li_launch_deltanet_layer_decode(const li_deltanet_layer *L, const float *x, float *y,
+                                    float *conv_state, float *state, int n_seqs, void *workspace,
+                                    size_t workspace_bytes, void *stream) {
+    if (!state) return LI_ERR_BAD_ARG;
+    return layer_decode(L, x, y, conv_state, state, nullptr, n_seqs, workspace, workspace_bytes, stream);
+}
+
+int li_launch_deltanet_layer_decode_f16state(const li_deltanet_layer *L, const float *x, float *y,
+                                             float *conv_state, void *state, int n_seqs, void *workspace,
+                                             size_t workspace_bytes, void *stream) {
+    if (!state) return LI_ERR_BAD_ARG;
+    return layer_decode(L, x, y, conv_state, nullptr, static_cast<__half *>(state), n_seqs, workspace,
+                        workspace_bytes, stream);
 }
 
 }  // extern "C"

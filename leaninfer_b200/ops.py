@@ -261,9 +261,12 @@ class DeltaNetLayerDecode:
         return self._ws
 
     def step(self, x, y, conv_state, state, workspace=None):
+        """One decode step; a float16 `state` takes the fp16-state entry."""
         n_seqs = x.shape[0]
         ws = workspace if workspace is not None else self.workspace(n_seqs)
-        check(_lib.load().li_launch_deltanet_layer_decode(
+        name = "li_launch_deltanet_layer_decode_f16state" if state.dtype == torch.float16 else \
+            "li_launch_deltanet_layer_decode"
+        check(getattr(_lib.load(), name)(
             ctypes.byref(self.L), _p(x), _p(y), _p(conv_state), _p(state), n_seqs, _p(ws), ws.numel(),
-            _stream()), "li_launch_deltanet_layer_decode")
+            _stream()), name)
         return y

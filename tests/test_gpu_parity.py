@@ -314,6 +314,36 @@ def test_layer_decode_steps(cuda, oracle_mod, wtype, B, hidden, Hk, Hv, repeat_t
         assert_close(N(st), st_ref, TOL, f"state step {step}")
 
 
+@pytest.mark.parametrize("wtype,B,hidden,Hk,Hv", [
+    (12, 2, 1024, 4, 8),           # SIMT projections
+    (8, 5, 1024, 2, 8),            # tensor-core projections
+    (12, 64, 4096, 16, 32),        # the decode workload
+])
+def test_layer_decode_f16_state(cuda, oracle_mod, wtype, B, hidden, Hk, Hv):
+    """fp16 state storage: the oracle's step with its state rounded to fp16
+    after every step (saturated at +-65504). States that round differently
+    differ by one fp16 step (2^-10 relative); 2e-3 normwise allows that."""
+    import torch
+    from leaninfer_b200 import synth
+    r = rng(700 + B + hidden)
+    w = synth.deltanet_layer(r, hidden=hidden, n_k_heads=Hk, n_v_heads=Hv, wtype=wtype)
+    layer = _layer(cuda, w, 0)
+    L, keep = oracle_mod.make_layer(w, repeat_type=0)
+    inp = synth.deltanet_inputs(r, B, w)
+    f16 = lambda a: np.clip(a, -65504, 65504).astype(np.float16).astype(np.float32)
+    cs_ref, st_ref = inp["conv_state"].copy(), f16(inp["state"])
+    cs, st = T(inp["conv_state"], cuda), T(st_ref, cuda).half()
+    for step in range(3):
+        x = (r.standard_normal((B, hidden)) * synth.DELTANET_X_SCALE).astype(np.float32)
+        y = torch.empty(B, hidden, device=cuda)
+        layer.step(T(x, cuda), y, cs, st)
+        y_ref = oracle_mod.deltanet_layer_decode(L, keep, x, cs_ref, st_ref)
+        st_ref[...] = f16(st_ref)
+        assert_close(N(y), y_ref, 2e-3, f"y step {step}")
+        assert_close(N(cs), cs_ref, TOL, f"conv state step {step}")
+        assert_close(N(st.float()), st_ref, 2e-3, f"state step {step}")
+
+
 def test_layer_decode_with_input_norm(cuda, oracle_mod):
     import torch
     from leaninfer_b200 import synth
