@@ -37,8 +37,10 @@
  *                               src0 x f32 [hidden, n_seqs];
  *                               src1 conv state f32 [3, C, n_seqs] (C = 2 Hk D
  *                               + Hv D), updated in place;
- *                               src2 recurrent state f32 [D, D, Hv, n_seqs]
- *                               ([seq][v-head][k][v]), updated in place;
+ *                               src2 recurrent state f32 or f16 [D, D, Hv,
+ *                               n_seqs] ([seq][v-head][k][v]), updated in
+ *                               place (f16: li_launch_deltanet_layer_decode_
+ *                               f16state);
  *                               src3 W_in Q8_0 / Q4_K [hidden, 2 Hk D + 2 Hv D
  *                               + 2 Hv]; src4 conv weights f32 [4, C];
  *                               src5 a_log f32 [Hv]; src6 dt_bias f32 [Hv];

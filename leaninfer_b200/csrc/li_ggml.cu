@@ -31,6 +31,17 @@ bool f32_contiguous(const li_ggml_tensor *t) {
     return true;
 }
 
+// f16, every stride the contiguous one
+bool f16_contiguous(const li_ggml_tensor *t) {
+    if (t->type != LI_GGML_TYPE_F16 || !dims_ok(t)) return false;
+    size_t s = 2;
+    for (int i = 0; i < LI_GGML_MAX_DIMS; ++i) {
+        if (t->ne[i] > 1 && t->nb[i] != s) return false;
+        s *= (size_t)t->ne[i];
+    }
+    return true;
+}
+
 // quantized matrix [k, n] of contiguous rows
 bool quant_matrix(const li_ggml_tensor *t, int64_t k, int64_t n) {
     if ((t->type != LI_GGML_TYPE_Q8_0 && t->type != LI_GGML_TYPE_Q4_K) || !dims_ok(t)) return false;
@@ -63,8 +74,9 @@ int layer_of(const li_ggml_tensor *node, li_deltanet_layer *L, int *n_seqs) {
     const li_ggml_tensor *x = node->src[0], *cs = node->src[1], *st = node->src[2], *win = node->src[3],
                          *cw = node->src[4], *wout = node->src[8], *inw = node->src[9];
     if (!is_quant(win) || !is_quant(wout)) return LI_ERR_UNSUPPORTED;
-    if (!f32_contiguous(x) || !f32_contiguous(node) || !f32_contiguous(cs) || !f32_contiguous(st) ||
-        !f32_contiguous(cw))
+    if (st->type != LI_GGML_TYPE_F32 && st->type != LI_GGML_TYPE_F16) return LI_ERR_UNSUPPORTED;
+    if (!f32_contiguous(x) || !f32_contiguous(node) || !f32_contiguous(cs) || !f32_contiguous(cw) ||
+        !(st->type == LI_GGML_TYPE_F32 ? f32_contiguous(st) : f16_contiguous(st)))
         return LI_ERR_BAD_SHAPE;
     const int64_t hidden = x->ne[0], n = rows_of(x);
     const int64_t D = st->ne[0], Hv = st->ne[2], Hk = node->op_params[0];
@@ -159,6 +171,11 @@ int li_ggml_compute_forward(const li_ggml_tensor *node, void *workspace, size_t 
         int n = 0;
         const int rc = layer_of(node, &L, &n);
         if (rc) return rc;
+        if (node->src[2]->type == LI_GGML_TYPE_F16)   // fp16 state storage
+            return li_launch_deltanet_layer_decode_f16state(&L, (const float *)node->src[0]->data,
+                                                            (float *)node->data, (float *)node->src[1]->data,
+                                                            node->src[2]->data, n, workspace, workspace_bytes,
+                                                            stream);
         return li_launch_deltanet_layer_decode(&L, (const float *)node->src[0]->data, (float *)node->data,
                                                (float *)node->src[1]->data, (float *)node->src[2]->data, n,
                                                workspace, workspace_bytes, stream);

@@ -126,6 +126,35 @@ def test_layer_node_workspace_and_checks(lib):
     nd = _layer_node(1024, 4, 8, 128, 2)
     nd.src[7] = ctypes.POINTER(type(nd))()                                            # no gamma
     assert _run(lib, nd) == 2001
+    # an f16 state is accepted with f16 strides (and refused with f32 strides)
+    nd = _layer_node(1024, 4, 8, 128, 2)
+    st = nd.src[2].contents
+    st.type = 1
+    assert _run(lib, nd) == 2002
+    for i, s in enumerate((2, 2 * 128, 2 * 128 * 128, 2 * 128 * 128 * 8)):
+        st.nb[i] = s
+    assert lib.li_ggml_workspace_size(ctypes.byref(nd)) > 0
+    st.type = 30                                                                       # bf16: not a state type
+    assert _run(lib, nd) == 2003
+
+
+def test_nodes_reach_their_entry(lib):
+    """A node that passes every check goes on to its entry's own checks: with
+    the descriptors' addresses misaligned on purpose, the entry answers
+    LI_ERR_MISALIGNED before any launch (so this runs without a GPU)."""
+    from leaninfer_b200 import ggml
+    W, x = _fake_quant(12, 4096, 64, ptr=258), _fake_f32([4096, 2], ptr=258)
+    assert _run(lib, ggml.node(ggml.OP_MUL_MAT, _fake_f32([64, 2], ptr=258), [W, x])) == 2005
+    for st_type in (0, 1):
+        nd = _layer_node(1024, 4, 8, 128, 2)
+        st = nd.src[2].contents
+        if st_type == 1:
+            st.type = 1
+            for i, s in enumerate((2, 2 * 128, 2 * 128 * 128, 2 * 128 * 128 * 8)):
+                st.nb[i] = s
+        st.data = 258                                                                  # state misaligned
+        ws = lib.li_ggml_workspace_size(ctypes.byref(nd))
+        assert lib.li_ggml_compute_forward(ctypes.byref(nd), ctypes.c_void_p(256), ws, None) == 2005
 
 
 # --------------------------------------------------------------------------
