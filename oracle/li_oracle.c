@@ -216,6 +216,24 @@ static void rms_norm_d(const float *x, const float *gamma, double *xn, int K,
 
 static double silu_d(double v) { return v / (1.0 + exp(-v)); }
 
+/* fp32 -> nearest binary16 value (round to nearest even), as __float2half:
+ * the value's fp16 step is found from its exponent. */
+static float fp16_round(float f) {
+    const float a = fabsf(f);
+    float out;
+    if (a >= 65520.0f) {
+        out = INFINITY;
+    } else if (a < 6.103515625e-05f) {     /* subnormal range: step 2^-24 */
+        out = nearbyintf(a * 16777216.0f) / 16777216.0f;
+    } else {
+        int e;
+        frexpf(a, &e);                      /* a = m * 2^e, m in [0.5, 1) */
+        const float step = ldexpf(1.0f, e - 11);
+        out = nearbyintf(a / step) * step;
+    }
+    return signbit(f) ? -out : out;
+}
+
 typedef struct {
     int wtype;
     const uint8_t *W;
@@ -247,6 +265,131 @@ int lio_rms_norm_matmul(int wtype, const float *x, const float *gamma,
     mm_ctx c = {wtype, (const uint8_t *)W, rb, xn, dst, K, N, n_rows};
     parallel_for(N, 16, mm_body, &c);
     free(xn);
+    return 0;
+}
+
+/* ---- ggml-style quantized activations (UNPINNED) ----------------------
+ * ggml's CPU MUL_MAT of a quantized matrix first quantizes the activation
+ * row and takes integer dot products: Q4_K weights against q8_K
+ * activations (256-value blocks, scale 1/iscale with iscale = -127/v where v
+ * is the element of largest magnitude, q = nearest(iscale * x) capped at 127,
+ * 16-value block sums for the min term), Q8_0 weights against q8_0
+ * activations (32-value blocks, d = max|x| / 127 stored as fp16, q =
+ * nearest(x / d) with the fp32 d). Restated from ggml's published
+ * quantize_row_q8_K / quantize_row_q8_0 and vec_dot_q4_K_q8_K /
+ * vec_dot_q8_0_q8_0 arithmetic; no reference test or vector pins ggml's CPU
+ * results, so this variant only measures how far that arithmetic lies from
+ * the exact dot products. The row is RMS-normalised in fp32 first, as
+ * ggml's RMS_NORM + MUL produce it. Block sums are exact integers; the
+ * per-block scaling is in double. */
+static void q8act_row(const double *xn, int K, int qk, int8_t *q, float *d) {
+    for (int b = 0; b < K / qk; ++b) {
+        float xb[256];
+        float amax = 0.f, vmax = 0.f;
+        for (int j = 0; j < qk; ++j) {
+            xb[j] = (float)xn[(size_t)b * qk + j];
+            if (fabsf(xb[j]) > amax) { amax = fabsf(xb[j]); vmax = xb[j]; }
+        }
+        int8_t *qb = q + (size_t)b * qk;
+        if (amax == 0.f) {
+            d[b] = 0.f;
+            memset(qb, 0, (size_t)qk);
+        } else if (qk == 256) {             /* q8_K */
+            const float iscale = -127.f / vmax;
+            for (int j = 0; j < qk; ++j) {
+                long v = lrintf(iscale * xb[j]);
+                qb[j] = (int8_t)(v > 127 ? 127 : v);
+            }
+            d[b] = 1.f / iscale;
+        } else {                            /* q8_0 */
+            const float db = amax / 127.f, id = 1.f / db;
+            for (int j = 0; j < qk; ++j) qb[j] = (int8_t)lrintf(xb[j] * id);
+            d[b] = fp16_round(db);
+        }
+    }
+}
+
+typedef struct {
+    int wtype;
+    const uint8_t *W;
+    size_t rb;
+    const int8_t *q;
+    const float *d;
+    float *dst;
+    int K, N, n_rows;
+} q8_ctx;
+
+static void q8_body(void *cp, int64_t n) {
+    q8_ctx *c = (q8_ctx *)cp;
+    const uint8_t *row = c->W + c->rb * n;
+    for (int r = 0; r < c->n_rows; ++r) {
+        const int8_t *q = c->q + (size_t)r * c->K;
+        const float *d = c->d + (size_t)r * (c->K / (c->wtype == 12 ? 256 : 32));
+        double acc = 0;
+        if (c->wtype == 12) {
+            for (int b = 0; b < c->K / 256; ++b) {
+                const uint8_t *blk = row + 144 * (size_t)b;
+                uint16_t dh, mh;
+                memcpy(&dh, blk, 2);
+                memcpy(&mh, blk + 2, 2);
+                int64_t s_sc = 0, s_mn = 0;
+                for (int j = 0; j < 8; ++j) {
+                    int sc, mn;
+                    q4k_scale_min(blk + 4, j, &sc, &mn);
+                    const uint8_t *src = blk + 16 + 32 * (j / 2);
+                    const int8_t *qj = q + 256 * b + 32 * j;
+                    int64_t dot = 0, sum = 0;
+                    for (int i = 0; i < 32; ++i) {
+                        dot += (int64_t)((src[i] >> ((j & 1) ? 4 : 0)) & 0x0f) * qj[i];
+                        sum += qj[i];
+                    }
+                    s_sc += sc * dot;
+                    s_mn += mn * sum;
+                }
+                acc += (double)lio_fp16_to_fp32(dh) * d[b] * (double)s_sc -
+                       (double)lio_fp16_to_fp32(mh) * d[b] * (double)s_mn;
+            }
+        } else {
+            for (int b = 0; b < c->K / 32; ++b) {
+                const uint8_t *blk = row + 34 * (size_t)b;
+                uint16_t dh;
+                memcpy(&dh, blk, 2);
+                const int8_t *w = (const int8_t *)(blk + 2);
+                int64_t dot = 0;
+                for (int i = 0; i < 32; ++i) dot += (int64_t)w[i] * q[32 * b + i];
+                acc += (double)lio_fp16_to_fp32(dh) * d[b] * (double)dot;
+            }
+        }
+        c->dst[(size_t)r * c->N + n] = (float)acc;
+    }
+}
+
+int lio_rms_norm_matmul_q8act(int wtype, const float *x, const float *gamma,
+                              const void *W, float *dst, int K, int N,
+                              int n_rows, float eps) {
+    const size_t rb = lio_row_bytes(wtype, K);
+    if (!rb || (wtype != 8 && wtype != 12)) return -1;
+    const int qk = wtype == 12 ? 256 : 32;
+    double *xn = (double *)malloc(sizeof(double) * (size_t)K);
+    int8_t *q = (int8_t *)malloc((size_t)K * n_rows);
+    float *d = (float *)malloc(sizeof(float) * (size_t)(K / qk) * n_rows);
+    for (int r = 0; r < n_rows; ++r) {
+        const float *xr = x + (size_t)r * K;
+        if (gamma) {                         /* fp32 RMS_NORM (double sum), then MUL */
+            double sq = 0;
+            for (int i = 0; i < K; ++i) sq += (double)xr[i] * xr[i];
+            const float scale = 1.0f / sqrtf((float)(sq / K) + eps);
+            for (int i = 0; i < K; ++i) xn[i] = (double)((xr[i] * scale) * gamma[i]);
+        } else {
+            for (int i = 0; i < K; ++i) xn[i] = xr[i];
+        }
+        q8act_row(xn, K, qk, q + (size_t)r * K, d + (size_t)r * (K / qk));
+    }
+    q8_ctx c = {wtype, (const uint8_t *)W, rb, q, d, dst, K, N, n_rows};
+    parallel_for(N, 16, q8_body, &c);
+    free(xn);
+    free(q);
+    free(d);
     return 0;
 }
 
@@ -283,29 +426,8 @@ int lio_rms_norm_swiglu(int wtype, const float *x, const float *gamma,
     for (int r = 0; r < n_rows; ++r) {
         double *xr = xn + (size_t)r * K;
         rms_norm_d(x + (size_t)r * K, gamma, xr, K, eps);
-        if (round_xn_f16) {
-            /* fp16 round-to-nearest-even of the fp32 value, as __float2half */
-            for (int i = 0; i < K; ++i) {
-                float f = (float)xr[i];
-                /* exact RNE to binary16 via scaling trick on the fp32 value */
-                uint32_t b;
-                memcpy(&b, &f, 4);
-                uint32_t sign = b & 0x80000000u;
-                float a = fabsf(f);
-                float out;
-                if (a >= 65520.0f) {
-                    out = INFINITY;
-                } else if (a < 6.103515625e-05f) { /* subnormal range: step 2^-24 */
-                    out = nearbyintf(a * 16777216.0f) / 16777216.0f;
-                } else {
-                    int e;
-                    frexpf(a, &e);                  /* a = m * 2^e, m in [0.5,1) */
-                    float step = ldexpf(1.0f, e - 11);
-                    out = nearbyintf(a / step) * step;
-                }
-                xr[i] = sign ? -(double)out : (double)out;
-            }
-        }
+        if (round_xn_f16)
+            for (int i = 0; i < K; ++i) xr[i] = fp16_round((float)xr[i]);
     }
     sw_ctx c = {wtype, (const uint8_t *)Wg, (const uint8_t *)Wu, rb, xn, h, K, N, n_rows};
     parallel_for(N, 16, sw_body, &c);

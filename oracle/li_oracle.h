@@ -28,6 +28,14 @@ int lio_rms_norm_matmul(int wtype, const float *x, const float *gamma,
                         const void *W, float *dst, int K, int N, int n_rows,
                         float eps);
 
+/* The same with ggml-style quantized activations (q8_K for Q4_K weights,
+ * q8_0 for Q8_0) and integer dots; UNPINNED (no reference vector fixes
+ * ggml's CPU results): a measure of that arithmetic's distance from the
+ * exact dots, not a parity target. */
+int lio_rms_norm_matmul_q8act(int wtype, const float *x, const float *gamma,
+                              const void *W, float *dst, int K, int N,
+                              int n_rows, float eps);
+
 /* h[r][n] = silu(<xn, Wg[n]>) * <xn, Wu[n]>. round_xn_f16 rounds xn to fp16
  * before the dots (the reference f16 kernel's behaviour). */
 int lio_rms_norm_swiglu(int wtype, const float *x, const float *gamma,

@@ -56,6 +56,8 @@ def lib() -> ctypes.CDLL:
         L.lio_dequantize.argtypes = [c_int, c_void_p, c_void_p, c_int64]
         L.lio_rms_norm_matmul.argtypes = [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                           c_float]
+        L.lio_rms_norm_matmul_q8act.argtypes = [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                                c_int, c_float]
         L.lio_rms_norm_swiglu.argtypes = [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
                                           c_int, c_int, c_float, c_int]
         L.lio_ffn.argtypes = [c_int] + [c_void_p] * 6 + [c_int, c_int, c_int, c_float]
@@ -103,6 +105,17 @@ def rms_norm_matmul(wtype, x, gamma, W, N, eps=1e-6):
     g = None if gamma is None else _f32(gamma)
     assert lib().lio_rms_norm_matmul(wtype, _ptr(x), _ptr(g), _ptr(np.ascontiguousarray(W)), _ptr(out), K, N,
                                      n_rows, eps) == 0
+    return out
+
+
+def rms_norm_matmul_q8act(wtype, x, gamma, W, N, eps=1e-6):
+    """ggml-style quantized-activation matmul (unpinned; see li_oracle.h)."""
+    x = _f32(np.atleast_2d(x))
+    n_rows, K = x.shape
+    out = np.empty((n_rows, N), np.float32)
+    g = None if gamma is None else _f32(gamma)
+    assert lib().lio_rms_norm_matmul_q8act(wtype, _ptr(x), _ptr(g), _ptr(np.ascontiguousarray(W)), _ptr(out), K,
+                                           N, n_rows, eps) == 0
     return out
 
 
