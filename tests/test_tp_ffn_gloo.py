@@ -1,7 +1,8 @@
 """Two-dimensional FFN sharding (leaninfer_b200/tp_ffn.py) on CPU: the
-block-aligned splits and weight slices reassemble the full matrices, and
-two gloo ranks (the oracle standing in for the device products) produce the
-unsharded FFN's output for their sequences."""
+block-aligned splits and weight slices reassemble the full matrices, two
+gloo ranks (the oracle standing in for the device products) produce the
+unsharded FFN's output for their sequences, and a rank that leaves between
+steps ends the other rank's next step with an error instead of a hang."""
 from __future__ import annotations
 
 import os
@@ -98,3 +99,38 @@ def test_two_ranks_match_unsharded_ffn(tmp_path, wtype):
     y_ref = oracle.ffn(wtype, x, gamma, Wg, Wu, Wd, N, 1e-6)
     err = np.abs(y - y_ref).max() / np.abs(y_ref).max()
     assert err <= 1e-5, err     # partial sums over the two halves of N meet in fp32
+
+
+def _worker_leaves(rank, world, port, out_dir):
+    """Rank 1 leaves after the rendezvous, before the step's collectives;
+    rank 0's step must end with an error inside the group's timeout."""
+    import datetime
+    import time
+
+    import torch
+    import torch.distributed as dist
+    from leaninfer_b200.tp_ffn import tp_ffn_forward
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        return                      # gone between steps: no collective of this rank in flight
+    K, N, wtype, n_total = 256, 1024, 8, 4
+    Wg, Wu, Wd, gamma, x = _weights(wtype, K, N, n_total)
+    shard = shard_ffn(Wg, Wu, Wd, wtype, K, N, world, rank)
+    t0 = time.time()
+    try:
+        tp_ffn_forward(torch.from_numpy(x[:2]), torch.from_numpy(gamma), shard, dist, n_total, OracleCompute(wtype))
+        outcome = "completed"
+    except Exception as e:          # the backend reports the lost peer or the timeout
+        outcome = f"error {type(e).__name__}"
+    with open(os.path.join(out_dir, "outcome.txt"), "w") as f:
+        f.write(f"{outcome} {time.time() - t0:.1f}")
+
+
+def test_lost_rank_ends_the_step_with_an_error(tmp_path):
+    import torch.multiprocessing as mp
+    mp.spawn(_worker_leaves, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    outcome, seconds = (tmp_path / "outcome.txt").read_text().rsplit(" ", 1)
+    assert outcome.startswith("error"), outcome
+    assert float(seconds) < 60
