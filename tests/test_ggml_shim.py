@@ -237,3 +237,17 @@ def test_layer_decode_node(cuda, B):
     assert ggml.compute_forward(nd, ws) == 0
     torch.cuda.synchronize()
     assert torch.equal(y1, y2) and torch.equal(cs1, cs2) and torch.equal(st1, st2)
+
+
+def test_descriptors_of_views_keep_their_strides(lib):
+    """f32_desc reads a tensor's real strides: a transposed view is not
+    contiguous, so the dispatch refuses it rather than reading it as rows."""
+    import torch
+    from leaninfer_b200 import ggml
+    x = torch.zeros(4096, 2).t()                     # [2, 4096] view with strides (1, 2)
+    d = ggml.f32_desc(x)
+    assert (d.ne[0], d.ne[1]) == (4096, 2) and (d.nb[0], d.nb[1]) == (8, 4)
+    W = _fake_quant(12, 4096, 64)
+    assert _run(lib, ggml.node(ggml.OP_MUL_MAT, _fake_f32([64, 2]), [W, d])) == 2002
+    c = ggml.f32_desc(x.contiguous())
+    assert (c.nb[0], c.nb[1]) == (4, 4 * 4096)
