@@ -222,3 +222,21 @@ def deltanet_layer(g: GGUFFile, il: int, *, n_k_heads: int, n_v_heads: int, head
                 w_in=np.ascontiguousarray(w_in), conv_w=f32("conv_w", (C, 4)), a_log=f32("a_log", (Hv,)),
                 dt_bias=f32("dt_bias", (Hv,)), norm_w=f32("norm_w", (D,)),
                 w_out=np.ascontiguousarray(g.raw(out.name)))
+
+
+FFN_NAMES = {"gate": "blk.{il}.ffn_gate.weight", "up": "blk.{il}.ffn_up.weight", "down": "blk.{il}.ffn_down.weight"}
+
+
+def ffn_weights(g: GGUFFile, il: int, names: dict | None = None) -> dict:
+    """The SwiGLU FFN of layer `il` for the FFN entries: Wg, Wu [N rows of K]
+    and Wd [K rows of N] as the file's quantized rows, with K (model width),
+    N (inner width) and the shared weight type."""
+    nm = names or FFN_NAMES
+    tg, tu, td = (g.tensors[nm[k].format(il=il)] for k in ("gate", "up", "down"))
+    wtype = tg.type
+    if wtype not in (8, 12) or tu.type != wtype or td.type != wtype:
+        raise GGUFError(f"layer {il}: FFN matrices must share one quantized type (Q4_K or Q8_0)")
+    K, N = tg.ne[0], tg.ne[1]
+    if tu.ne != (K, N) or td.ne != (N, K):
+        raise GGUFError(f"layer {il}: FFN shapes gate {tg.ne}, up {tu.ne}, down {td.ne} do not match")
+    return dict(wtype=wtype, K=K, N=N, Wg=g.raw(tg.name), Wu=g.raw(tu.name), Wd=g.raw(td.name))

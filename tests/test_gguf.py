@@ -1,8 +1,8 @@
 """GGUF weight loading (leaninfer_b200/gguf_file.py), CPU only: files written
 by gguf-py (the format's reference implementation in this image) read back
 with their metadata, tensor directory and raw blocks intact; malformed files
-rejected; a DeltaNet layer assembled from its GGUF tensors equals the layer
-it was written from."""
+rejected; a DeltaNet layer and an FFN assembled from their GGUF tensors
+equal the weights they were written from."""
 from __future__ import annotations
 
 import numpy as np
@@ -139,3 +139,27 @@ def test_deltanet_layer_from_gguf(tmp_path, oracle_mod):
         outs.append((oracle_mod.deltanet_layer_decode(L, keep, x, cs, st), cs, st))
     for a, b in zip(outs[0], outs[1]):
         assert np.array_equal(a, b)
+
+
+def test_ffn_weights_from_gguf(tmp_path, oracle_mod):
+    from leaninfer_b200 import synth
+    from leaninfer_b200.gguf_file import FFN_NAMES, GGUFError, GGUFFile, ffn_weights
+    r = rng(35)
+    K, N = 256, 512
+    Wg, Wu, Wd = (synth.random_weights(r, 8, N, K), synth.random_weights(r, 8, N, K),
+                  synth.random_weights(r, 8, K, N))
+    Q = gguf.GGMLQuantizationType.Q8_0
+    p = tmp_path / "ffn.gguf"
+    _write(p, [(FFN_NAMES["gate"].format(il=0), Wg, Q), (FFN_NAMES["up"].format(il=0), Wu, Q),
+               (FFN_NAMES["down"].format(il=0), Wd, Q), (FFN_NAMES["down"].format(il=1), Wg, Q),
+               (FFN_NAMES["gate"].format(il=1), Wg, Q), (FFN_NAMES["up"].format(il=1), Wu, Q)])
+    x = r.standard_normal((2, K)).astype(np.float32)
+    gamma = r.uniform(0.5, 1.5, K).astype(np.float32)
+    with GGUFFile(p) as g:
+        f = ffn_weights(g, 0)
+        assert (f["wtype"], f["K"], f["N"]) == (8, K, N)
+        y = oracle_mod.ffn(8, x, gamma, np.ascontiguousarray(f["Wg"]), np.ascontiguousarray(f["Wu"]),
+                           np.ascontiguousarray(f["Wd"]), N)
+        with pytest.raises(GGUFError):
+            ffn_weights(g, 1)                       # down written with the gate's shape
+    assert np.array_equal(y, oracle_mod.ffn(8, x, gamma, Wg, Wu, Wd, N))
