@@ -240,3 +240,25 @@ def ffn_weights(g: GGUFFile, il: int, names: dict | None = None) -> dict:
     if tu.ne != (K, N) or td.ne != (N, K):
         raise GGUFError(f"layer {il}: FFN shapes gate {tg.ne}, up {tu.ne}, down {td.ne} do not match")
     return dict(wtype=wtype, K=K, N=N, Wg=g.raw(tg.name), Wu=g.raw(tu.name), Wd=g.raw(td.name))
+
+
+QKV_NAMES = {"q": "blk.{il}.attn_q.weight", "k": "blk.{il}.attn_k.weight", "v": "blk.{il}.attn_v.weight",
+             "norm": "blk.{il}.attn_norm.weight"}
+
+
+def qkv_weights(g: GGUFFile, il: int, names: dict | None = None) -> dict:
+    """The attention input projections of layer `il` for the fused RMSNorm +
+    Q/K/V entry: Wq, Wk, Wv as the file's quantized rows (one shared type and
+    input width K), their row counts Nq, Nk, Nv, and the RMSNorm weight."""
+    nm = names or QKV_NAMES
+    tq, tk, tv = (g.tensors[nm[k].format(il=il)] for k in ("q", "k", "v"))
+    wtype, K = tq.type, tq.ne[0]
+    if wtype not in (8, 12) or tk.type != wtype or tv.type != wtype:
+        raise GGUFError(f"layer {il}: Q/K/V must share one quantized type (Q4_K or Q8_0)")
+    if any(len(t.ne) != 2 or t.ne[0] != K for t in (tq, tk, tv)):
+        raise GGUFError(f"layer {il}: Q/K/V disagree on the input width")
+    gamma = np.asarray(g.raw(nm["norm"].format(il=il)), dtype=np.float32).reshape(-1)
+    if gamma.shape[0] != K:
+        raise GGUFError(f"layer {il}: the norm weight has {gamma.shape[0]} values, the projections take {K}")
+    return dict(wtype=wtype, K=K, Nq=tq.ne[1], Nk=tk.ne[1], Nv=tv.ne[1], Wq=g.raw(tq.name), Wk=g.raw(tk.name),
+                Wv=g.raw(tv.name), gamma=np.ascontiguousarray(gamma))

@@ -163,3 +163,28 @@ def test_ffn_weights_from_gguf(tmp_path, oracle_mod):
         with pytest.raises(GGUFError):
             ffn_weights(g, 1)                       # down written with the gate's shape
     assert np.array_equal(y, oracle_mod.ffn(8, x, gamma, Wg, Wu, Wd, N))
+
+
+def test_qkv_weights_from_gguf(tmp_path, oracle_mod):
+    from leaninfer_b200 import synth
+    from leaninfer_b200.gguf_file import QKV_NAMES, GGUFError, GGUFFile, qkv_weights
+    r = rng(36)
+    K = 512
+    Ws = {k: synth.random_weights(r, 8, n, K) for k, n in (("q", 512), ("k", 128), ("v", 128))}
+    gamma = r.uniform(0.5, 1.5, K).astype(np.float32)
+    Q = gguf.GGMLQuantizationType.Q8_0
+    p = tmp_path / "qkv.gguf"
+    _write(p, [(QKV_NAMES[k].format(il=2), Ws[k], Q) for k in ("q", "k", "v")] +
+           [(QKV_NAMES["norm"].format(il=2), gamma, None), (QKV_NAMES["norm"].format(il=5), gamma[:256], None)] +
+           [(QKV_NAMES[k].format(il=5), Ws[k], Q) for k in ("q", "k", "v")])
+    x = r.standard_normal((1, K)).astype(np.float32)
+    with GGUFFile(p) as g:
+        f = qkv_weights(g, 2)
+        assert (f["wtype"], f["K"], f["Nq"], f["Nk"], f["Nv"]) == (8, K, 512, 128, 128)
+        assert np.array_equal(f["gamma"], gamma)
+        for k, n in (("q", 512), ("k", 128), ("v", 128)):
+            W = f["W" + k]
+            assert np.array_equal(oracle_mod.rms_norm_matmul(8, x, f["gamma"], np.ascontiguousarray(W), n),
+                                  oracle_mod.rms_norm_matmul(8, x, gamma, Ws[k], n))
+        with pytest.raises(GGUFError):
+            qkv_weights(g, 5)                       # norm weight of the wrong width
