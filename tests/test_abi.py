@@ -140,3 +140,20 @@ def test_layer_projection_path_by_shape(lib):
     NI2 = 2 * 4 * 128 + 2 * 8 * 128 + 16
     assert lib.li_deltanet_layer_workspace_size(ctypes.byref(L2), 2) == al(NI2 * 2 * 4) + al(1024 * 2 * 4)
     assert lib.li_deltanet_layer_workspace_size(ctypes.byref(L2), 3) > al(NI2 * 3 * 4) + al(1024 * 3 * 4)
+
+
+def test_f16_state_layer_entry_checks_before_launch(lib):
+    """The fp16-state layer entry applies the fp32 entry's host checks."""
+    from leaninfer_b200._lib import DeltaNetLayer
+    c = ctypes
+    p = c.c_void_p(256)
+    L = DeltaNetLayer(hidden=1024, n_k_heads=4, n_v_heads=8, head_dim=128, conv_kernel=4, w_in_type=12,
+                      w_out_type=12, w_in=256, conv_w=256, a_log=256, dt_bias=256, norm_w=256, w_out=256)
+    f = lib.li_launch_deltanet_layer_decode_f16state
+    ws = lib.li_deltanet_layer_workspace_size(c.byref(L), 2)
+    assert f(c.byref(L), p, p, p, None, 2, p, ws, None) == 2001                   # no state
+    assert f(c.byref(L), p, p, p, c.c_void_p(258), 2, p, ws, None) == 2005        # misaligned state
+    assert f(c.byref(L), p, p, p, p, 2, None, 0, None) == 2004                    # no workspace
+    assert f(c.byref(L), p, p, p, p, 0, p, ws, None) == 0                         # no sequences: no-op
+    L.head_dim = 64
+    assert f(c.byref(L), p, p, p, p, 2, p, ws, None) == 2003                      # head_dim not built
