@@ -156,9 +156,13 @@ void li_launch_fused_deltanet_recurrent_out_f32(
 
 /* RMSNorm + three fp32 projections sharing one normalised x:
  * dst_ptrs[i][n] = <rmsnorm(x), W_ptrs[i][n]>, i = 0..2, each W [N_OUT, K].
- * W_ptrs and dst_ptrs are HOST arrays of three device pointers (read at
- * launch, so the launch can be graph-captured). The reference exports this
- * symbol as a stub (reference cuda/leaninfer-fused-deltanet.cu:306-327). */
+ * W_ptrs and dst_ptrs are arrays of three device pointers, both in device
+ * memory (as the reference's comment asks, "pass device-side pointer
+ * arrays"; the kernel reads them when it runs, so a captured graph follows
+ * later changes to the arrays) or both in host memory (read at launch).
+ * The side is found with cudaPointerGetAttributes; arrays on different sides
+ * record LI_ERR_BAD_ARG. The reference exports this symbol as a stub
+ * (reference cuda/leaninfer-fused-deltanet.cu:306-327). */
 void li_launch_fused_rms_norm_qkv_f32(
         const float * x, const float * gamma,
         const float * const * W_ptrs,
@@ -182,6 +186,16 @@ int li_device_status(void);
 /* Bytes of one row of k values of type wtype (0 if k is not a multiple of
  * the block size or the type is unknown). */
 size_t li_row_bytes(int wtype, int64_t k);
+
+/* Diagnostic of the bounded device-side waits (no counterpart in the
+ * reference, which has no device-side failure reporting). Launches one small
+ * kernel whose mbarrier wait can never complete, with the library's bounded
+ * wait cut to limit_us microseconds (1 .. 1000000): the wait gives up, the
+ * kernel returns by itself, and the next li_device_status() reports
+ * LI_ERR_TIMEOUT, exactly as when a wait of a real kernel runs out. If
+ * elapsed_ns is not NULL (device memory), the kernel stores how long the wait
+ * ran before giving up. Returns the launch status. */
+int li_selftest_bounded_wait(int limit_us, unsigned long long * elapsed_ns, void * stream);
 
 /* Block decode to fp32 (ggml to_float, as called from reference
  * metal/leaninfer-metal.mm:187-193). Bit-exact with gguf-py's dequantize for
@@ -334,6 +348,70 @@ static inline void li_launch_fused_rms_norm_qkv_f32(
         const float*x,const float*g,const float*const*W,float*const*d,int K,int N,float e,void*s)
         {(void)x;(void)g;(void)W;(void)d;(void)K;(void)N;(void)e;(void)s;}
 static inline int li_get_last_error(void) { return LI_ERR_NO_CUDA; }
+
+/* The additive entries without CUDA: each returns LI_ERR_NO_CUDA (sizes 0),
+ * so a caller compiled without GGML_USE_CUDA still compiles and links. The
+ * row size is host arithmetic and keeps its meaning. */
+static inline int li_device_status(void) { return LI_ERR_NO_CUDA; }
+static inline int li_selftest_bounded_wait(int l, unsigned long long*e, void*s)
+        {(void)l;(void)e;(void)s; return LI_ERR_NO_CUDA;}
+static inline size_t li_row_bytes(int t, int64_t k) {
+    if (k <= 0) return 0;
+    if (t == LI_WTYPE_F32) return (size_t)k * 4;
+    if (t == LI_WTYPE_F16) return (size_t)k * 2;
+    if (t == LI_WTYPE_Q8_0) return (k % 32) ? 0 : (size_t)(k / 32) * 34;
+    if (t == LI_WTYPE_Q4_K) return (k % 256) ? 0 : (size_t)(k / 256) * 144;
+    return 0;
+}
+static inline int li_launch_dequantize(int t, const void*s, float*d, int64_t n, void*st)
+        {(void)t;(void)s;(void)d;(void)n;(void)st; return LI_ERR_NO_CUDA;}
+static inline int li_launch_rms_norm_matmul_q(int t, const float*x, const float*g, const void*W, float*d,
+        int K, int N, int r, float e, void*s)
+        {(void)t;(void)x;(void)g;(void)W;(void)d;(void)K;(void)N;(void)r;(void)e;(void)s; return LI_ERR_NO_CUDA;}
+static inline int li_launch_fused_rms_norm_qkv_q(int t, const float*x, const float*g,
+        const void*wq, const void*wk, const void*wv, float*q, float*k, float*v,
+        int K, int nq, int nk, int nv, int r, float e, void*s)
+        {(void)t;(void)x;(void)g;(void)wq;(void)wk;(void)wv;(void)q;(void)k;(void)v;(void)K;(void)nq;(void)nk;
+         (void)nv;(void)r;(void)e;(void)s; return LI_ERR_NO_CUDA;}
+static inline int li_launch_fused_rms_norm_swiglu_q(int t, const float*x, const float*g,
+        const void*wg, const void*wu, float*h, int K, int N, int r, float e, void*s)
+        {(void)t;(void)x;(void)g;(void)wg;(void)wu;(void)h;(void)K;(void)N;(void)r;(void)e;(void)s;
+         return LI_ERR_NO_CUDA;}
+static inline size_t li_fused_ffn_workspace_size(int K, int N, int r) {(void)K;(void)N;(void)r; return 0;}
+static inline int li_launch_fused_ffn_q(int t, const float*x, const float*g,
+        const void*wg, const void*wu, const void*wd, float*y, int K, int N, int r, float e,
+        void*ws, size_t wb, void*s)
+        {(void)t;(void)x;(void)g;(void)wg;(void)wu;(void)wd;(void)y;(void)K;(void)N;(void)r;(void)e;(void)ws;
+         (void)wb;(void)s; return LI_ERR_NO_CUDA;}
+static inline int li_launch_deltanet_recurrent_f32(const float*q, const float*k, const float*v,
+        const float*g, const float*b, const float*si, float*o, float*so,
+        int64_t hd, int64_t nt, int64_t nh, int64_t gr, int rt, int64_t ns,
+        size_t v1, size_t v2, size_t v3, void*s)
+        {(void)q;(void)k;(void)v;(void)g;(void)b;(void)si;(void)o;(void)so;(void)hd;(void)nt;(void)nh;(void)gr;
+         (void)rt;(void)ns;(void)v1;(void)v2;(void)v3;(void)s; return LI_ERR_NO_CUDA;}
+static inline size_t li_deltanet_layer_workspace_size(const li_deltanet_layer*L, int n)
+        {(void)L;(void)n; return 0;}
+static inline int li_launch_deltanet_layer_decode(const li_deltanet_layer*L, const float*x, float*y,
+        float*cs, float*st, int n, void*ws, size_t wb, void*s)
+        {(void)L;(void)x;(void)y;(void)cs;(void)st;(void)n;(void)ws;(void)wb;(void)s; return LI_ERR_NO_CUDA;}
+static inline int li_launch_deltanet_layer_decode_f16state(const li_deltanet_layer*L, const float*x, float*y,
+        float*cs, void*st, int n, void*ws, size_t wb, void*s)
+        {(void)L;(void)x;(void)y;(void)cs;(void)st;(void)n;(void)ws;(void)wb;(void)s; return LI_ERR_NO_CUDA;}
+static inline int li_launch_deltanet_layer_decode_noalloc(const li_deltanet_layer*L, const float*x, float*y,
+        float*cs, float*st, int n, void*s)
+        {(void)L;(void)x;(void)y;(void)cs;(void)st;(void)n;(void)s; return LI_ERR_NO_CUDA;}
+static inline size_t li_deltanet_chunk_prefill_workspace_size(int T, int hv, int hd)
+        {(void)T;(void)hv;(void)hd; return 0;}
+static inline int li_launch_deltanet_chunk_prefill_bf16(const void*q, const void*k, const void*v,
+        const float*g, const float*b, float*st, float*o, int T, int hk, int hv, int hd, float sc,
+        void*ws, size_t wb, void*s)
+        {(void)q;(void)k;(void)v;(void)g;(void)b;(void)st;(void)o;(void)T;(void)hk;(void)hv;(void)hd;(void)sc;
+         (void)ws;(void)wb;(void)s; return LI_ERR_NO_CUDA;}
+static inline int li_launch_gated_rmsnorm_bf16(const float*o, const float*z, const float*g, void*d, int K,
+        int64_t n, float e, void*s)
+        {(void)o;(void)z;(void)g;(void)d;(void)K;(void)n;(void)e;(void)s; return LI_ERR_NO_CUDA;}
+static inline int li_launch_gemm_bf16_f32(const void*A, const void*W, float*C, int M, int N, int K, void*s)
+        {(void)A;(void)W;(void)C;(void)M;(void)N;(void)K;(void)s; return LI_ERR_NO_CUDA;}
 
 #endif
 

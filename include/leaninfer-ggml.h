@@ -99,12 +99,23 @@ typedef struct li_ggml_tensor {
     void   *data;                               /* device memory */
 } li_ggml_tensor;
 
+#if defined(GGML_USE_CUDA) || defined(GGML_USE_CUBLAS)
+
 /* Workspace bytes the node needs (0 for all but LI_GGML_OP_DELTANET_DECODE). */
 size_t li_ggml_workspace_size(const li_ggml_tensor *node);
 
 /* Runs the node on `stream` (a cudaStream_t); capture-safe like the entries. */
 int li_ggml_compute_forward(const li_ggml_tensor *node, void *workspace, size_t workspace_bytes,
                             void *stream);
+
+#else  /* no CUDA: the same dual shape as leaninfer-cuda.h */
+
+static inline size_t li_ggml_workspace_size(const li_ggml_tensor *node) { (void)node; return 0; }
+static inline int li_ggml_compute_forward(const li_ggml_tensor *node, void *workspace, size_t workspace_bytes,
+                                          void *stream)
+        {(void)node;(void)workspace;(void)workspace_bytes;(void)stream; return LI_ERR_NO_CUDA;}
+
+#endif
 
 #ifdef __cplusplus
 }

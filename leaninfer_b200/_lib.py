@@ -73,6 +73,7 @@ _SIGS = {
     # additive entries (int status)
     "li_device_status": (c_int, []),
     "li_row_bytes": (c_size_t, [c_int, c_int64]),
+    "li_selftest_bounded_wait": (c_int, [c_int, c_void_p, c_void_p]),
     "li_launch_dequantize": (c_int, [c_int, c_void_p, c_void_p, c_int64, c_void_p]),
     "li_launch_rms_norm_matmul_q": (
         c_int, [c_int] + [c_void_p] * 4 + [c_int, c_int, c_int, c_float, c_void_p]),

@@ -9,6 +9,7 @@ int li_tu_status_deltanet(int clear);
 int li_tu_status_tcgemm(int clear);
 int li_tu_status_prefill(int clear);
 int li_tu_status_gemm_bf16(int clear);
+int li_tu_status_selftest(int clear);
 
 namespace li {
 
@@ -72,6 +73,7 @@ int li_device_status(void) {
     if ((v = li_tu_status_tcgemm(1)) && !s) s = v;
     if ((v = li_tu_status_prefill(1)) && !s) s = v;
     if ((v = li_tu_status_gemm_bf16(1)) && !s) s = v;
+    if ((v = li_tu_status_selftest(1)) && !s) s = v;
     return s;
 }
 

@@ -137,17 +137,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait for phase `parity` of `bar`. Returns false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+// Wait for phase `parity` of `bar` for at most limit_ns of %globaltimer.
+// On timeout it raises LI_ERR_TIMEOUT on the device flag and returns false.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t parity, unsigned long long limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = global_ns();
     while (!mbar_try_wait(bar, parity)) {
-        if (global_ns() - t0 > kWaitNs) {
+        if (global_ns() - t0 > limit_ns) {
             atomicExch(&g_device_error, LI_ERR_TIMEOUT);
             return false;
         }
     }
     return true;
+}
+
+// Bounded wait (kWaitNs) for phase `parity` of `bar`. Returns false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    return mbar_wait_for(bar, parity, kWaitNs);
 }
 
 // Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned)

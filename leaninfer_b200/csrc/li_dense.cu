@@ -191,6 +191,44 @@ dense_gemv_kernel(DenseArgs a) {
     }
 }
 
+// li_launch_fused_rms_norm_qkv_f32 with W_ptrs / dst_ptrs in device memory
+// (the reference's comment at cuda/leaninfer-fused-deltanet.cu:304-317 asks
+// callers for device-side pointer arrays): the kernel reads the six pointers
+// when it runs, so a graph replay sees the arrays' contents at replay time.
+// Alignment is known only then, so each row picks the vector or scalar loop;
+// a null pointer makes the CTA skip its work and raise LI_ERR_BAD_ARG on the
+// device flag.
+__global__ void __launch_bounds__(kDenseThreads)
+dense_qkv_devptr_kernel(const float *x, const float *gamma, const float *const *W_ptrs, float *const *dst_ptrs,
+                        int N, int K, float eps) {
+    extern __shared__ float4 smem4[];
+    float *xs = reinterpret_cast<float *>(smem4);
+    __shared__ float red[kDenseWarps];
+    const float *W[3];
+    float *dst[3];
+    bool ok = true, vec = (K & 3) == 0;
+#pragma unroll
+    for (int m = 0; m < 3; ++m) {
+        W[m] = W_ptrs[m];
+        dst[m] = dst_ptrs[m];
+        ok = ok && W[m] && dst[m];
+        vec = vec && ((uintptr_t)W[m] & 15u) == 0;
+    }
+    if (!ok) {
+        if (threadIdx.x == 0) atomicExch(&g_device_error, LI_ERR_BAD_ARG);
+        return;
+    }
+    rmsnorm_to_smem(x, gamma, xs, K, eps, false, red);
+    const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+    const int stride = gridDim.x * kDenseWarps;
+    for (int row = blockIdx.x * kDenseWarps + warp; row < 3 * N; row += stride) {
+        const int m = row / N, r = row - m * N;
+        const float *w = (m == 0 ? W[0] : m == 1 ? W[1] : W[2]) + (size_t)r * K;
+        const float acc = vec ? row_dot_f32<true>(w, xs, K, lane) : row_dot_f32<false>(w, xs, K, lane);
+        if (lane == 0) (m == 0 ? dst[0] : m == 1 ? dst[1] : dst[2])[r] = acc;
+    }
+}
+
 template <typename WT, int MODE, bool VEC>
 int launch_dense_t(const DenseArgs &a, cudaStream_t stream) {
     const size_t smem = (size_t)a.K * sizeof(float);
@@ -291,6 +329,42 @@ void li_launch_fused_rms_norm_qkv_f32(const float *x, const float *gamma,
                                       const float *const *W_ptrs, float *const *dst_ptrs,
                                       int K, int N_OUT, float eps, void *stream) {
     int rc = (!W_ptrs || !dst_ptrs) ? LI_ERR_BAD_ARG : 0;
+    // Where do the two pointer arrays live? Host arrays (pageable or pinned)
+    // are read here, at launch; device (or managed) arrays are read by the
+    // kernel. Both arrays must live on the same side.
+    int on_device = -1;
+    for (const void *arr : {(const void *)W_ptrs, (const void *)dst_ptrs}) {
+        if (rc) break;
+        cudaPointerAttributes attr;
+        int dev_side = 0;
+        if (cudaPointerGetAttributes(&attr, arr) == cudaSuccess)
+            dev_side = attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged;
+        else
+            cudaGetLastError();   // an unknown pointer is a plain host pointer
+        if (on_device >= 0 && on_device != dev_side) rc = LI_ERR_BAD_ARG;
+        on_device = dev_side;
+    }
+    if (!rc && on_device == 1) {
+        if (!x || !gamma || K <= 0 || N_OUT < 0) rc = LI_ERR_BAD_ARG;
+        else if (K > kMaxDenseK) rc = LI_ERR_BAD_SHAPE;
+        if (!rc && N_OUT > 0) {
+            const size_t smem = (size_t)K * sizeof(float);
+            if (smem > 48 * 1024) {
+                const cudaError_t e = cudaFuncSetAttribute(dense_qkv_devptr_kernel,
+                                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+                if (e != cudaSuccess) rc = (int)e;
+            }
+            if (!rc) {
+                const int want = (3 * N_OUT + kDenseWarps - 1) / kDenseWarps;
+                const int grid = want < num_sms() * 4 ? want : num_sms() * 4;
+                dense_qkv_devptr_kernel<<<grid, kDenseThreads, smem, (cudaStream_t)stream>>>(
+                    x, gamma, W_ptrs, dst_ptrs, N_OUT, K, eps);
+                rc = launch_status();
+            }
+        }
+        set_last_error(rc);
+        return;
+    }
     DenseArgs a = {};
     if (!rc) {
         a.x = x; a.gamma = gamma; a.n_mat = 3; a.K = K; a.eps = eps;

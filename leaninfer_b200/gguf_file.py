@@ -257,7 +257,13 @@ def qkv_weights(g: GGUFFile, il: int, names: dict | None = None) -> dict:
         raise GGUFError(f"layer {il}: Q/K/V must share one quantized type (Q4_K or Q8_0)")
     if any(len(t.ne) != 2 or t.ne[0] != K for t in (tq, tk, tv)):
         raise GGUFError(f"layer {il}: Q/K/V disagree on the input width")
-    gamma = np.asarray(g.raw(nm["norm"].format(il=il)), dtype=np.float32).reshape(-1)
+    tn = g.tensors[nm["norm"].format(il=il)]
+    if tn.type == 0:                    # F32
+        gamma = np.asarray(g.raw(tn.name), dtype=np.float32).reshape(-1)
+    elif tn.type == 1:                  # F16, widened exactly
+        gamma = np.asarray(g.raw(tn.name)).astype(np.float32).reshape(-1)
+    else:
+        raise GGUFError(f"layer {il}: the norm weight has ggml type {tn.type}; F32 or F16 expected")
     if gamma.shape[0] != K:
         raise GGUFError(f"layer {il}: the norm weight has {gamma.shape[0]} values, the projections take {K}")
     return dict(wtype=wtype, K=K, Nq=tq.ne[1], Nk=tk.ne[1], Nv=tv.ne[1], Wq=g.raw(tq.name), Wk=g.raw(tk.name),

@@ -83,13 +83,23 @@ def rms_norm_swiglu_f16(x, gamma, W_gate, W_up, eps: float = 1e-6):
     return h
 
 
-def rms_norm_qkv_f32(x, gamma, Ws, eps: float = 1e-6):
+def rms_norm_qkv_f32(x, gamma, Ws, eps: float = 1e-6, device_arrays: bool = False):
+    """device_arrays: pass W_ptrs / dst_ptrs as arrays in device memory (the
+    form the reference's comment prescribes) instead of host arrays."""
     N, K = Ws[0].shape
     outs = [torch.empty(N, device=x.device, dtype=torch.float32) for _ in range(3)]
-    wp = (ctypes.c_void_p * 3)(*[_p(w) for w in Ws])
-    dp = (ctypes.c_void_p * 3)(*[_p(o) for o in outs])
+    if device_arrays:
+        wt = torch.tensor([_p(w) for w in Ws], dtype=torch.int64, device=x.device)
+        dt = torch.tensor([_p(o) for o in outs], dtype=torch.int64, device=x.device)
+        wp = ctypes.cast(ctypes.c_void_p(wt.data_ptr()), ctypes.POINTER(ctypes.c_void_p))
+        dp = ctypes.cast(ctypes.c_void_p(dt.data_ptr()), ctypes.POINTER(ctypes.c_void_p))
+    else:
+        wp = (ctypes.c_void_p * 3)(*[_p(w) for w in Ws])
+        dp = (ctypes.c_void_p * 3)(*[_p(o) for o in outs])
     _lib.load().li_launch_fused_rms_norm_qkv_f32(_p(x), _p(gamma), wp, dp, K, N, eps, _stream())
     _legacy_check("li_launch_fused_rms_norm_qkv_f32")
+    if device_arrays:
+        torch.cuda.current_stream().synchronize()   # the pointer arrays must outlive the launch
     return tuple(outs)
 
 

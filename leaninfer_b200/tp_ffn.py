@@ -36,6 +36,10 @@ def ffn_split(N: int, wtype: int, world: int, rank: int) -> tuple[int, int]:
     blk = BLOCK[wtype][0]
     if N % blk:
         raise ValueError(f"N = {N} is not a multiple of the {blk}-value block")
+    if world > N // blk:
+        # a rank with an empty range would call the entries with N = 0 and fail
+        # between the collectives, leaving the other ranks waiting in them
+        raise ValueError(f"{world} ranks cannot each take a block of the {N // blk} blocks of N = {N}")
     b0, nb = shard_bounds(N // blk, world, rank)
     return b0 * blk, (b0 + nb) * blk
 

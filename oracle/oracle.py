@@ -8,6 +8,7 @@ GPU and nothing in leaninfer_b200/ imports it.
 from __future__ import annotations
 
 import ctypes
+import os
 import subprocess
 from ctypes import POINTER, c_float, c_int, c_int64, c_size_t, c_uint16, c_void_p
 from pathlib import Path
@@ -18,7 +19,9 @@ HERE = Path(__file__).resolve().parent
 LIB = HERE / "liboracle.so"
 REF_BENCH = HERE / "_ref" / "libliref_bench.so"
 REF_GPU = HERE / "_ref" / "libliref_gpu.so"
-REF_SRC = Path("/root/reference")
+# The reference checkout, only where it is mounted (never on the GPU box):
+# its sources are compiled where they lie into _ref/.
+REF_SRC = Path(os.environ["LEANINFER_REF_SRC"]) if os.environ.get("LEANINFER_REF_SRC") else None
 
 Q8_0, Q4_K = 8, 12
 
@@ -37,13 +40,16 @@ _lib = None
 
 
 def build(with_ref: bool | None = None) -> None:
-    """make liboracle.so; with_ref (default: when the reference checkout is
-    present) also builds the reference's sources into _ref/."""
+    """make liboracle.so; with_ref (default: when LEANINFER_REF_SRC names an
+    existing reference checkout) also builds the reference's sources into
+    _ref/."""
     subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
     if with_ref is None:
-        with_ref = REF_SRC.exists()
+        with_ref = REF_SRC is not None and REF_SRC.is_dir()
     if with_ref:
-        subprocess.run(["make", "-s", "-C", str(HERE), "ref"], check=True,
+        if REF_SRC is None:
+            raise RuntimeError("LEANINFER_REF_SRC is not set: no reference checkout to build _ref/ from")
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={REF_SRC}"], check=True,
                        stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
 
 

@@ -33,6 +33,21 @@ def max_rel_err(got, ref) -> float:
     return float(np.abs(got - ref).max(initial=0.0) / denom)
 
 
+def elementwise_rel_err(got, ref, floor: float = 1e-3) -> float:
+    """Largest elementwise relative error |got - ref| / |ref| over the
+    elements with |ref| above floor * max|ref| (below that floor an element
+    is the residue of cancellation and its relative error says nothing about
+    the arithmetic)."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    assert got.shape == ref.shape, (got.shape, ref.shape)
+    a = np.abs(ref)
+    m = a > floor * max(a.max(initial=0.0), 1e-30)
+    if not m.any():
+        return 0.0
+    return float((np.abs(got - ref)[m] / a[m]).max())
+
+
 def assert_close(got, ref, tol: float, what: str = "") -> None:
     e = max_rel_err(got, ref)
     assert np.all(np.isfinite(got)), f"{what}: non-finite output"

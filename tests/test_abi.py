@@ -104,6 +104,9 @@ def test_argument_checks_reject_before_launch(lib):
                                                    384, None)
     assert lib.li_get_last_error() == 2003
     assert lib.li_get_last_error() == 0
+    # the bounded-wait diagnostic takes 1 us .. 1 s
+    assert lib.li_selftest_bounded_wait(0, None, None) == 2001
+    assert lib.li_selftest_bounded_wait(1000001, None, None) == 2001
 
 
 def test_layer_workspace_size(lib):

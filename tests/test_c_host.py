@@ -80,3 +80,86 @@ def test_c_program_links_and_calls_the_host_api(tmp_path):
     assert row == 4096 // 32 * 34
     assert ws_layer > 0 and ws_node == ws_layer
     assert bad_shape == 2002 and bad_op == 2003
+
+
+def _declared_names(text: str) -> set[str]:
+    import re
+    return set(re.findall(r"^(?:int|size_t|void)\s+(li_\w+)\(", text, flags=re.M))
+
+
+def _stub_names(text: str) -> set[str]:
+    import re
+    return set(re.findall(r"^static inline (?:int|size_t|void)\s+(li_\w+)\(", text, flags=re.M))
+
+
+def test_every_declared_entry_has_a_no_cuda_stub():
+    """The headers keep the reference's dual shape (reference
+    cuda/leaninfer-cuda.h:16, :54-76) for every entry: each function declared
+    for CUDA builds has a static inline stand-in for builds without it."""
+    for name in ("leaninfer-cuda.h", "leaninfer-ggml.h"):
+        text = (ROOT / "include" / name).read_text()
+        decl, stubs = _declared_names(text), _stub_names(text)
+        assert decl, name
+        assert decl == stubs, (name, sorted(decl ^ stubs))
+
+
+NO_CUDA_SRC = r"""
+#include <stdio.h>
+#include "leaninfer-ggml.h"
+
+int main(void) {
+    int bad = 0;
+    float f = 0.f;
+    li_deltanet_layer L = {0};
+    li_ggml_tensor node = {0};
+    /* the reference entries are no-ops and report LI_ERR_NO_CUDA */
+    li_launch_fused_rms_norm_matmul_f32(&f, &f, &f, &f, 1, 1, 1e-6f, NULL);
+    li_launch_fused_rms_norm_swiglu_f32(&f, &f, &f, &f, &f, 1, 1, 1e-6f, NULL);
+    li_launch_fused_rms_norm_swiglu_f16(&f, &f, &f, &f, &f, 1, 1, 1e-6f, NULL);
+    li_launch_fused_rms_norm_silu_gate_f32(&f, &f, &f, &f, 1, 1, 1e-6f, NULL);
+    li_launch_fused_deltanet_recurrent_out_f32(&f, &f, &f, &f, &f, &f, &f, &f, &f, 128, 1, 1, 1, 0, 1, 1,
+                                               0, 0, 0, NULL);
+    li_launch_fused_rms_norm_qkv_f32(&f, &f, NULL, NULL, 1, 1, 1e-6f, NULL);
+    bad += li_get_last_error() != LI_ERR_NO_CUDA;
+    /* the additive entries return LI_ERR_NO_CUDA, size queries 0 */
+    bad += li_device_status() != LI_ERR_NO_CUDA;
+    bad += li_row_bytes(LI_WTYPE_Q4_K, 4096) != 16 * 144;
+    bad += li_launch_dequantize(LI_WTYPE_Q8_0, &f, &f, 32, NULL) != LI_ERR_NO_CUDA;
+    bad += li_launch_rms_norm_matmul_q(LI_WTYPE_Q8_0, &f, &f, &f, &f, 32, 1, 1, 1e-6f, NULL) != LI_ERR_NO_CUDA;
+    bad += li_launch_fused_rms_norm_qkv_q(LI_WTYPE_Q8_0, &f, &f, &f, &f, &f, &f, &f, &f, 32, 1, 1, 1, 1, 1e-6f,
+                                          NULL) != LI_ERR_NO_CUDA;
+    bad += li_launch_fused_rms_norm_swiglu_q(LI_WTYPE_Q8_0, &f, &f, &f, &f, &f, 32, 1, 1, 1e-6f, NULL)
+           != LI_ERR_NO_CUDA;
+    bad += li_fused_ffn_workspace_size(32, 32, 1) != 0;
+    bad += li_launch_fused_ffn_q(LI_WTYPE_Q8_0, &f, &f, &f, &f, &f, &f, 32, 32, 1, 1e-6f, NULL, 0, NULL)
+           != LI_ERR_NO_CUDA;
+    bad += li_launch_deltanet_recurrent_f32(&f, &f, &f, &f, &f, &f, &f, &f, 128, 1, 1, 1, 0, 1, 0, 0, 0, NULL)
+           != LI_ERR_NO_CUDA;
+    bad += li_deltanet_layer_workspace_size(&L, 1) != 0;
+    bad += li_launch_deltanet_layer_decode(&L, &f, &f, &f, &f, 1, NULL, 0, NULL) != LI_ERR_NO_CUDA;
+    bad += li_launch_deltanet_layer_decode_f16state(&L, &f, &f, &f, &f, 1, NULL, 0, NULL) != LI_ERR_NO_CUDA;
+    bad += li_launch_deltanet_layer_decode_noalloc(&L, &f, &f, &f, &f, 1, NULL) != LI_ERR_NO_CUDA;
+    bad += li_deltanet_chunk_prefill_workspace_size(64, 1, 128) != 0;
+    bad += li_launch_deltanet_chunk_prefill_bf16(&f, &f, &f, &f, &f, &f, &f, 64, 1, 1, 128, 1.f, NULL, 0, NULL)
+           != LI_ERR_NO_CUDA;
+    bad += li_launch_gated_rmsnorm_bf16(&f, &f, &f, &f, 4, 1, 1e-6f, NULL) != LI_ERR_NO_CUDA;
+    bad += li_launch_gemm_bf16_f32(&f, &f, &f, 128, 256, 64, NULL) != LI_ERR_NO_CUDA;
+    bad += li_ggml_workspace_size(&node) != 0;
+    bad += li_ggml_compute_forward(&node, NULL, 0, NULL) != LI_ERR_NO_CUDA;
+    printf("%d\n", bad);
+    return bad != 0;
+}
+"""
+
+
+def test_c_program_without_cuda_compiles_against_the_stubs(tmp_path):
+    """A C99 caller of every entry, compiled without GGML_USE_CUDA (a CPU-only
+    ggml build), compiles, links with nothing and gets LI_ERR_NO_CUDA."""
+    src = tmp_path / "nocuda.c"
+    src.write_text(NO_CUDA_SRC)
+    exe = tmp_path / "nocuda"
+    r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-Werror", f"-I{ROOT / 'include'}", str(src),
+                        "-o", str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert out.returncode == 0 and out.stdout.strip() == "0", out.stdout + out.stderr

@@ -176,7 +176,11 @@ def test_qkv_weights_from_gguf(tmp_path, oracle_mod):
     p = tmp_path / "qkv.gguf"
     _write(p, [(QKV_NAMES[k].format(il=2), Ws[k], Q) for k in ("q", "k", "v")] +
            [(QKV_NAMES["norm"].format(il=2), gamma, None), (QKV_NAMES["norm"].format(il=5), gamma[:256], None)] +
-           [(QKV_NAMES[k].format(il=5), Ws[k], Q) for k in ("q", "k", "v")])
+           [(QKV_NAMES[k].format(il=5), Ws[k], Q) for k in ("q", "k", "v")] +
+           [(QKV_NAMES[k].format(il=6), Ws[k], Q) for k in ("q", "k", "v")] +
+           [(QKV_NAMES["norm"].format(il=6), synth.random_weights(r, 8, 1, K).reshape(-1), Q),
+            (QKV_NAMES["norm"].format(il=7), gamma.astype(np.float16), None)] +
+           [(QKV_NAMES[k].format(il=7), Ws[k], Q) for k in ("q", "k", "v")])
     x = r.standard_normal((1, K)).astype(np.float32)
     with GGUFFile(p) as g:
         f = qkv_weights(g, 2)
@@ -188,3 +192,7 @@ def test_qkv_weights_from_gguf(tmp_path, oracle_mod):
                                   oracle_mod.rms_norm_matmul(8, x, gamma, Ws[k], n))
         with pytest.raises(GGUFError):
             qkv_weights(g, 5)                       # norm weight of the wrong width
+        with pytest.raises(GGUFError):
+            qkv_weights(g, 6)                       # a quantized norm weight (K values as Q8_0 blocks)
+        f16 = qkv_weights(g, 7)                     # an F16 norm weight is widened exactly
+        assert np.array_equal(f16["gamma"], gamma.astype(np.float16).astype(np.float32))

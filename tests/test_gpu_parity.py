@@ -84,6 +84,10 @@ def test_dense_matmul_and_swiglu(cuda, oracle_mod, K, N_):
     assert_close(sw16, ref16, TOL, "swiglu f16")
     qkv = ops.rms_norm_qkv_f32(dx, dg, [dWg, dWu, dWg], 1e-6)
     assert_close(N(qkv[1]), oracle_mod.rms_norm_matmul(0, x, gamma, Wu, N_, 1e-6)[0], TOL, "qkv f32")
+    # the same with the pointer arrays in device memory: the same arithmetic, bit for bit
+    qkv_d = ops.rms_norm_qkv_f32(dx, dg, [dWg, dWu, dWg], 1e-6, device_arrays=True)
+    for a, b in zip(qkv, qkv_d):
+        assert np.array_equal(N(a), N(b))
     ref = _ref_gpu()
     if ref is not None and K % 4 == 0:
         # the reference's own kernel on the same device buffers
@@ -93,6 +97,22 @@ def test_dense_matmul_and_swiglu(cuda, oracle_mod, K, N_):
                                                 ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
         torch.cuda.synchronize()
         assert max_rel_err(sw, N(out)) <= TOL
+
+
+def test_qkv_f32_pointer_arrays_on_different_sides_are_refused(cuda):
+    import torch
+    from leaninfer_b200 import _lib
+    lib = _lib.load()
+    x = torch.ones(256, device=cuda)
+    W = torch.zeros(4, 256, device=cuda)
+    out = torch.empty(4, device=cuda)
+    host_w = (ctypes.c_void_p * 3)(*[W.data_ptr()] * 3)
+    dev_d = torch.tensor([out.data_ptr()] * 3, dtype=torch.int64, device=cuda)
+    lib.li_launch_fused_rms_norm_qkv_f32(x.data_ptr(), x.data_ptr(), host_w,
+                                         ctypes.cast(ctypes.c_void_p(dev_d.data_ptr()),
+                                                     ctypes.POINTER(ctypes.c_void_p)),
+                                         256, 4, 1e-6, None)
+    assert lib.li_get_last_error() == 2001
 
 
 def test_silu_gate(cuda, oracle_mod):

@@ -34,6 +34,9 @@ def test_splits_and_slices_reassemble(wtype, world):
     assert np.array_equal(slice_down(Wd, wtype, 0, N), Wd)
     with pytest.raises(ValueError):
         ffn_split(N + 1, wtype, world, 0)
+    # more ranks than blocks: refused before any collective could start
+    with pytest.raises(ValueError):
+        ffn_split(N, wtype, N // blk + 1, 0)
 
 
 class OracleCompute:
