@@ -98,6 +98,42 @@ typedef struct li_deltanet_layer {
     const void  *w_out;     /* [hidden, Hv*D] quantized rows             */
 } li_deltanet_layer;
 
+/*
+ * Gated GQA attention layer for the decode entry (the attention layers of the
+ * hybrid DeltaNet / attention stack; the reference describes them in
+ * docs/ASSESSMENT.md:1077 and :1086-1087 and has no kernel for them).
+ *
+ * In-projection rows, in order (n_rows_in = 2*Hq*D + 2*Hkv*D):
+ *   q [Hq*D] | gate [Hq*D] | k [Hkv*D] | v [Hkv*D]
+ * Per step and sequence s, the new token at position pos[s]:
+ *   p      = W_in . rmsnorm?(x)                 (rmsnorm only if in_norm_w)
+ *   q_h    = rope(rmsnorm(q_h) * q_norm_w)      per q head (norm skipped if NULL)
+ *   k_j    = rope(rmsnorm(k_j) * k_norm_w)      per kv head
+ *            rope: NeoX rotate-half over dims 0..rope_dim-1, angle of pair i
+ *            pos * rope_theta^(-2i/rope_dim)
+ *   K[s][pos][j] = f16(k_j), V[s][pos][j] = f16(v_j)
+ *   o_h    = softmax_t(q_h . K[s][t][j] / sqrt(D)) V[s][t][j],  t = 0..pos,
+ *            j = h / (Hq / Hkv)
+ *   y      = W_out . (o * sigmoid(gate))
+ */
+typedef struct li_attn_layer {
+    int   hidden;        /* model width K of W_in, rows of W_out          */
+    int   n_q_heads;     /* Hq                                            */
+    int   n_kv_heads;    /* Hkv; Hq / Hkv in 1..6 or 8                    */
+    int   head_dim;      /* D; 128 is the only built size                 */
+    int   rope_dim;      /* even, <= D; 0: no rotary embedding            */
+    int   w_in_type;     /* LI_WTYPE_Q4_K or LI_WTYPE_Q8_0                */
+    int   w_out_type;    /* LI_WTYPE_Q4_K or LI_WTYPE_Q8_0                */
+    float rope_theta;    /* base of the rotary frequencies (> 1)          */
+    float in_norm_eps;   /* eps of the optional input RMSNorm             */
+    float qk_norm_eps;   /* eps of the per-head q / k RMSNorm             */
+    const float *in_norm_w; /* [hidden] or NULL: no input RMSNorm         */
+    const void  *w_in;      /* [n_rows_in, hidden] quantized rows          */
+    const float *q_norm_w;  /* [D] or NULL                                 */
+    const float *k_norm_w;  /* [D] or NULL                                 */
+    const void  *w_out;     /* [hidden, Hq*D] quantized rows               */
+} li_attn_layer;
+
 #if defined(GGML_USE_CUDA) || defined(GGML_USE_CUBLAS)
 
 /* ======================================================================
@@ -293,6 +329,19 @@ int li_launch_deltanet_layer_decode_noalloc(const li_deltanet_layer * L,
         const float * x, float * y, float * conv_state, float * state,
         int n_seqs, void * stream);
 
+/* One decode step (one token per sequence) of the gated attention layer
+ * described at li_attn_layer. x, y [n_seqs, hidden] fp32; k_cache and
+ * v_cache are __half [n_seqs][max_ctx][Hkv][D] (token-major, as ggml's KV
+ * cache rows); pos [n_seqs] int32 in device memory, 0 <= pos[s] < max_ctx:
+ * the step writes the new token's k and v at pos[s] and attends over tokens
+ * 0..pos[s]; the caller advances pos between steps. No counterpart among the
+ * reference's kernels. */
+size_t li_attn_layer_workspace_size(const li_attn_layer * L, int n_seqs, int max_ctx);
+int li_launch_attn_layer_decode(const li_attn_layer * L,
+        const float * x, float * y, void * k_cache, void * v_cache,
+        const int32_t * pos, int n_seqs, int max_ctx,
+        void * workspace, size_t workspace_bytes, void * stream);
+
 /* Chunked (WY form, chunk 64) gated delta rule prefill of one sequence of T
  * tokens on the tensor cores (bf16 operands, fp32 accumulation and state).
  * No counterpart in the reference (its prefill is the upstream per-token
@@ -400,6 +449,12 @@ static inline int li_launch_deltanet_layer_decode_f16state(const li_deltanet_lay
 static inline int li_launch_deltanet_layer_decode_noalloc(const li_deltanet_layer*L, const float*x, float*y,
         float*cs, float*st, int n, void*s)
         {(void)L;(void)x;(void)y;(void)cs;(void)st;(void)n;(void)s; return LI_ERR_NO_CUDA;}
+static inline size_t li_attn_layer_workspace_size(const li_attn_layer*L, int n, int c)
+        {(void)L;(void)n;(void)c; return 0;}
+static inline int li_launch_attn_layer_decode(const li_attn_layer*L, const float*x, float*y, void*kc, void*vc,
+        const int32_t*p, int n, int c, void*ws, size_t wb, void*s)
+        {(void)L;(void)x;(void)y;(void)kc;(void)vc;(void)p;(void)n;(void)c;(void)ws;(void)wb;(void)s;
+         return LI_ERR_NO_CUDA;}
 static inline size_t li_deltanet_chunk_prefill_workspace_size(int T, int hv, int hd)
         {(void)T;(void)hv;(void)hd; return 0;}
 static inline int li_launch_deltanet_chunk_prefill_bf16(const void*q, const void*k, const void*v,

@@ -47,6 +47,18 @@ class DeltaNetLayer(ctypes.Structure):
     ]
 
 
+class AttnLayer(ctypes.Structure):
+    """Mirror of ``li_attn_layer``."""
+
+    _fields_ = [
+        ("hidden", c_int), ("n_q_heads", c_int), ("n_kv_heads", c_int), ("head_dim", c_int),
+        ("rope_dim", c_int), ("w_in_type", c_int), ("w_out_type", c_int),
+        ("rope_theta", c_float), ("in_norm_eps", c_float), ("qk_norm_eps", c_float),
+        ("in_norm_w", c_void_p), ("w_in", c_void_p), ("q_norm_w", c_void_p), ("k_norm_w", c_void_p),
+        ("w_out", c_void_p),
+    ]
+
+
 class GgmlTensor(ctypes.Structure):
     """Mirror of ``li_ggml_tensor`` (include/leaninfer-ggml.h)."""
 
@@ -101,6 +113,9 @@ _SIGS = {
                 c_void_p, c_size_t, c_void_p]),
     "li_launch_deltanet_layer_decode_noalloc": (
         c_int, [POINTER(DeltaNetLayer), c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
+    "li_attn_layer_workspace_size": (c_size_t, [POINTER(AttnLayer), c_int, c_int]),
+    "li_launch_attn_layer_decode": (
+        c_int, [POINTER(AttnLayer)] + [c_void_p] * 5 + [c_int, c_int, c_void_p, c_size_t, c_void_p]),
     # ggml-style node dispatch (include/leaninfer-ggml.h)
     "li_ggml_workspace_size": (c_size_t, [c_void_p]),
     "li_ggml_compute_forward": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),

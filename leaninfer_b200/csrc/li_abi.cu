@@ -10,6 +10,7 @@ int li_tu_status_tcgemm(int clear);
 int li_tu_status_prefill(int clear);
 int li_tu_status_gemm_bf16(int clear);
 int li_tu_status_selftest(int clear);
+int li_tu_status_attn(int clear);
 
 namespace li {
 
@@ -74,6 +75,7 @@ int li_device_status(void) {
     if ((v = li_tu_status_prefill(1)) && !s) s = v;
     if ((v = li_tu_status_gemm_bf16(1)) && !s) s = v;
     if ((v = li_tu_status_selftest(1)) && !s) s = v;
+    if ((v = li_tu_status_attn(1)) && !s) s = v;
     return s;
 }
 

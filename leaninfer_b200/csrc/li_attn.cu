@@ -1,0 +1,472 @@
+// Gated GQA attention layer, one decode step per sequence (the attention
+// layers of the hybrid DeltaNet/attention stack; the reference describes them
+// in docs/ASSESSMENT.md:1077 and :1086-1087 and has no kernel for them).
+//
+// Per sequence s, with the new token at position pos[s]:
+//   p = W_in . rmsnorm?(x)                 rows q [Hq*D] | gate [Hq*D] | k [Hkv*D] | v [Hkv*D]
+//   q_h = rope(rmsnorm(q_h) * q_norm_w),  k_j = rope(rmsnorm(k_j) * k_norm_w)
+//   K[s][pos][j] = f16(k_j), V[s][pos][j] = f16(v_j)
+//   o_h = softmax_t(q_h . K[s][t][j] / sqrt(D)) V[s][t][j],  t = 0..pos, j = h / (Hq/Hkv)
+//   y = W_out . (o * sigmoid(gate))
+//
+// Kernels (one stream, programmatic dependent launches after the first):
+//   projection     the quantized GEMV (SIMT, few rows) or the tcgen05 GEMM, as
+//                  in the DeltaNet layer (li_qgemv.cu / li_tcgemm.cu);
+//   attn_prep      one warp per (sequence, head): per-head RMSNorm and RoPE of
+//                  q (in place, fp32) and k, k and v rounded to f16 into the
+//                  caches at pos;
+//   attn_decode    split-K decode attention: CTA (chunk, kv head, sequence)
+//                  streams `chunk` cached tokens of one kv head once for all
+//                  Hq/Hkv q heads of its group (K and V rows are read with
+//                  16-byte loads, a half-warp per 256-byte row), online
+//                  softmax per warp, the four warps merged in shared memory,
+//                  and writes (max, sum, o[D]) per q head and chunk;
+//   attn_combine   merges the chunks of each (sequence, head), divides by the
+//                  softmax sum and applies sigmoid(gate);
+//   out-projection the quantized GEMV or tcgen05 GEMM again.
+// HBM-bound: a step reads each cached token's K and V row once per kv head.
+#include "li_common.cuh"
+#include "li_qgemv.cuh"
+#include "li_tcgemm.cuh"
+
+LI_DEFINE_TU_STATUS(attn)
+
+namespace li {
+namespace {
+
+constexpr int kD = 128;              // head_dim (the only built size)
+constexpr int kDecThreads = 128;     // 4 warps per attention CTA
+constexpr int kSub = 16;             // tokens per warp per softmax sub-chunk (2 per iteration)
+constexpr int kPartStride = kD + 4;  // floats per (sequence, head, chunk) record: m, l, pad, pad, o[D]
+
+struct AttnArgs {
+    float *proj;                 // [B][NP]: q | gate | k | v (q rewritten in place by attn_prep)
+    int NP, Hq, Hkv, rope_dim;
+    const float *q_norm_w, *k_norm_w;
+    float eps;
+    double log2_theta;
+    const int *pos;              // [B]
+    __half *k_cache, *v_cache;   // [B][max_ctx][Hkv][D]
+    int max_ctx;
+    int chunk, n_chunk;          // tokens per attention CTA, chunks per sequence (max)
+    float *part;                 // [B][Hq][n_chunk][kPartStride]
+    float *og;                   // [B][Hq*D] gated outputs (fp32)
+    float scale;                 // D^-1/2
+};
+
+// ---------------------------------------------------------------------------
+// attn_prep: warp per (sequence, head slot); slots 0..Hq-1 are q heads,
+// Hq..Hq+Hkv-1 the kv heads (k normalised and rotated, v copied).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) attn_prep_kernel(AttnArgs a, int B) {
+    __shared__ float vec[8][kD];
+    grid_dep_wait();
+    grid_dep_launch_dependents();
+    const int wi = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+    const int slots = a.Hq + a.Hkv;
+    const int gw = blockIdx.x * 8 + wi;
+    if (gw >= B * slots) return;
+    const int s = gw / slots, hs = gw % slots;
+    const int pos = a.pos[s];
+    float *ps = a.proj + (size_t)s * a.NP;
+    const bool is_q = hs < a.Hq;
+    const int j = hs - a.Hq;
+    float *src = is_q ? ps + (size_t)hs * kD : ps + (size_t)2 * a.Hq * kD + (size_t)j * kD;
+    const float *w = is_q ? a.q_norm_w : a.k_norm_w;
+    float v[4];
+    float sq = 0.f;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        v[m] = src[lane + 32 * m];
+        sq = fmaf(v[m], v[m], sq);
+    }
+    if (w) {
+        const float r = rsqrtf(warp_sum(sq) / (float)kD + a.eps);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) v[m] = v[m] * w[lane + 32 * m] * r;
+    }
+#pragma unroll
+    for (int m = 0; m < 4; ++m) vec[wi][lane + 32 * m] = v[m];
+    __syncwarp();
+    const int half = a.rope_dim / 2;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const int i = lane + 32 * m;
+        if (i < a.rope_dim) {
+            const int f = i < half ? i : i - half;   // frequency index
+            // angle in double: pos * theta^(-2f/rope_dim) reaches ~pos radians
+            const double ang = (double)pos * exp2(-(2.0 * f / a.rope_dim) * a.log2_theta);
+            double sn, cs;
+            sincos(ang, &sn, &cs);
+            const float x1 = vec[wi][f], x2 = vec[wi][f + half];
+            v[m] = i < half ? x1 * (float)cs - x2 * (float)sn : x2 * (float)cs + x1 * (float)sn;
+        }
+    }
+    if (is_q) {
+#pragma unroll
+        for (int m = 0; m < 4; ++m) src[lane + 32 * m] = v[m];
+    } else {
+        const size_t off = (((size_t)s * a.max_ctx + pos) * a.Hkv + j) * kD;
+        const float *vs = ps + (size_t)2 * a.Hq * kD + (size_t)a.Hkv * kD + (size_t)j * kD;
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+            a.k_cache[off + lane + 32 * m] = __float2half_rn(v[m]);
+            a.v_cache[off + lane + 32 * m] = __float2half_rn(vs[lane + 32 * m]);
+        }
+    }
+}
+
+__device__ __forceinline__ uint4 ld_nc_u4(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ void h8_to_f(const uint4 u, float (&f)[8]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 t = __half22float2(*reinterpret_cast<const __half2 *>(&w[i]));
+        f[2 * i] = t.x;
+        f[2 * i + 1] = t.y;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// attn_decode: CTA (chunk, kv head j, sequence s), 4 warps. In a warp, lane
+// l works on token (l / 16) of each pair of tokens and on dims 8*(l % 16) ..
+// +7 of it; every q head of the group is held in registers for those dims.
+// ---------------------------------------------------------------------------
+template <int G>
+__global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(AttnArgs a) {
+    __shared__ float sc[4][G][kSub];                 // scores, then probabilities
+    __shared__ float wm[4][G], wl[4][G];
+    __shared__ __align__(16) float wo[4][G][kD];
+    grid_dep_wait();
+    grid_dep_launch_dependents();
+    const int chunk = blockIdx.x, j = blockIdx.y, s = blockIdx.z;
+    const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+    const int hw = lane >> 4, c = lane & 15;
+    const int pos = a.pos[s];
+    const int t0 = chunk * a.chunk;
+    const int t1 = min(t0 + a.chunk, pos + 1);
+    if (t0 >= t1) return;                            // beyond this sequence's context
+    // this warp's tokens: a contiguous quarter of the chunk's range
+    const int per = (t1 - t0 + 3) / 4;
+    const int wb = t0 + warp * per, we = min(wb + per, t1);
+
+    float q[G][8];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const float *qs = a.proj + (size_t)s * a.NP + (size_t)(j * G + g) * kD + 8 * c;
+        const float4 q0 = *reinterpret_cast<const float4 *>(qs), q1 = *reinterpret_cast<const float4 *>(qs + 4);
+        q[g][0] = q0.x * a.scale; q[g][1] = q0.y * a.scale; q[g][2] = q0.z * a.scale; q[g][3] = q0.w * a.scale;
+        q[g][4] = q1.x * a.scale; q[g][5] = q1.y * a.scale; q[g][6] = q1.z * a.scale; q[g][7] = q1.w * a.scale;
+    }
+    float m[G], l[G], o[G][8];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.f;
+#pragma unroll
+        for (int d = 0; d < 8; ++d) o[g][d] = 0.f;
+    }
+    const size_t row_stride = (size_t)a.Hkv * kD;   // halves between consecutive tokens
+    const __half *kbase = a.k_cache + ((size_t)s * a.max_ctx * a.Hkv + j) * kD + 8 * c;
+    const __half *vbase = a.v_cache + ((size_t)s * a.max_ctx * a.Hkv + j) * kD + 8 * c;
+
+    for (int tb = wb; tb < we; tb += kSub) {
+        // scores of kSub tokens (kSub/2 iterations of one token per half-warp)
+        uint4 kr[kSub / 2];
+#pragma unroll
+        for (int it = 0; it < kSub / 2; ++it) {
+            const int t = tb + 2 * it + hw;
+            kr[it] = t < we ? ld_nc_u4(kbase + (size_t)t * row_stride) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int it = 0; it < kSub / 2; ++it) {
+            float kf[8];
+            h8_to_f(kr[it], kf);
+            const int t = tb + 2 * it + hw;
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                float d = 0.f;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) d = fmaf(q[g][e], kf[e], d);
+#pragma unroll
+                for (int off = 8; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+                if (c == g % 16) sc[warp][g][2 * it + hw] = t < we ? d : -INFINITY;
+            }
+        }
+        __syncwarp();
+        // online softmax over the sub-chunk: lane i (< kSub) owns token i
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float sv = sc[warp][g][lane & (kSub - 1)];
+            float cm = sv;
+#pragma unroll
+            for (int off = kSub / 2; off > 0; off >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, off));
+            const float mn = fmaxf(m[g], cm);
+            const float alpha = m[g] == -INFINITY ? 0.f : __expf(m[g] - mn);
+            const float pv = sv == -INFINITY ? 0.f : __expf(sv - mn);
+            float ps = pv;
+#pragma unroll
+            for (int off = kSub / 2; off > 0; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+            l[g] = l[g] * alpha + ps;
+            m[g] = mn;
+#pragma unroll
+            for (int d = 0; d < 8; ++d) o[g][d] *= alpha;
+            __syncwarp();
+            if (lane < kSub) sc[warp][g][lane] = pv;
+        }
+        __syncwarp();
+        // weighted V rows
+        uint4 vr[kSub / 2];
+#pragma unroll
+        for (int it = 0; it < kSub / 2; ++it) {
+            const int t = tb + 2 * it + hw;
+            vr[it] = t < we ? ld_nc_u4(vbase + (size_t)t * row_stride) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int it = 0; it < kSub / 2; ++it) {
+            float vf[8];
+            h8_to_f(vr[it], vf);
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float pw = sc[warp][g][2 * it + hw];
+#pragma unroll
+                for (int d = 0; d < 8; ++d) o[g][d] = fmaf(pw, vf[d], o[g][d]);
+            }
+        }
+        __syncwarp();
+    }
+    // the two half-warps hold different tokens of the same running softmax
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int d = 0; d < 8; ++d) o[g][d] += __shfl_xor_sync(0xffffffffu, o[g][d], 16);
+    if (lane < 16) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            *reinterpret_cast<float4 *>(&wo[warp][g][8 * c]) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
+            *reinterpret_cast<float4 *>(&wo[warp][g][8 * c + 4]) = make_float4(o[g][4], o[g][5], o[g][6], o[g][7]);
+        }
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) { wm[warp][g] = m[g]; wl[warp][g] = l[g]; }
+    }
+    __syncthreads();
+    // merge the 4 warps: thread d of the CTA owns dim d of every head
+    const int d = threadIdx.x;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w][g]);
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const float f = wm[w][g] == -INFINITY ? 0.f : __expf(wm[w][g] - M);
+            L = fmaf(wl[w][g], f, L);
+            O = fmaf(wo[w][g][d], f, O);
+        }
+        float *rec = a.part + (((size_t)s * a.Hq + (size_t)j * G + g) * a.n_chunk + chunk) * kPartStride;
+        rec[4 + d] = O;
+        if (d == 0) { rec[0] = M; rec[1] = L; }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// attn_combine: CTA per (sequence, head), thread per dim.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kD) attn_combine_kernel(AttnArgs a) {
+    grid_dep_wait();
+    grid_dep_launch_dependents();
+    const int s = blockIdx.x / a.Hq, h = blockIdx.x % a.Hq, d = threadIdx.x;
+    const int nch = (a.pos[s] + a.chunk) / a.chunk;   // chunks holding tokens 0..pos
+    const float *rec = a.part + ((size_t)s * a.Hq + h) * a.n_chunk * kPartStride;
+    float M = -INFINITY;
+    for (int c = 0; c < nch; ++c) M = fmaxf(M, rec[(size_t)c * kPartStride]);
+    float L = 0.f, O = 0.f;
+    for (int c = 0; c < nch; ++c) {
+        const float *r = rec + (size_t)c * kPartStride;
+        const float f = __expf(r[0] - M);
+        L = fmaf(r[1], f, L);
+        O = fmaf(r[4 + d], f, O);
+    }
+    const float gate = a.proj[(size_t)s * a.NP + (size_t)a.Hq * kD + (size_t)h * kD + d];
+    a.og[(size_t)s * a.Hq * kD + (size_t)h * kD + d] = O / L * sigmoid(gate);
+}
+
+template <int G>
+int launch_decode(const AttnArgs &a, int B, cudaStream_t s) {
+    return (int)launch_pdl(attn_decode_kernel<G>, dim3((unsigned)a.n_chunk, (unsigned)a.Hkv, (unsigned)B),
+                           dim3(kDecThreads), 0, s, true, a);
+}
+
+int launch_decode_any(int G, const AttnArgs &a, int B, cudaStream_t s) {
+    switch (G) {
+    case 1: return launch_decode<1>(a, B, s);
+    case 2: return launch_decode<2>(a, B, s);
+    case 3: return launch_decode<3>(a, B, s);
+    case 4: return launch_decode<4>(a, B, s);
+    case 5: return launch_decode<5>(a, B, s);
+    case 6: return launch_decode<6>(a, B, s);
+    case 8: return launch_decode<8>(a, B, s);
+    default: return LI_ERR_UNSUPPORTED;
+    }
+}
+
+size_t al256(size_t v) { return (v + 255) / 256 * 256; }
+
+// Tokens per attention CTA: enough CTAs to cover the SMs several times over
+// (about 2048), at least 64 (four warps of one sub-chunk each), at most 1024.
+int pick_chunk(int B, int Hkv, int max_ctx) {
+    const long long want = (long long)B * Hkv * max_ctx / 2048;
+    int c = 64;
+    while (c < 1024 && c < want) c <<= 1;
+    return c;
+}
+
+// Projections on the SIMT GEMVs below kTcMinRows rows, and up to 3 rows when
+// both shapes suit the few-row kernel; on the tensor cores otherwise (the
+// rule of the DeltaNet layer).
+bool attn_simt(const li_attn_layer *L, int n) {
+    if (n < kTcMinRows) return true;
+    return n <= 3 && qgemv_few_rows(L->w_in_type, L->hidden, n) &&
+           qgemv_few_rows(L->w_out_type, L->n_q_heads * L->head_dim, n);
+}
+
+struct AttnWs {
+    size_t proj, part, og, x16, xscale, og16, oscale, partials, total;
+};
+
+AttnWs attn_ws_layout(const li_attn_layer *L, int n, int max_ctx) {
+    AttnWs w = {};
+    const size_t D = L->head_dim, Hq = L->n_q_heads, Hkv = L->n_kv_heads, nn = (size_t)n;
+    const size_t NP = 2 * Hq * D + 2 * Hkv * D;
+    const int chunk = pick_chunk(n, (int)Hkv, max_ctx);
+    const size_t nch = ((size_t)max_ctx + chunk - 1) / chunk;
+    size_t off = 0;
+    w.proj = off; off += al256(NP * nn * 4);
+    w.part = off; off += al256(nn * Hq * nch * kPartStride * 4);
+    w.og = off; off += al256(Hq * D * nn * 4);
+    if (!attn_simt(L, n)) {
+        const size_t nx = (nn + 31) / 32 * 32;
+        w.x16 = off; off += al256((size_t)L->hidden * nx * 2);
+        w.xscale = off; off += al256(nn * 4);
+        w.og16 = off; off += al256(Hq * D * nx * 2);
+        w.oscale = off; off += al256(nn * 4);
+        const size_t pin = tc_gemm_partials_bytes(L->w_in_type, kTcStore, L->hidden, (int)NP, n);
+        const size_t pout = tc_gemm_partials_bytes(L->w_out_type, kTcStore, (int)(Hq * D), L->hidden, n);
+        w.partials = off; off += al256(pin > pout ? pin : pout);
+    }
+    w.total = off;
+    return w;
+}
+
+// One projection y[b] = W . (rmsnorm?(x[b])): SIMT GEMV or prep + tcgen05 GEMM.
+int project(bool simt, int wtype, const void *W, int K, int N, const float *x, const float *gamma, float eps,
+            float *dst, int B, char *ws, const AttnWs &lay, bool first, bool out, cudaStream_t s) {
+    int rc;
+    if (simt) {
+        QGemvArgs g = {};
+        g.wtype = wtype; g.epi = kEpiStore;
+        if ((rc = qgemv_plan(wtype, K, N, kEpiStore, &g.plan))) return rc;
+        g.x = x; g.x_stride = K; g.gamma = gamma; g.K = K; g.eps = eps;
+        g.n_seg = 1; g.W[0] = W; g.seg_rows[0] = N; g.dst[0] = dst; g.dst_stride[0] = N;
+        return qgemv_launch(g, B, s, !first);
+    }
+    TcArgs t = {};
+    t.wtype = wtype; t.epi = kTcStore; t.K = K; t.total_rows = N; t.B = B;
+    t.W[0] = W; t.n_seg = 1; t.seg_rows[0] = N; t.dst[0] = dst; t.dst_stride[0] = N;
+    t.X16 = reinterpret_cast<const __half *>(ws + (out ? lay.og16 : lay.x16));
+    t.xscale = reinterpret_cast<const float *>(ws + (out ? lay.oscale : lay.xscale));
+    t.partials = lay.partials ? reinterpret_cast<float *>(ws + lay.partials) : nullptr;
+    t.x_npad = tc_gemm_x_npad(t);
+    if ((rc = tc_prep_launch(x, K, gamma, eps, B, K, const_cast<__half *>(t.X16), const_cast<float *>(t.xscale), s,
+                             !first, t.x_npad)))
+        return rc;
+    if (tc_gemm_splits_k(t)) {
+        // the K-split CTAs add into dst; ordered after the prep by the stream
+        cudaError_t e = cudaMemsetAsync(dst, 0, (size_t)B * N * sizeof(float), s);
+        if (e != cudaSuccess) return (int)e;
+        return tc_gemm_launch(t, s, false);
+    }
+    return tc_gemm_launch(t, s, true);
+}
+
+}  // namespace
+}  // namespace li
+
+using namespace li;
+
+extern "C" {
+
+size_t li_attn_layer_workspace_size(const li_attn_layer *L, int n_seqs, int max_ctx) {
+    if (!L || n_seqs <= 0 || max_ctx <= 0 || L->n_kv_heads <= 0 || L->head_dim != kD) return 0;
+    return attn_ws_layout(L, n_seqs, max_ctx).total;
+}
+
+int li_launch_attn_layer_decode(const li_attn_layer *L, const float *x, float *y, void *k_cache, void *v_cache,
+                                const int32_t *pos, int n_seqs, int max_ctx, void *workspace,
+                                size_t workspace_bytes, void *stream) {
+    if (!L || !x || !y || !k_cache || !v_cache || !pos || n_seqs < 0 || max_ctx <= 0) return LI_ERR_BAD_ARG;
+    if (n_seqs == 0) return 0;
+    if (!L->w_in || !L->w_out) return LI_ERR_BAD_ARG;
+    if (L->head_dim != kD) return LI_ERR_UNSUPPORTED;
+    const int Hq = L->n_q_heads, Hkv = L->n_kv_heads;
+    if (Hkv <= 0 || Hq <= 0 || Hq % Hkv) return LI_ERR_BAD_SHAPE;
+    const int G = Hq / Hkv;
+    if (G > 8 || G == 7) return LI_ERR_UNSUPPORTED;
+    if (L->rope_dim < 0 || L->rope_dim % 2 || L->rope_dim > kD) return LI_ERR_BAD_SHAPE;
+    if (L->rope_dim > 0 && !(L->rope_theta > 1.0f)) return LI_ERR_BAD_ARG;
+    if ((L->w_in_type != LI_WTYPE_Q4_K && L->w_in_type != LI_WTYPE_Q8_0) ||
+        (L->w_out_type != LI_WTYPE_Q4_K && L->w_out_type != LI_WTYPE_Q8_0))
+        return LI_ERR_UNSUPPORTED;
+    if (!aligned16(x) || !aligned16(y) || !aligned16(k_cache) || !aligned16(v_cache)) return LI_ERR_MISALIGNED;
+    if (L->in_norm_w && !aligned16(L->in_norm_w)) return LI_ERR_MISALIGNED;
+    const AttnWs lay = attn_ws_layout(L, n_seqs, max_ctx);
+    if (!workspace || workspace_bytes < lay.total) return LI_ERR_WORKSPACE;
+    if (!aligned16(workspace)) return LI_ERR_MISALIGNED;
+    char *ws = (char *)workspace;
+    const cudaStream_t s = (cudaStream_t)stream;
+    const int D = kD, NP = 2 * Hq * D + 2 * Hkv * D;
+    const bool simt = attn_simt(L, n_seqs);
+    int rc;
+
+    AttnArgs a = {};
+    a.proj = reinterpret_cast<float *>(ws + lay.proj);
+    a.NP = NP; a.Hq = Hq; a.Hkv = Hkv; a.rope_dim = L->rope_dim;
+    a.q_norm_w = L->q_norm_w; a.k_norm_w = L->k_norm_w; a.eps = L->qk_norm_eps;
+    a.log2_theta = L->rope_dim > 0 ? log2((double)L->rope_theta) : 0.0;
+    a.pos = pos;
+    a.k_cache = static_cast<__half *>(k_cache); a.v_cache = static_cast<__half *>(v_cache);
+    a.max_ctx = max_ctx;
+    a.chunk = pick_chunk(n_seqs, Hkv, max_ctx);
+    a.n_chunk = (max_ctx + a.chunk - 1) / a.chunk;
+    a.part = reinterpret_cast<float *>(ws + lay.part);
+    a.og = reinterpret_cast<float *>(ws + lay.og);
+    a.scale = 1.0f / sqrtf((float)D);
+
+    // 1. input projection (RMSNorm fused); the first kernel is not a dependent launch
+    if ((rc = project(simt, L->w_in_type, L->w_in, L->hidden, NP, x, L->in_norm_w, L->in_norm_eps, a.proj, n_seqs,
+                      ws, lay, true, false, s)))
+        return rc;
+    // 2. per-head norm + RoPE, cache append
+    const int warps = n_seqs * (Hq + Hkv);
+    if ((rc = (int)launch_pdl(attn_prep_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, s, true, a,
+                              n_seqs)))
+        return rc;
+    // 3. split-K attention, 4. merge + output gate
+    if ((rc = launch_decode_any(G, a, n_seqs, s))) return rc;
+    if ((rc = (int)launch_pdl(attn_combine_kernel, dim3((unsigned)(n_seqs * Hq)), dim3(kD), 0, s, true, a)))
+        return rc;
+    // 5. output projection
+    return project(simt, L->w_out_type, L->w_out, Hq * D, L->hidden, a.og, nullptr, 0.f, y, n_seqs, ws, lay, false,
+                   true, s);
+}
+
+}  // extern "C"

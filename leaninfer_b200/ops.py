@@ -15,13 +15,13 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import (LI_WTYPE_Q4_K, LI_WTYPE_Q8_0, DeltaNetLayer, LeanInferError, check)
+from ._lib import (LI_WTYPE_Q4_K, LI_WTYPE_Q8_0, AttnLayer, DeltaNetLayer, LeanInferError, check)
 
 __all__ = [
     "rms_norm_matmul_f32", "rms_norm_swiglu_f32", "rms_norm_swiglu_f16", "rms_norm_qkv_f32",
     "rms_norm_silu_gate_f32", "deltanet_recurrent_out_f32", "deltanet_recurrent_f32",
     "dequantize", "rms_norm_matmul_q", "rms_norm_qkv_q", "rms_norm_swiglu_q", "ffn_q",
-    "DeltaNetLayerDecode", "device_status", "row_bytes", "LI_WTYPE_Q8_0", "LI_WTYPE_Q4_K",
+    "DeltaNetLayerDecode", "AttnLayerDecode", "device_status", "row_bytes", "LI_WTYPE_Q8_0", "LI_WTYPE_Q4_K",
 ]
 
 
@@ -279,4 +279,41 @@ class DeltaNetLayerDecode:
         check(getattr(_lib.load(), name)(
             ctypes.byref(self.L), _p(x), _p(y), _p(conv_state), _p(state), n_seqs, _p(ws), ws.numel(),
             _stream()), name)
+        return y
+
+
+class AttnLayerDecode:
+    """One gated attention layer's device weights plus a workspace, stepping
+    B sequences one token at a time through li_launch_attn_layer_decode
+    against caller-owned fp16 KV caches [B, max_ctx, Hkv, D]."""
+
+    def __init__(self, *, hidden, n_q_heads, n_kv_heads, head_dim, w_in, w_out, rope_dim=64,
+                 rope_theta=1e7, in_norm_w=None, q_norm_w=None, k_norm_w=None, w_in_type=LI_WTYPE_Q4_K,
+                 w_out_type=LI_WTYPE_Q4_K, in_norm_eps=1e-6, qk_norm_eps=1e-6):
+        self.keep = [w_in, w_out, in_norm_w, q_norm_w, k_norm_w]
+        self.L = AttnLayer(
+            hidden=hidden, n_q_heads=n_q_heads, n_kv_heads=n_kv_heads, head_dim=head_dim, rope_dim=rope_dim,
+            w_in_type=w_in_type, w_out_type=w_out_type, rope_theta=rope_theta, in_norm_eps=in_norm_eps,
+            qk_norm_eps=qk_norm_eps, in_norm_w=_p(in_norm_w), w_in=_p(w_in), q_norm_w=_p(q_norm_w),
+            k_norm_w=_p(k_norm_w), w_out=_p(w_out))
+        self.device = w_in.device
+        self._ws = None
+
+    def workspace_bytes(self, n_seqs: int, max_ctx: int) -> int:
+        return int(_lib.load().li_attn_layer_workspace_size(ctypes.byref(self.L), n_seqs, max_ctx))
+
+    def workspace(self, n_seqs: int, max_ctx: int) -> torch.Tensor:
+        need = self.workspace_bytes(n_seqs, max_ctx)
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(need, device=self.device, dtype=torch.uint8)
+        return self._ws
+
+    def step(self, x, y, k_cache, v_cache, pos, workspace=None):
+        """One decode step: the new token of sequence s goes to slot pos[s]
+        (an int32 device tensor) of the caches."""
+        n_seqs, max_ctx = x.shape[0], k_cache.shape[1]
+        ws = workspace if workspace is not None else self.workspace(n_seqs, max_ctx)
+        check(_lib.load().li_launch_attn_layer_decode(
+            ctypes.byref(self.L), _p(x), _p(y), _p(k_cache), _p(v_cache), _p(pos), n_seqs, max_ctx, _p(ws),
+            ws.numel(), _stream()), "li_launch_attn_layer_decode")
         return y

@@ -89,3 +89,36 @@ def deltanet_inputs(rng: np.random.Generator, n_seqs: int, layer: dict) -> dict:
         conv_state=np.zeros((n_seqs, C, 3), np.float32),
         state=rng.normal(0.0, 0.02, size=(n_seqs, Hv, D, D)).astype(np.float32),
     )
+
+
+def attn_layer(rng: np.random.Generator, *, hidden=5120, n_q_heads=40, n_kv_heads=8, head_dim=128,
+               rope_dim=64, rope_theta=1e7, wtype=Q4_K) -> dict:
+    """Weights of one gated attention layer (numpy). In-projection rows:
+    q | gate | k | v; out-projection [hidden, Hq*D]. The input RMSNorm weight
+    is U(0.5, 1.5)/128, which puts a random-code Q4_K row dot of the
+    normalised x near N(0, 1) (so the sigmoid gates stay informative); the
+    per-head q / k norm weights are U(0.5, 1.5)."""
+    D, Hq, Hkv = head_dim, n_q_heads, n_kv_heads
+    NP = 2 * Hq * D + 2 * Hkv * D
+    return dict(
+        hidden=hidden, n_q_heads=Hq, n_kv_heads=Hkv, head_dim=D, rope_dim=rope_dim, rope_theta=rope_theta,
+        wtype=wtype, eps=1e-6,
+        w_in=random_weights(rng, wtype, NP, hidden),
+        in_norm_w=(rng.uniform(0.5, 1.5, size=hidden) / 128.0).astype(np.float32),
+        q_norm_w=rng.uniform(0.5, 1.5, size=D).astype(np.float32),
+        k_norm_w=rng.uniform(0.5, 1.5, size=D).astype(np.float32),
+        w_out=random_weights(rng, wtype, hidden, Hq * D),
+    )
+
+
+def attn_inputs(rng: np.random.Generator, n_seqs: int, layer: dict, max_ctx: int, pos=None) -> dict:
+    """x ~ N(0, 1); fp16 KV caches [n, max_ctx, Hkv, D] pre-filled with
+    N(0, 1) keys and values (as uint16 bits); pos[s] (default max_ctx - 1 for
+    every sequence) is the slot the step writes."""
+    Hkv, D = layer["n_kv_heads"], layer["head_dim"]
+    kc = rng.standard_normal((n_seqs, max_ctx, Hkv, D)).astype(np.float16).view(np.uint16)
+    vc = rng.standard_normal((n_seqs, max_ctx, Hkv, D)).astype(np.float16).view(np.uint16)
+    if pos is None:
+        pos = np.full(n_seqs, max_ctx - 1, np.int32)
+    return dict(x=rng.standard_normal((n_seqs, layer["hidden"])).astype(np.float32), k_cache=kc, v_cache=vc,
+                pos=np.asarray(pos, np.int32))

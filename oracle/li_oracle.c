@@ -753,3 +753,127 @@ int lio_gdr_prefill(const uint16_t *q, const uint16_t *k, const uint16_t *v,
     parallel_for(Hv, 1, pf_body, &c);
     return 0;
 }
+
+/* ---------------------------------------------------------------------- */
+/* Gated GQA attention decode layer (no kernel of the reference: the hybrid
+ * stack's attention layers, reference docs/ASSESSMENT.md:1077 and
+ * :1086-1087, "standard grouped-query attention ... RoPE" with a normal KV
+ * cache). The norm is the reference's RMSNorm form
+ * (cuda/leaninfer-fused-ffn.cu:62-83); the output gate sigmoid(gate) and the
+ * per-head q/k RMSNorm follow the Qwen3.5 gated-attention convention, the
+ * RoPE is NeoX rotate-half: choices, not pinned by the reference. */
+
+uint16_t lio_fp32_to_fp16(float f) {
+    const float r = fp16_round(f);
+    uint32_t b;
+    memcpy(&b, &r, 4);
+    const uint16_t sign = (uint16_t)((b >> 16) & 0x8000u);
+    const float a = fabsf(r);
+    if (isnan(f)) return (uint16_t)(sign | 0x7e00u);
+    if (isinf(a)) return (uint16_t)(sign | 0x7c00u);
+    if (a == 0.0f) return sign;
+    if (a < 6.103515625e-05f) return (uint16_t)(sign | (uint16_t)(a * 16777216.0f));   /* subnormal: m * 2^-24 */
+    int e;
+    const float m = frexpf(a, &e);            /* a = m * 2^e, m in [0.5, 1) */
+    const uint16_t ebits = (uint16_t)(e - 1 + 15);
+    const uint16_t mbits = (uint16_t)((m * 2.0f - 1.0f) * 1024.0f);
+    return (uint16_t)(sign | (ebits << 10) | mbits);
+}
+
+static void head_rms_rope(double *v, const float *w, int D, float eps, int rope_dim, double theta, int pos) {
+    if (w) {
+        double sq = 0;
+        for (int i = 0; i < D; ++i) sq += v[i] * v[i];
+        const double r = 1.0 / sqrt(sq / D + (double)eps);
+        for (int i = 0; i < D; ++i) v[i] = v[i] * w[i] * r;
+    }
+    const int half = rope_dim / 2;
+    for (int i = 0; i < half; ++i) {
+        const double ang = (double)pos * pow(theta, -2.0 * i / rope_dim);
+        const double c = cos(ang), sn = sin(ang);
+        const double x1 = v[i], x2 = v[i + half];
+        v[i] = x1 * c - x2 * sn;
+        v[i + half] = x2 * c + x1 * sn;
+    }
+}
+
+typedef struct {
+    const lio_attn_layer *L;
+    const float *p;            /* [n][NP] projections */
+    const uint16_t *kc, *vc;
+    const int32_t *pos;
+    float *og;                 /* [n][Hq*D] */
+    int NP, max_ctx;
+} attn_ctx;
+
+static double sigmoid_d(double v) { return 1.0 / (1.0 + exp(-v)); }
+
+static void attn_head_body(void *cp, int64_t idx) {
+    attn_ctx *c = (attn_ctx *)cp;
+    const lio_attn_layer *L = c->L;
+    const int D = L->head_dim, Hq = L->n_q_heads, Hkv = L->n_kv_heads;
+    const int s = (int)(idx / Hq), h = (int)(idx % Hq), j = h / (Hq / Hkv);
+    const int pos = c->pos[s];
+    const float *ps = c->p + (size_t)s * c->NP;
+    double *q = (double *)malloc(sizeof(double) * D);
+    double *acc = (double *)calloc(D, sizeof(double));
+    double *sc = (double *)malloc(sizeof(double) * (pos + 1));
+    for (int i = 0; i < D; ++i) q[i] = ps[h * D + i];
+    head_rms_rope(q, L->q_norm_w, D, L->qk_norm_eps, L->rope_dim, L->rope_theta, pos);
+    const double scale = 1.0 / sqrt((double)D);
+    double mx = -INFINITY;
+    for (int t = 0; t <= pos; ++t) {
+        const uint16_t *kr = c->kc + (((size_t)s * c->max_ctx + t) * Hkv + j) * D;
+        double d = 0;
+        for (int i = 0; i < D; ++i) d += q[i] * lio_fp16_to_fp32(kr[i]);
+        sc[t] = d * scale;
+        if (sc[t] > mx) mx = sc[t];
+    }
+    double l = 0;
+    for (int t = 0; t <= pos; ++t) {
+        const double w = exp(sc[t] - mx);
+        l += w;
+        const uint16_t *vr = c->vc + (((size_t)s * c->max_ctx + t) * Hkv + j) * D;
+        for (int i = 0; i < D; ++i) acc[i] += w * lio_fp16_to_fp32(vr[i]);
+    }
+    const float *gate = ps + (size_t)Hq * D + h * D;
+    for (int i = 0; i < D; ++i)
+        c->og[(size_t)s * Hq * D + h * D + i] = (float)(acc[i] / l * sigmoid_d(gate[i]));
+    free(sc);
+    free(acc);
+    free(q);
+}
+
+int lio_attn_layer_decode(const lio_attn_layer *L, const float *x, float *y,
+                          uint16_t *k_cache, uint16_t *v_cache,
+                          const int32_t *pos, int n_seqs, int max_ctx) {
+    const int D = L->head_dim, Hq = L->n_q_heads, Hkv = L->n_kv_heads, hid = L->hidden;
+    if (Hkv <= 0 || Hq % Hkv || L->rope_dim % 2 || L->rope_dim > D) return -1;
+    const int NP = 2 * Hq * D + 2 * Hkv * D;
+    for (int s = 0; s < n_seqs; ++s)
+        if (pos[s] < 0 || pos[s] >= max_ctx) return -1;
+    float *p = (float *)malloc(sizeof(float) * (size_t)NP * n_seqs);
+    int rc = lio_rms_norm_matmul(L->w_in_type, x, L->in_norm_w, L->w_in, p, hid, NP, n_seqs, L->in_norm_eps);
+    if (rc) { free(p); return rc; }
+    double *kv = (double *)malloc(sizeof(double) * D);
+    for (int s = 0; s < n_seqs; ++s) {      /* the new token's k, v into the caches */
+        const float *ps = p + (size_t)s * NP;
+        for (int j = 0; j < Hkv; ++j) {
+            const size_t off = (((size_t)s * max_ctx + pos[s]) * Hkv + j) * D;
+            for (int i = 0; i < D; ++i) kv[i] = ps[2 * Hq * D + j * D + i];
+            head_rms_rope(kv, L->k_norm_w, D, L->qk_norm_eps, L->rope_dim, L->rope_theta, pos[s]);
+            for (int i = 0; i < D; ++i) {
+                k_cache[off + i] = lio_fp32_to_fp16((float)kv[i]);
+                v_cache[off + i] = lio_fp32_to_fp16(ps[2 * Hq * D + Hkv * D + j * D + i]);
+            }
+        }
+    }
+    free(kv);
+    float *og = (float *)malloc(sizeof(float) * (size_t)Hq * D * n_seqs);
+    attn_ctx ac = {L, p, k_cache, v_cache, pos, og, NP, max_ctx};
+    parallel_for((int64_t)n_seqs * Hq, 1, attn_head_body, &ac);
+    rc = lio_rms_norm_matmul(L->w_out_type, og, NULL, L->w_out, y, Hq * D, hid, n_seqs, 0.f);
+    free(og);
+    free(p);
+    return rc;
+}

@@ -90,6 +90,37 @@ int lio_gdr_prefill(const uint16_t *q, const uint16_t *k, const uint16_t *v,
                     const float *g, const float *beta, float *state, float *o,
                     int T, int Hk, int Hv, int D, float scale);
 
+/* fp32 -> IEEE binary16 bits, round to nearest even (as __float2half_rn). */
+uint16_t lio_fp32_to_fp16(float f);
+
+/* Gated GQA attention layer, one decode step per sequence (the hybrid
+ * stack's attention layers). Weights: w_in [2*Hq*D + 2*Hkv*D, hidden] with
+ * rows q | gate | k | v; w_out [hidden, Hq*D]. KV caches are fp16 bits
+ * [n_seqs][max_ctx][Hkv][D]; pos[s] is the slot of the new token (the number
+ * of tokens already cached). Per sequence:
+ *   p = W_in . rmsnorm?(x)
+ *   q_h = rope(rmsnorm(q_h) * q_norm_w), k_j = rope(rmsnorm(k_j) * k_norm_w)
+ *         (per-head RMSNorm skipped when the weight is NULL; NeoX rotate-half
+ *         RoPE over the first rope_dim dims, angle pos * theta^(-2i/rope_dim))
+ *   K[pos][j] = fp16(k_j), V[pos][j] = fp16(v_j)
+ *   o_h = softmax_t(q_h . K[t][j] / sqrt(D)) V[t][j] over t = 0..pos,
+ *         j = h / (Hq/Hkv), with the fp16 cache values
+ *   y = W_out . (o * sigmoid(gate))
+ * Double precision except the fp32 projection outputs and the fp16 cache. */
+typedef struct lio_attn_layer {
+    int hidden, n_q_heads, n_kv_heads, head_dim, rope_dim;
+    int w_in_type, w_out_type;
+    float rope_theta, in_norm_eps, qk_norm_eps;
+    const float *in_norm_w;
+    const void *w_in;
+    const float *q_norm_w, *k_norm_w;
+    const void *w_out;
+} lio_attn_layer;
+
+int lio_attn_layer_decode(const lio_attn_layer *L, const float *x, float *y,
+                          uint16_t *k_cache, uint16_t *v_cache,
+                          const int32_t *pos, int n_seqs, int max_ctx);
+
 int lio_num_threads(void);
 
 #ifdef __cplusplus

@@ -36,6 +36,16 @@ class Layer(ctypes.Structure):
     ]
 
 
+class AttnLayer(ctypes.Structure):
+    _fields_ = [
+        ("hidden", c_int), ("n_q_heads", c_int), ("n_kv_heads", c_int), ("head_dim", c_int), ("rope_dim", c_int),
+        ("w_in_type", c_int), ("w_out_type", c_int),
+        ("rope_theta", c_float), ("in_norm_eps", c_float), ("qk_norm_eps", c_float),
+        ("in_norm_w", c_void_p), ("w_in", c_void_p), ("q_norm_w", c_void_p), ("k_norm_w", c_void_p),
+        ("w_out", c_void_p),
+    ]
+
+
 _lib = None
 
 
@@ -78,6 +88,9 @@ def lib() -> ctypes.CDLL:
         L.lio_gdr_prefill.argtypes = [c_void_p] * 7 + [c_int, c_int, c_int, c_int, c_float]
         L.lio_fp16_to_fp32.argtypes = [c_uint16]
         L.lio_fp16_to_fp32.restype = c_float
+        L.lio_fp32_to_fp16.argtypes = [c_float]
+        L.lio_fp32_to_fp16.restype = c_uint16
+        L.lio_attn_layer_decode.argtypes = [POINTER(AttnLayer)] + [c_void_p] * 5 + [c_int, c_int]
         L.lio_num_threads.restype = c_int
         _lib = L
     return _lib
@@ -196,6 +209,38 @@ def deltanet_layer_decode(layer, keep, x, conv_state, state, with_taps=False):
     assert lib().lio_deltanet_layer_decode(ctypes.byref(layer), _ptr(x), _ptr(y), _ptr(conv_state),
                                            _ptr(state), n, _ptr(taps)) == 0
     return (y, taps) if with_taps else y
+
+
+def fp32_to_fp16_bits(f: float) -> int:
+    return int(lib().lio_fp32_to_fp16(float(f)))
+
+
+def make_attn_layer(w: dict):
+    """w: synth.attn_layer's dict (weights as numpy, shapes and eps)."""
+    keep = {k: (_f32(v) if isinstance(v, np.ndarray) and v.dtype != np.uint8 else
+                (np.ascontiguousarray(v) if isinstance(v, np.ndarray) else v)) for k, v in w.items()}
+    L = AttnLayer(hidden=w["hidden"], n_q_heads=w["n_q_heads"], n_kv_heads=w["n_kv_heads"], head_dim=w["head_dim"],
+                  rope_dim=w["rope_dim"], w_in_type=w["wtype"], w_out_type=w["wtype"], rope_theta=w["rope_theta"],
+                  in_norm_eps=w["eps"], qk_norm_eps=w["eps"],
+                  in_norm_w=_ptr(keep.get("in_norm_w")), w_in=_ptr(keep["w_in"]),
+                  q_norm_w=_ptr(keep.get("q_norm_w")), k_norm_w=_ptr(keep.get("k_norm_w")),
+                  w_out=_ptr(keep["w_out"]))
+    return L, keep
+
+
+def attn_layer_decode(layer, keep, x, k_cache, v_cache, pos):
+    """One step; the fp16 caches (uint16 [n, max_ctx, Hkv, D]) get the new
+    token's k, v at pos[s]."""
+    x = _f32(np.atleast_2d(x))
+    n = x.shape[0]
+    y = np.empty((n, layer.hidden), np.float32)
+    pos = np.ascontiguousarray(pos, dtype=np.int32)
+    assert k_cache.dtype == np.uint16 and v_cache.dtype == np.uint16
+    assert k_cache.flags["C_CONTIGUOUS"] and v_cache.flags["C_CONTIGUOUS"]
+    max_ctx = k_cache.shape[1]
+    assert lib().lio_attn_layer_decode(ctypes.byref(layer), _ptr(x), _ptr(y), _ptr(k_cache), _ptr(v_cache),
+                                       _ptr(pos), n, max_ctx) == 0
+    return y
 
 
 def gdr_prefill(q_bf16, k_bf16, v_bf16, g, beta, state, scale):
