@@ -52,6 +52,7 @@ enum li_wtype {
 #define LI_ERR_NO_CUDA        2007  /* built without CUDA (stub branch)     */
 #define LI_ERR_SCRATCH_LIMIT  2008  /* the call needs more scratch than the
                                        library's static scratch array holds */
+#define LI_ERR_NCCL           2009  /* an NCCL call of a multi-GPU entry failed */
 
 /* Size of the library's own device scratch used by
  * li_launch_deltanet_layer_decode_noalloc (32 MiB: every batch the tensor-core
@@ -133,6 +134,36 @@ typedef struct li_attn_layer {
     const float *k_norm_w;  /* [D] or NULL                                 */
     const void  *w_out;     /* [hidden, Hq*D] quantized rows               */
 } li_attn_layer;
+
+/* One layer's SwiGLU FFN for the stack entry: y = W_down . (silu(W_gate . xn)
+ * * (W_up . xn)), xn = rmsnorm(x) * norm_w. W_gate, W_up [n_inner, hidden];
+ * W_down [hidden, n_inner]; with the weights sharded across GPUs, n_inner is
+ * this rank's share and W_down holds the matching columns (see
+ * li_launch_ffn_q_tp). */
+typedef struct li_ffn_weights {
+    int   wtype;         /* LI_WTYPE_Q4_K or LI_WTYPE_Q8_0                */
+    int   hidden;
+    int   n_inner;
+    float eps;
+    const float *norm_w;    /* [hidden] (NULL: no RMSNorm)                */
+    const void  *w_gate;
+    const void  *w_up;
+    const void  *w_down;
+} li_ffn_weights;
+
+/* One layer of a hybrid decode stack: a mixer (DeltaNet or gated attention)
+ * with its per-sequence state, followed by an FFN; both with residual adds. */
+#define LI_LAYER_DELTANET 1
+#define LI_LAYER_ATTN     2
+typedef struct li_stack_layer {
+    int kind;                            /* LI_LAYER_DELTANET or LI_LAYER_ATTN */
+    const li_deltanet_layer *deltanet;   /* DELTANET: weights (in_norm_w is the pre-norm) */
+    float *conv_state;                   /* DELTANET: [n_seqs][C][3]               */
+    float *state;                        /* DELTANET: [n_seqs][Hv][D][D]           */
+    const li_attn_layer *attn;           /* ATTN: weights (in_norm_w is the pre-norm) */
+    void  *k_cache, *v_cache;            /* ATTN: __half [n_seqs][max_ctx][Hkv][D] */
+    li_ffn_weights ffn;
+} li_stack_layer;
 
 #if defined(GGML_USE_CUDA) || defined(GGML_USE_CUBLAS)
 
@@ -232,6 +263,10 @@ size_t li_row_bytes(int wtype, int64_t k);
  * elapsed_ns is not NULL (device memory), the kernel stores how long the wait
  * ran before giving up. Returns the launch status. */
 int li_selftest_bounded_wait(int limit_us, unsigned long long * elapsed_ns, void * stream);
+
+/* dst[i] = a[i] + b[i], i < n (fp32; dst may alias a or b): the residual
+ * connection between the layers of a decode stack (ggml ADD). */
+int li_launch_add_f32(float * dst, const float * a, const float * b, int64_t n, void * stream);
 
 /* Block decode to fp32 (ggml to_float, as called from reference
  * metal/leaninfer-metal.mm:187-193). Bit-exact with gguf-py's dequantize for
@@ -342,6 +377,49 @@ int li_launch_attn_layer_decode(const li_attn_layer * L,
         const int32_t * pos, int n_seqs, int max_ctx,
         void * workspace, size_t workspace_bytes, void * stream);
 
+/* ----------------------------------------------------------------------
+ * Multi-GPU: the SwiGLU FFN sharded two ways over NCCL (no counterpart in
+ * the reference, which has no multi-GPU code). Sequences stay sharded by rank
+ * (rows_per_rank rows of x and y per rank, the same count on every rank);
+ * the FFN's inner dimension is split into block-aligned ranges, one per rank:
+ * this rank holds W_gate and W_up rows [n0, n0 + N_local) and the matching
+ * byte range of every W_down row (W_down shard [K, N_local], row stride
+ * li_row_bytes(wtype, N_local)). A step all-gathers x over the communicator,
+ * runs li_launch_fused_ffn_q on all nranks * rows_per_rank rows with the
+ * local shard, and reduce-scatters (sums) the partial outputs back to this
+ * rank's rows of y. `comm` is an ncclComm_t of nranks ranks (one per GPU);
+ * NCCL is loaded with dlopen("libnccl.so.2") at first use, the copy already
+ * in the process when there is one. Every rank calls with the same shapes in
+ * the same order. Returns LI_ERR_NCCL if an NCCL call fails,
+ * LI_ERR_UNSUPPORTED if no NCCL library can be loaded. With nranks == 1 it
+ * is li_launch_fused_ffn_q (comm unused).
+ * ---------------------------------------------------------------------- */
+int li_nccl_available(void);
+int li_nccl_get_unique_id(void * id);   /* 128 bytes (ncclUniqueId) */
+int li_nccl_comm_init_rank(void ** comm, int nranks, const void * id, int rank);
+int li_nccl_comm_destroy(void * comm);
+size_t li_ffn_tp_workspace_size(int K, int N_local, int rows_per_rank, int nranks);
+int li_launch_ffn_q_tp(int wtype,
+        const float * x, const float * gamma,
+        const void * Wg, const void * Wu, const void * Wd, float * y,
+        int K, int N_local, int rows_per_rank, float eps,
+        void * comm, int nranks,
+        void * workspace, size_t workspace_bytes, void * stream);
+
+/* One decode step of a hybrid layer stack for n_seqs sequences (one token
+ * each): for every layer in order, x += mixer(x), then x += ffn(x), where x
+ * [n_seqs][hidden] fp32 is the residual stream, updated in place; the mixers
+ * update their states and caches in place (attention layers write slot
+ * pos[s]). With tp_nranks > 1 every FFN runs as li_launch_ffn_q_tp over
+ * tp_comm (an ncclComm_t) with this rank's FFN shards. No counterpart in the
+ * reference: the composition of the reference product's decode graph
+ * (docs/ASSESSMENT.md:1073-1090) over this library's layer entries. */
+size_t li_stack_workspace_size(const li_stack_layer * layers, int n_layers, int n_seqs, int max_ctx,
+        int tp_nranks);
+int li_launch_stack_decode(const li_stack_layer * layers, int n_layers, float * x,
+        const int32_t * pos, int n_seqs, int max_ctx, void * tp_comm, int tp_nranks,
+        void * workspace, size_t workspace_bytes, void * stream);
+
 /* Chunked (WY form, chunk 64) gated delta rule prefill of one sequence of T
  * tokens on the tensor cores (bf16 operands, fp32 accumulation and state).
  * No counterpart in the reference (its prefill is the upstream per-token
@@ -412,6 +490,8 @@ static inline size_t li_row_bytes(int t, int64_t k) {
     if (t == LI_WTYPE_Q4_K) return (k % 256) ? 0 : (size_t)(k / 256) * 144;
     return 0;
 }
+static inline int li_launch_add_f32(float*d, const float*a, const float*b, int64_t n, void*s)
+        {(void)d;(void)a;(void)b;(void)n;(void)s; return LI_ERR_NO_CUDA;}
 static inline int li_launch_dequantize(int t, const void*s, float*d, int64_t n, void*st)
         {(void)t;(void)s;(void)d;(void)n;(void)st; return LI_ERR_NO_CUDA;}
 static inline int li_launch_rms_norm_matmul_q(int t, const float*x, const float*g, const void*W, float*d,
@@ -454,6 +534,22 @@ static inline size_t li_attn_layer_workspace_size(const li_attn_layer*L, int n, 
 static inline int li_launch_attn_layer_decode(const li_attn_layer*L, const float*x, float*y, void*kc, void*vc,
         const int32_t*p, int n, int c, void*ws, size_t wb, void*s)
         {(void)L;(void)x;(void)y;(void)kc;(void)vc;(void)p;(void)n;(void)c;(void)ws;(void)wb;(void)s;
+         return LI_ERR_NO_CUDA;}
+static inline int li_nccl_available(void) { return 0; }
+static inline int li_nccl_get_unique_id(void*id) {(void)id; return LI_ERR_NO_CUDA;}
+static inline int li_nccl_comm_init_rank(void**c, int n, const void*id, int r)
+        {(void)c;(void)n;(void)id;(void)r; return LI_ERR_NO_CUDA;}
+static inline int li_nccl_comm_destroy(void*c) {(void)c; return LI_ERR_NO_CUDA;}
+static inline size_t li_ffn_tp_workspace_size(int K, int N, int r, int n) {(void)K;(void)N;(void)r;(void)n; return 0;}
+static inline int li_launch_ffn_q_tp(int t, const float*x, const float*g, const void*wg, const void*wu,
+        const void*wd, float*y, int K, int N, int r, float e, void*c, int n, void*ws, size_t wb, void*s)
+        {(void)t;(void)x;(void)g;(void)wg;(void)wu;(void)wd;(void)y;(void)K;(void)N;(void)r;(void)e;(void)c;(void)n;
+         (void)ws;(void)wb;(void)s; return LI_ERR_NO_CUDA;}
+static inline size_t li_stack_workspace_size(const li_stack_layer*l, int nl, int n, int c, int tp)
+        {(void)l;(void)nl;(void)n;(void)c;(void)tp; return 0;}
+static inline int li_launch_stack_decode(const li_stack_layer*l, int nl, float*x, const int32_t*p, int n, int c,
+        void*comm, int tp, void*ws, size_t wb, void*s)
+        {(void)l;(void)nl;(void)x;(void)p;(void)n;(void)c;(void)comm;(void)tp;(void)ws;(void)wb;(void)s;
          return LI_ERR_NO_CUDA;}
 static inline size_t li_deltanet_chunk_prefill_workspace_size(int T, int hv, int hd)
         {(void)T;(void)hv;(void)hd; return 0;}

@@ -43,7 +43,7 @@ elseif (LEANINFER_CUDA)
     target_include_directories(leaninfer_cuda
         PUBLIC "${_LI_DIR}/include"
         PRIVATE "${_LI_DIR}/leaninfer_b200/csrc")
-    target_link_libraries(leaninfer_cuda PUBLIC CUDA::cudart)
+    target_link_libraries(leaninfer_cuda PUBLIC CUDA::cudart ${CMAKE_DL_LIBS})
 
     if (TARGET llama)
         target_link_libraries(llama PRIVATE leaninfer_cuda)

@@ -23,6 +23,7 @@ STATUS_NAMES = {
     2006: "LI_ERR_TIMEOUT",
     2007: "LI_ERR_NO_CUDA",
     2008: "LI_ERR_SCRATCH_LIMIT",
+    2009: "LI_ERR_NCCL",
 }
 
 
@@ -59,6 +60,27 @@ class AttnLayer(ctypes.Structure):
     ]
 
 
+class FfnWeights(ctypes.Structure):
+    """Mirror of ``li_ffn_weights``."""
+
+    _fields_ = [
+        ("wtype", c_int), ("hidden", c_int), ("n_inner", c_int), ("eps", c_float),
+        ("norm_w", c_void_p), ("w_gate", c_void_p), ("w_up", c_void_p), ("w_down", c_void_p),
+    ]
+
+
+class StackLayer(ctypes.Structure):
+    """Mirror of ``li_stack_layer``."""
+
+    _fields_ = [
+        ("kind", c_int), ("deltanet", POINTER(DeltaNetLayer)), ("conv_state", c_void_p), ("state", c_void_p),
+        ("attn", POINTER(AttnLayer)), ("k_cache", c_void_p), ("v_cache", c_void_p), ("ffn", FfnWeights),
+    ]
+
+
+LI_LAYER_DELTANET, LI_LAYER_ATTN = 1, 2
+
+
 class GgmlTensor(ctypes.Structure):
     """Mirror of ``li_ggml_tensor`` (include/leaninfer-ggml.h)."""
 
@@ -86,6 +108,7 @@ _SIGS = {
     "li_device_status": (c_int, []),
     "li_row_bytes": (c_size_t, [c_int, c_int64]),
     "li_selftest_bounded_wait": (c_int, [c_int, c_void_p, c_void_p]),
+    "li_launch_add_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
     "li_launch_dequantize": (c_int, [c_int, c_void_p, c_void_p, c_int64, c_void_p]),
     "li_launch_rms_norm_matmul_q": (
         c_int, [c_int] + [c_void_p] * 4 + [c_int, c_int, c_int, c_float, c_void_p]),
@@ -116,6 +139,18 @@ _SIGS = {
     "li_attn_layer_workspace_size": (c_size_t, [POINTER(AttnLayer), c_int, c_int]),
     "li_launch_attn_layer_decode": (
         c_int, [POINTER(AttnLayer)] + [c_void_p] * 5 + [c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "li_nccl_available": (c_int, []),
+    "li_nccl_get_unique_id": (c_int, [c_void_p]),
+    "li_nccl_comm_init_rank": (c_int, [POINTER(c_void_p), c_int, c_void_p, c_int]),
+    "li_nccl_comm_destroy": (c_int, [c_void_p]),
+    "li_ffn_tp_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "li_launch_ffn_q_tp": (
+        c_int, [c_int] + [c_void_p] * 6 + [c_int, c_int, c_int, c_float, c_void_p, c_int, c_void_p, c_size_t,
+                                           c_void_p]),
+    "li_stack_workspace_size": (c_size_t, [POINTER(StackLayer), c_int, c_int, c_int, c_int]),
+    "li_launch_stack_decode": (
+        c_int, [POINTER(StackLayer), c_int, c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p, c_size_t,
+                c_void_p]),
     # ggml-style node dispatch (include/leaninfer-ggml.h)
     "li_ggml_workspace_size": (c_size_t, [c_void_p]),
     "li_ggml_compute_forward": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),

@@ -70,7 +70,7 @@ def build(force: bool = False, ptxas_verbose: bool = False, verbose: bool = Fals
                 print(f"--- {obj.name}\n{log}", file=sys.stderr)
     tmp = LIB.with_suffix(".so.tmp")
     cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *[str(o) for o, _ in results],
-           "-lcudart"]
+           "-lcudart", "-ldl"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

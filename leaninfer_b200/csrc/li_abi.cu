@@ -61,6 +61,42 @@ size_t li_row_bytes(int wtype, int64_t k) {
     }
 }
 
+}  // extern "C"
+
+namespace li {
+namespace {
+
+// dst = a + b, four floats per thread when the pointers allow (the residual
+// adds between the layers of a decode stack); a programmatic dependent launch.
+__global__ void __launch_bounds__(256) add_f32_kernel(float *dst, const float *a, const float *b, int64_t n,
+                                                      bool vec) {
+    grid_dep_wait();
+    grid_dep_launch_dependents();
+    const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
+    if (vec) {
+        if (4 * i + 3 < n) {
+            const float4 x = reinterpret_cast<const float4 *>(a)[i], y = reinterpret_cast<const float4 *>(b)[i];
+            reinterpret_cast<float4 *>(dst)[i] = make_float4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w);
+        }
+    } else if (i < n) {
+        dst[i] = a[i] + b[i];
+    }
+}
+
+}  // namespace
+}  // namespace li
+
+extern "C" {
+
+int li_launch_add_f32(float *dst, const float *a, const float *b, int64_t n, void *stream) {
+    if (!dst || !a || !b || n < 0) return LI_ERR_BAD_ARG;
+    if (n == 0) return 0;
+    const bool vec = n % 4 == 0 && li::aligned16(dst) && li::aligned16(a) && li::aligned16(b);
+    const int64_t items = vec ? n / 4 : n;
+    return (int)li::launch_pdl(li::add_f32_kernel, dim3((unsigned)((items + 255) / 256)), dim3(256), 0,
+                               (cudaStream_t)stream, true, dst, a, b, n, vec);
+}
+
 // Synchronises the current device, then returns and clears the device-side
 // failure flag raised by a bounded wait that gave up (LI_ERR_TIMEOUT), or a
 // CUDA error from the synchronisation. Not for use inside graph capture.
