@@ -698,12 +698,266 @@ def cpu_baseline_gemv(kind: str, wtype: int, rows: int) -> dict:
                       f"{oracle.num_threads()} host threads)", "seconds": round(dt, 3)}
 
 
+# --------------------------------------------------------------------------
+# hybrid decode stack (Qwen3.5-27B-like): 48 Gated DeltaNet + 16 gated
+# attention layers (3:1), SwiGLU FFN after each, 256 sequences over N GPUs
+# --------------------------------------------------------------------------
+ST_HIDDEN, ST_HK, ST_HV, ST_D = 5120, 16, 48, 128
+ST_HQ, ST_HKV, ST_ROPE, ST_FFN = 40, 8, 64, 17408
+ST_CONV = 2 * ST_HK * ST_D + ST_HV * ST_D
+ST_NI = ST_CONV + ST_HV * ST_D + 2 * ST_HV
+ST_NP = 2 * ST_HQ * ST_D + 2 * ST_HKV * ST_D
+
+
+def q4k_bytes(rows: int, k: int) -> int:
+    return rows * (k // 256) * 144
+
+
+def stack_bytes(n_layers: int, batch: int, ctx: int, tp: int) -> dict:
+    """Algorithmic bytes of one stack step on one GPU holding `batch`
+    sequences: every weight byte once (FFN shards when tp > 1), per sequence
+    the DeltaNet state and conv state read and written, the KV cache read (and
+    the new token's row written), x in and out of every layer."""
+    n_attn = n_layers // 4
+    n_dn = n_layers - n_attn
+    dn_w = q4k_bytes(ST_NI, ST_HIDDEN) + q4k_bytes(ST_HIDDEN, ST_HV * ST_D) + ST_CONV * 16 + (2 * ST_HV + ST_D + ST_HIDDEN) * 4
+    at_w = q4k_bytes(ST_NP, ST_HIDDEN) + q4k_bytes(ST_HIDDEN, ST_HQ * ST_D) + (2 * ST_D + ST_HIDDEN) * 4
+    ffn_w = (2 * q4k_bytes(ST_FFN, ST_HIDDEN) + q4k_bytes(ST_HIDDEN, ST_FFN)) // tp + ST_HIDDEN * 4
+    per_seq = n_dn * (ST_HV * ST_D * ST_D * 4 * 2 + ST_CONV * 3 * 4 * 2) + \
+        n_attn * (ctx * ST_HKV * ST_D * 2 * 2 + ST_HKV * ST_D * 2 * 2) + n_layers * 2 * (ST_HIDDEN * 4 * 2)
+    weights = n_dn * dn_w + n_attn * at_w + n_layers * ffn_w
+    return {"weights": weights, "per_seq": per_seq, "total": weights + batch * per_seq}
+
+
+def build_stack(dev, batch: int, n_layers: int, ctx: int, tp: int, tp_rank: int, seed: int = 1):
+    """The stack's layers on the device, weights drawn per layer from a
+    generator seeded by the layer index (the same on every rank, so FFN shards
+    of different ranks are slices of one set of weights)."""
+    import torch
+    from leaninfer_b200.stack import random_q4_k_device
+    from leaninfer_b200.tp_ffn import ffn_split
+    layers = []
+    for li in range(n_layers):
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed * 100000 + li)
+        u = lambda *shape: torch.rand(*shape, device=dev, generator=g)
+        q4 = lambda n, k: random_q4_k_device(n, k, dev, g)
+        attn = li % 4 == 3
+        if not attn:
+            l = dict(kind="deltanet", hidden=ST_HIDDEN, n_k_heads=ST_HK, n_v_heads=ST_HV, head_dim=ST_D, wtype=12,
+                     w_in=q4(ST_NI, ST_HIDDEN), w_out=q4(ST_HIDDEN, ST_HV * ST_D),
+                     conv_w=0.1 * torch.randn(ST_CONV, 4, device=dev, generator=g),
+                     a_log=0.5 * torch.randn(ST_HV, device=dev, generator=g), dt_bias=torch.zeros(ST_HV, device=dev),
+                     norm_w=u(ST_D) + 0.5, in_norm_w=(u(ST_HIDDEN) + 0.5) / 128.0,
+                     conv_state=torch.zeros(batch, ST_CONV, 3, device=dev),
+                     state=0.02 * torch.randn(batch, ST_HV, ST_D, ST_D, device=dev, generator=g))
+        else:
+            kc = torch.randn(batch, ctx, ST_HKV, ST_D, device=dev, generator=g).half()
+            vc = torch.randn(batch, ctx, ST_HKV, ST_D, device=dev, generator=g).half()
+            l = dict(kind="attn", hidden=ST_HIDDEN, n_q_heads=ST_HQ, n_kv_heads=ST_HKV, head_dim=ST_D,
+                     rope_dim=ST_ROPE, rope_theta=1e7, wtype=12, w_in=q4(ST_NP, ST_HIDDEN),
+                     w_out=q4(ST_HIDDEN, ST_HQ * ST_D), in_norm_w=(u(ST_HIDDEN) + 0.5) / 128.0,
+                     q_norm_w=u(ST_D) + 0.5, k_norm_w=u(ST_D) + 0.5, k_cache=kc, v_cache=vc)
+        wg, wu, wd = q4(ST_FFN, ST_HIDDEN), q4(ST_FFN, ST_HIDDEN), q4(ST_HIDDEN, ST_FFN)
+        n0, n1 = ffn_split(ST_FFN, 12, tp, tp_rank) if tp > 1 else (0, ST_FFN)
+        if tp > 1:
+            wg, wu = wg[n0:n1].contiguous(), wu[n0:n1].contiguous()
+            wd = wd[:, n0 // 256 * 144:n1 // 256 * 144].contiguous()
+        l["ffn"] = dict(wtype=12, hidden=ST_HIDDEN, n_inner=n1 - n0, norm_w=(u(ST_HIDDEN) + 0.5) / 128.0,
+                        w_gate=wg, w_up=wu, w_down=wd)
+        layers.append(l)
+    return layers
+
+
+def run_stack(args, rank: int, world: int, dist) -> dict | None:
+    """One step = one token for every sequence through the whole stack.
+    Sequences shard across ranks (strong scaling: args.batch in total);
+    with --tp-ffn the FFN weights are also split across the ranks (NCCL
+    all-gather + reduce-scatter inside li_launch_ffn_q_tp)."""
+    import ctypes
+
+    import torch
+    from leaninfer_b200 import _lib, ops
+    from leaninfer_b200.shard import max_over_ranks, shard_bounds
+    from leaninfer_b200.stack import HybridStackDecode
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    lib = _lib.load()
+    tp = world if (args.tp_ffn and world > 1) else 1
+    if tp > 1 and args.batch % world:
+        raise ValueError("--tp-ffn needs the same number of sequences on every rank")
+    _, B = shard_bounds(args.batch, world, rank)
+    comm = None
+    if tp > 1:
+        uid = ctypes.create_string_buffer(128)
+        if rank == 0 and lib.li_nccl_get_unique_id(uid) != 0:
+            raise RuntimeError("li_nccl_get_unique_id failed")
+        obj = [bytes(uid.raw)]
+        dist.broadcast_object_list(obj, src=0)
+        uid = ctypes.create_string_buffer(obj[0], 128)
+        c = ctypes.c_void_p()
+        rc = lib.li_nccl_comm_init_rank(ctypes.byref(c), tp, uid, rank)
+        if rc:
+            raise RuntimeError(f"li_nccl_comm_init_rank: {rc}")
+        comm = c.value
+    layers = build_stack(dev, B, args.layers, args.ctx, tp, rank)
+    stack = HybridStackDecode(layers, n_seqs=B, max_ctx=args.ctx, tp_comm=comm, tp_nranks=tp)
+    x = torch.randn(B, ST_HIDDEN, device=dev)
+    pos = torch.full((B,), args.ctx - 1, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize()
+    stack.step(x, pos)                       # eager call: fills the launch-attribute caches
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            stack.step(x, pos)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    sampler = ClockSampler(dev.index)
+    sampler.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_wall0 = time.time()
+    e0.record(stream)
+    for _ in range(args.steps):
+        graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    ms = e0.elapsed_time(e1)
+    sampler.stop()
+    # e2e: x from pinned host memory in, the residual stream out, every step
+    hx = x.cpu().pin_memory()
+    hy = torch.empty_like(hx).pin_memory()
+    e_steps = max(1, min(args.steps, 10))
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0.record(stream)
+    for _ in range(e_steps):
+        x.copy_(hx, non_blocking=True)
+        graph.replay()
+        hy.copy_(x, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    status = ops.device_status()
+    if status:
+        raise RuntimeError(f"device status {status} after the timed region")
+    del graph
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    if comm:
+        lib.li_nccl_comm_destroy(ctypes.c_void_p(comm))
+    ms, e2e_ms = max_over_ranks([ms, e2e_ms], dist, device=dev)
+    if rank != 0:
+        return None
+    peaks = measured_peaks()
+    step_s = ms / 1e3 / args.steps
+    by = stack_bytes(args.layers, B, args.ctx, tp)
+    achieved = by["total"] / step_s / 1e9
+    line = {
+        "metric": "hybrid-stack decode tokens/s", "value": round(args.batch * args.steps / (ms / 1e3), 1),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32 (Q4_K weights, fp16 KV cache)", "data": "synthetic",
+        "config": {"workload": "hybrid_stack_decode", "layers": args.layers,
+                   "pattern": "3 Gated DeltaNet : 1 gated attention, SwiGLU FFN after each",
+                   "global_batch": args.batch, "batch_per_gpu": B, "hidden": ST_HIDDEN,
+                   "deltanet": {"k_heads": ST_HK, "v_heads": ST_HV, "head_dim": ST_D},
+                   "attention": {"q_heads": ST_HQ, "kv_heads": ST_HKV, "head_dim": ST_D, "rope_dim": ST_ROPE,
+                                 "context": args.ctx},
+                   "ffn": ST_FFN, "weights": "Q4_K",
+                   "parallelism": f"sequence-sharded x{world}" + (f", FFN 2-D sharded x{tp} (NCCL)" if tp > 1 else
+                                                                  ", weights replicated"),
+                   "l2": f"{by['total'] / 1e9:.1f} GB moved per step per GPU, far beyond L2"},
+        "roofline": {"bound": "hbm", "kernel": "whole stack step (one CUDA graph)", "achieved": round(achieved, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "peak_source": peaks["source"], "algorithmic_bytes_per_step": by["total"], "traffic": None},
+        "e2e": {"value": round(args.batch * e_steps / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": B * ST_HIDDEN * 4, "d2h_bytes_per_step": B * ST_HIDDEN * 4},
+        "gpu_launches": stack_launches(args.layers, B, tp) * args.steps,
+        "clocks": sampler.summary(t_wall0, t_wall1),
+    }
+    if not args.no_cpu_baseline and world == 1:
+        line["cpu_baseline"] = cpu_baseline_stack(args.layers, args.ctx)
+    return line
+
+
+def cpu_baseline_stack(n_layers: int, ctx: int) -> dict:
+    """The oracle on the host cores: one DeltaNet layer step, one attention
+    layer step (a cache of `ctx` tokens) and one FFN, each for one sequence at
+    the stack's shapes, timed and combined as the stack composes them
+    (tokens/s of one sequence = 1 / (48 t_deltanet + 16 t_attention + 64 t_ffn)
+    for 64 layers)."""
+    from leaninfer_b200 import synth
+    from oracle import oracle
+    r = np.random.Generator(np.random.PCG64(17))
+    w = synth.deltanet_layer(r, hidden=ST_HIDDEN, n_k_heads=ST_HK, n_v_heads=ST_HV, head_dim=ST_D, wtype=12)
+    L, keep = oracle.make_layer(w)
+    inp = synth.deltanet_inputs(r, 1, w)
+    t0 = time.perf_counter()
+    oracle.deltanet_layer_decode(L, keep, inp["x"], inp["conv_state"], inp["state"])
+    t_dn = time.perf_counter() - t0
+    wa = synth.attn_layer(r, hidden=ST_HIDDEN, n_q_heads=ST_HQ, n_kv_heads=ST_HKV, rope_dim=ST_ROPE, wtype=12)
+    La, keepa = oracle.make_attn_layer(wa)
+    ia = synth.attn_inputs(r, 1, wa, ctx)
+    t0 = time.perf_counter()
+    oracle.attn_layer_decode(La, keepa, ia["x"], ia["k_cache"], ia["v_cache"], ia["pos"])
+    t_at = time.perf_counter() - t0
+    Wg, Wu = synth.random_q4_k(r, ST_FFN, ST_HIDDEN), synth.random_q4_k(r, ST_FFN, ST_HIDDEN)
+    Wd = synth.random_q4_k(r, ST_HIDDEN, ST_FFN)
+    x = r.standard_normal((1, ST_HIDDEN)).astype(np.float32)
+    gamma = r.uniform(0.5, 1.5, ST_HIDDEN).astype(np.float32)
+    t0 = time.perf_counter()
+    oracle.ffn(12, x, gamma, Wg, Wu, Wd, ST_FFN)
+    t_ffn = time.perf_counter() - t0
+    n_attn = n_layers // 4
+    per_token = (n_layers - n_attn) * t_dn + n_attn * t_at + n_layers * t_ffn
+    return {"value": round(1.0 / per_token, 4), "unit": "tokens/s", "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"one sequence: one DeltaNet layer ({t_dn * 1e3:.1f} ms), one attention layer over {ctx} "
+                      f"cached tokens ({t_at * 1e3:.1f} ms) and one FFN ({t_ffn * 1e3:.1f} ms) of the oracle "
+                      f"(oracle/li_oracle.c, double accumulation, {oracle.num_threads()} host threads), composed "
+                      f"for {n_layers} layers", "seconds": round(t_dn + t_at + t_ffn, 3)}
+
+
+def stack_launches(n_layers: int, batch: int, tp: int) -> int:
+    """Kernels of the library per stack step (NCCL's own kernels not counted):
+    per layer the mixer's, the FFN's and two residual adds."""
+    def proj(rows):   # one projection: SIMT GEMV, or prep + GEMM (+ reduce for the X-stationary kernel)
+        return 1 if rows < TC_MIN_ROWS else (3 if rows <= TCX_MAX_ROWS else 2)
+    n_attn = n_layers // 4
+    dn = kernels_per_step(batch)
+    at = proj(batch) + 3 + proj(batch)
+    ffn = gemv_launches("ffn", batch * tp)
+    return (n_layers - n_attn) * (dn + ffn + 2) + n_attn * (at + ffn + 2)
+
+
 def run_reference(args, rank: int) -> dict | None:
     """The reference's CPU path for the workload (the oracle port: ggml's CPU
     ops are not vendored), on the host cores with all threads; rank 0 only."""
     if rank != 0:
         return None
     if args.workload != "decode":
+        if args.workload == "stack":
+            cb = cpu_baseline_stack(args.layers, args.ctx)
+            cfg = {"workload": "hybrid_stack_decode", "layers": args.layers, "global_batch": args.batch,
+                   "context": args.ctx, "rows_timed": 1}
+            cfg["note"] = "the reference's ggml CPU ops are not vendored; its CPU path is the C oracle port"
+            return {"impl": "reference", "metric": "hybrid-stack decode tokens/s", "value": cb["value"],
+                    "unit": cb["unit"], "n_gpus": 0, "steps": args.steps, "warmup": args.warmup,
+                    "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                    "dtype": "f64 accumulation", "data": "synthetic", "config": cfg,
+                    "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                    "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
+                            "d2h_bytes_per_step": 0}}
         if args.workload == "prefill":
             cb, metric, cfg = cpu_baseline_prefill(), "chunked prefill tokens/s", {
                 "workload": "deltanet_chunk_prefill_bf16", "tokens_per_sequence": PF_T, "chunk": 64}
@@ -735,12 +989,17 @@ def main():
     # 5000 decode steps at B = 64 are ~0.5 s of timed work: several clock samples (100 ms apart)
     ap.add_argument("--steps", type=int, default=5000)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--batch", type=int, default=None,
+                    help="sequences per GPU (decode, default 64; ffn rows, default 64); stack: sequences in total "
+                         "(default 256)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-steps", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--traffic", type=float, default=None, help="ncu DRAM bytes per step, if captured")
-    ap.add_argument("--workload", choices=["decode", "prefill", "qkv", "ffn"], default="decode",
+    ap.add_argument("--layers", type=int, default=64, help="stack: layers (3 DeltaNet : 1 attention)")
+    ap.add_argument("--ctx", type=int, default=4096, help="stack: attention context (KV cache length)")
+    ap.add_argument("--tp-ffn", action="store_true", help="stack: shard the FFN weights across the GPUs (NCCL)")
+    ap.add_argument("--workload", choices=["decode", "prefill", "qkv", "ffn", "stack"], default="decode",
                     help="decode: the fused DeltaNet layer decode step (the headline); prefill: one 8192-token "
                          "chunked prefill + gated norm + bf16 out-projection; qkv: RMSNorm + Q/K/V Q8_0 GEMV "
                          "(K=2048, one token); ffn: RMSNorm + SwiGLU FFN 4096 -> 12288 -> 4096 (--batch rows, "
@@ -751,6 +1010,10 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.batch is None:
+        args.batch = 256 if args.workload == "stack" else 64
+    if args.workload == "stack" and "--steps" not in sys.argv:
+        args.steps = 20          # about 1 s of timed work on one GPU (a step is ~50 ms there)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -779,6 +1042,8 @@ def main():
     try:
         if args.workload == "prefill":
             line = run_prefill(args, rank, world, dist)
+        elif args.workload == "stack":
+            line = run_stack(args, rank, world, dist)
         elif args.workload in ("qkv", "ffn"):
             line = run_gemv(args, rank, world, dist)
         else:

@@ -47,6 +47,22 @@ class AttnLayer(ctypes.Structure):
 
 
 _lib = None
+NATIVE = HERE / "_native" / "liboracle_native.so"
+
+
+def use_native() -> bool:
+    """Build the oracle with -march=native for the host it runs on (the CPU
+    baseline legs of bench.py, on the GPU box) and load that copy instead of
+    the portable one; False (and the portable copy stays) if the build fails.
+    Call before the first use of lib()."""
+    global _lib
+    if _lib is not None:
+        return False
+    r = subprocess.run(["make", "-s", "-C", str(HERE), "native"], capture_output=True, text=True)
+    if r.returncode != 0 or not NATIVE.exists():
+        return False
+    _load(NATIVE)
+    return True
 
 
 def build(with_ref: bool | None = None) -> None:
@@ -64,36 +80,40 @@ def build(with_ref: bool | None = None) -> None:
 
 
 def lib() -> ctypes.CDLL:
-    global _lib
     if _lib is None:
         if not LIB.exists() or LIB.stat().st_mtime < (HERE / "li_oracle.c").stat().st_mtime:
             build(with_ref=False)
-        L = ctypes.CDLL(str(LIB))
-        L.lio_dequantize.argtypes = [c_int, c_void_p, c_void_p, c_int64]
-        L.lio_rms_norm_matmul.argtypes = [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
-                                          c_float]
-        L.lio_rms_norm_matmul_q8act.argtypes = [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
-                                                c_int, c_float]
-        L.lio_rms_norm_swiglu.argtypes = [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
-                                          c_int, c_int, c_float, c_int]
-        L.lio_ffn.argtypes = [c_int] + [c_void_p] * 6 + [c_int, c_int, c_int, c_float]
-        L.lio_silu_gate.argtypes = [c_void_p] * 4 + [c_int, c_int, c_float]
-        L.lio_silu_gate.restype = None
-        L.lio_deltanet_recurrent.argtypes = [c_void_p] * 10 + [c_int64] * 4 + [c_int, c_int64, c_int64,
-                                                                                c_size_t, c_size_t, c_size_t]
-        L.lio_deltanet_taps_per_seq.argtypes = [POINTER(Layer)]
-        L.lio_deltanet_taps_per_seq.restype = c_size_t
-        L.lio_deltanet_layer_decode.argtypes = [POINTER(Layer), c_void_p, c_void_p, c_void_p, c_void_p, c_int,
-                                                c_void_p]
-        L.lio_gdr_prefill.argtypes = [c_void_p] * 7 + [c_int, c_int, c_int, c_int, c_float]
-        L.lio_fp16_to_fp32.argtypes = [c_uint16]
-        L.lio_fp16_to_fp32.restype = c_float
-        L.lio_fp32_to_fp16.argtypes = [c_float]
-        L.lio_fp32_to_fp16.restype = c_uint16
-        L.lio_attn_layer_decode.argtypes = [POINTER(AttnLayer)] + [c_void_p] * 5 + [c_int, c_int]
-        L.lio_num_threads.restype = c_int
-        _lib = L
+        _load(LIB)
     return _lib
+
+
+def _load(path: Path) -> None:
+    global _lib
+    L = ctypes.CDLL(str(path))
+    L.lio_dequantize.argtypes = [c_int, c_void_p, c_void_p, c_int64]
+    L.lio_rms_norm_matmul.argtypes = [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                      c_float]
+    L.lio_rms_norm_matmul_q8act.argtypes = [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                            c_int, c_float]
+    L.lio_rms_norm_swiglu.argtypes = [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+                                      c_int, c_int, c_float, c_int]
+    L.lio_ffn.argtypes = [c_int] + [c_void_p] * 6 + [c_int, c_int, c_int, c_float]
+    L.lio_silu_gate.argtypes = [c_void_p] * 4 + [c_int, c_int, c_float]
+    L.lio_silu_gate.restype = None
+    L.lio_deltanet_recurrent.argtypes = [c_void_p] * 10 + [c_int64] * 4 + [c_int, c_int64, c_int64,
+                                                                            c_size_t, c_size_t, c_size_t]
+    L.lio_deltanet_taps_per_seq.argtypes = [POINTER(Layer)]
+    L.lio_deltanet_taps_per_seq.restype = c_size_t
+    L.lio_deltanet_layer_decode.argtypes = [POINTER(Layer), c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+                                            c_void_p]
+    L.lio_gdr_prefill.argtypes = [c_void_p] * 7 + [c_int, c_int, c_int, c_int, c_float]
+    L.lio_fp16_to_fp32.argtypes = [c_uint16]
+    L.lio_fp16_to_fp32.restype = c_float
+    L.lio_fp32_to_fp16.argtypes = [c_float]
+    L.lio_fp32_to_fp16.restype = c_uint16
+    L.lio_attn_layer_decode.argtypes = [POINTER(AttnLayer)] + [c_void_p] * 5 + [c_int, c_int]
+    L.lio_num_threads.restype = c_int
+    _lib = L
 
 
 def _ptr(a: np.ndarray | None):

@@ -6,9 +6,14 @@ position advancing. Hidden 1024 (DeltaNet 4 k / 8 v heads, attention 8 q / 2
 kv heads, FFN 1024 -> 2816, Q4_K), at 3, 8 and 40 sequences (SIMT GEMVs,
 X-stationary and one-tile tensor-core projections).
 
-Tolerance: 5e-3 normwise on the residual stream after the step (eight
-sub-layers compose, each within its own entry's tolerance) and 2e-3 on the
-recurrent states."""
+Tolerances, normwise on the residual stream after each step: 2e-3 with the
+SIMT projections (3 sequences, fp32 operands), 1e-2 with the tensor-core
+projections (f16 operands, about 4e-4 per projection): eight sub-layers
+compose, and the DeltaNet gates and the SwiGLU amplify an operand error on
+some rows (the per-entry tests hold each sub-layer to its own tolerance; one
+DeltaNet layer + FFN already measures up to 1.2e-3 on random inputs here). A
+wiring fault (a wrong buffer, a missing residual add) gives errors of order
+one. Recurrent states within 2e-3."""
 from __future__ import annotations
 
 import json
@@ -88,7 +93,7 @@ def test_stack_block_two_steps(cuda, oracle_mod, B):
         x = _oracle_step(oracle_mod, layers, x, pos)
         got = xd.cpu().numpy()
         print(json.dumps({"case": f"stack B={B} step {step}", "normwise": max_rel_err(got, x)}))
-        assert_close(got, x, 5e-3, f"residual stream B={B} step {step}")
+        assert_close(got, x, 2e-3 if B < 4 else 1e-2, f"residual stream B={B} step {step}")
     for l, d in zip(layers, dev_layers):
         if l["kind"] == "deltanet":
             assert_close(d["state"].cpu().numpy(), l["st"]["state"], 2e-3, f"state B={B}")
