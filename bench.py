@@ -46,9 +46,10 @@ N_IN = CONV_CH + HV * D + 2 * HV
 METRIC = "fused-layer decode tokens/s"
 
 # DRAM bytes per step (dram__bytes_read.sum + dram__bytes_write.sum summed over
-# the step's kernels) from one ncu capture of this bench per batch; writes
-# still in L2 when a kernel ends are not counted by ncu.
-NCU_TRAFFIC = {64: 262_778_000}
+# the step's kernels), the mean of two steps of one ncu capture of this bench
+# (profiles/layer_decode_q4k_b64_traffic.md); writes still in L2 when a kernel
+# ends are not counted by ncu.
+NCU_TRAFFIC = {64: 265_325_056}
 UNIT = "tokens/s"
 
 
@@ -348,22 +349,34 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
 # --------------------------------------------------------------------------
 # CPU legs: the oracle (the C restatement of the path) on the host cores
 # --------------------------------------------------------------------------
-def cpu_baseline(batch: int, steps: int) -> dict:
-    from leaninfer_b200 import synth
+def cpu_oracle():
+    """The oracle for the timed CPU legs: rebuilt with -march=native for this
+    host when the compiler allows (else the portable build)."""
     from oracle import oracle
+    native = oracle.use_native()
+    return oracle, ("-O3 -march=native" if native else "-O3 -march=x86-64-v3")
+
+
+def cpu_baseline(batch: int, steps: int) -> dict:
+    """The layer step on the host cores in ggml's CPU arithmetic (q8_K
+    activations, integer dots for the Q4_K projections; the recurrence in
+    double), all threads."""
+    from leaninfer_b200 import synth
+    oracle, flags = cpu_oracle()
     r = np.random.Generator(np.random.PCG64(7))
     w = synth.deltanet_layer(r, hidden=HIDDEN, n_k_heads=HK, n_v_heads=HV, head_dim=D, wtype=synth.Q4_K)
     L, keep = oracle.make_layer(w)
     inp = synth.deltanet_inputs(r, batch, w)
     cs, st = inp["conv_state"], inp["state"]
-    oracle.deltanet_layer_decode(L, keep, inp["x"], cs, st)        # warm-up
+    oracle.deltanet_layer_decode_q8act(L, keep, inp["x"], cs, st)        # warm-up
     t0 = time.perf_counter()
     for _ in range(steps):
-        oracle.deltanet_layer_decode(L, keep, inp["x"], cs, st)
+        oracle.deltanet_layer_decode_q8act(L, keep, inp["x"], cs, st)
     dt = time.perf_counter() - t0
     return {"value": round(batch * steps / dt, 2), "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
-            "sample": f"{steps} decode steps of the same layer at batch {batch} (oracle/li_oracle.c, "
-                      f"double accumulation, {oracle.num_threads()} host threads)",
+            "sample": f"{steps} decode steps of the same layer at batch {batch} (oracle/li_oracle.c built {flags}: "
+                      f"projections with ggml-style q8_K activations and integer dots, recurrence in double; "
+                      f"{oracle.num_threads()} host threads)",
             "seconds": round(dt, 3)}
 
 
@@ -483,7 +496,7 @@ def cpu_baseline_prefill() -> dict:
     """The oracle's token-by-token recurrence (double precision, all host
     threads over the heads) on the first 256 tokens of a sequence; the
     out-projection is not in the sample."""
-    from oracle import oracle
+    oracle, flags = cpu_oracle()
     r = np.random.Generator(np.random.PCG64(11))
     n = 256
 
@@ -500,7 +513,7 @@ def cpu_baseline_prefill() -> dict:
     oracle.gdr_prefill(q, k, v, g, beta, st, PF_D ** -0.5)
     dt = time.perf_counter() - t0
     return {"value": round(n / dt, 2), "unit": "tokens/s", "cores": oracle.num_threads(), "kind": "port",
-            "sample": f"{n} tokens of the chunk recurrence, 32 v-heads (oracle/li_oracle.c token by token, "
+            "sample": f"{n} tokens of the chunk recurrence, 32 v-heads (oracle/li_oracle.c built {flags}, token by token, "
                       f"double precision, {oracle.num_threads()} host threads; out-projection not included)",
             "seconds": round(dt, 3)}
 
@@ -674,10 +687,13 @@ def run_gemv(args, rank: int, world: int, dist) -> dict | None:
 
 
 def cpu_baseline_gemv(kind: str, wtype: int, rows: int) -> dict:
-    """The oracle (dequantize, double accumulation) on the same shapes: one
-    step of the qkv workload, one row of the FFN."""
+    """The oracle in ggml's CPU arithmetic (quantized activations, integer
+    dots), all threads, on the same shapes: one step of the qkv workload, one
+    row of the FFN. For the FFN also the reference's own single-thread fp32
+    CPU function (cpu_rms_norm_swiglu, cuda/benchmark_fused.cu:99-121) at the
+    gate/up shape, when it was built (oracle/_ref)."""
     from leaninfer_b200 import synth
-    from oracle import oracle
+    oracle, flags = cpu_oracle()
     r = np.random.Generator(np.random.PCG64(13))
     K = QKV_K if kind == "qkv" else FFN_K
     x = r.standard_normal((1, K)).astype(np.float32)
@@ -686,16 +702,27 @@ def cpu_baseline_gemv(kind: str, wtype: int, rows: int) -> dict:
         Ws = [synth.random_weights(r, wtype, n, K) for n in QKV_N]
         t0 = time.perf_counter()
         for w, n in zip(Ws, QKV_N):
-            oracle.rms_norm_matmul(wtype, x, gamma, w, n, 1e-6)
+            oracle.rms_norm_matmul_q8act(wtype, x, gamma, w, n, 1e-6)
     else:
         Wg, Wu = synth.random_weights(r, wtype, FFN_N, K), synth.random_weights(r, wtype, FFN_N, K)
         Wd = synth.random_weights(r, wtype, K, FFN_N)
         t0 = time.perf_counter()
-        oracle.ffn(wtype, x, gamma, Wg, Wu, Wd, FFN_N, 1e-6)
+        oracle.ffn_q8act(wtype, x, gamma, Wg, Wu, Wd, FFN_N, 1e-6)
     dt = time.perf_counter() - t0
-    return {"value": round(1 / dt, 2), "unit": "tokens/s", "cores": oracle.num_threads(), "kind": "port",
-            "sample": f"one row of the {kind} workload (oracle/li_oracle.c, dequantize + double accumulation, "
-                      f"{oracle.num_threads()} host threads)", "seconds": round(dt, 3)}
+    out = {"value": round(1 / dt, 2), "unit": "tokens/s", "cores": oracle.num_threads(), "kind": "port",
+           "sample": f"one row of the {kind} workload (oracle/li_oracle.c built {flags}: ggml-style quantized "
+                     f"activations and integer dots, {oracle.num_threads()} host threads)", "seconds": round(dt, 3)}
+    if kind == "ffn" and oracle.REF_BENCH.exists():
+        Wgf = (0.02 * r.standard_normal((FFN_N, K))).astype(np.float32)
+        Wuf = (0.02 * r.standard_normal((FFN_N, K))).astype(np.float32)
+        t0 = time.perf_counter()
+        oracle.ref_cpu_rms_norm_swiglu(x[0], gamma, Wgf, Wuf, 1e-6)
+        t_ref = time.perf_counter() - t0
+        out["reference_literal"] = {
+            "value": round(1 / t_ref, 2), "unit": "rows/s (gate/up only, fp32 weights)", "cores": 1,
+            "sample": "the reference's cpu_rms_norm_swiglu (cuda/benchmark_fused.cu:99-121) compiled from its "
+                      "sources, one row at K=4096 N=12288 with fp32 weights", "seconds": round(t_ref, 3)}
+    return out
 
 
 # --------------------------------------------------------------------------
@@ -898,7 +925,7 @@ def cpu_baseline_stack(n_layers: int, ctx: int) -> dict:
     (tokens/s of one sequence = 1 / (48 t_deltanet + 16 t_attention + 64 t_ffn)
     for 64 layers)."""
     from leaninfer_b200 import synth
-    from oracle import oracle
+    oracle, flags = cpu_oracle()
     r = np.random.Generator(np.random.PCG64(17))
     w = synth.deltanet_layer(r, hidden=ST_HIDDEN, n_k_heads=ST_HK, n_v_heads=ST_HV, head_dim=ST_D, wtype=12)
     L, keep = oracle.make_layer(w)
@@ -924,7 +951,7 @@ def cpu_baseline_stack(n_layers: int, ctx: int) -> dict:
     return {"value": round(1.0 / per_token, 4), "unit": "tokens/s", "cores": oracle.num_threads(), "kind": "port",
             "sample": f"one sequence: one DeltaNet layer ({t_dn * 1e3:.1f} ms), one attention layer over {ctx} "
                       f"cached tokens ({t_at * 1e3:.1f} ms) and one FFN ({t_ffn * 1e3:.1f} ms) of the oracle "
-                      f"(oracle/li_oracle.c, double accumulation, {oracle.num_threads()} host threads), composed "
+                      f"(oracle/li_oracle.c built {flags}, double accumulation, {oracle.num_threads()} host threads), composed "
                       f"for {n_layers} layers", "seconds": round(t_dn + t_at + t_ffn, 3)}
 
 
@@ -940,11 +967,121 @@ def stack_launches(n_layers: int, batch: int, tp: int) -> int:
     return (n_layers - n_attn) * (dn + ffn + 2) + n_attn * (at + ffn + 2)
 
 
+# --------------------------------------------------------------------------
+# the reference's own GPU kernels next to this library's entries, same box
+# --------------------------------------------------------------------------
+# fp32 RMSNorm + SwiGLU shapes of the reference benchmark
+# (cuda/benchmark_fused.cu:144-148): Qwen2.5-0.5B, Qwen3.5-9B, Qwen3-14B
+REF_SWIGLU_SHAPES = [("Qwen2.5-0.5B", 896, 4864), ("Qwen3.5-9B", 3584, 18944), ("Qwen3-14B", 5120, 17408)]
+
+
+def run_refgpu(args, impl: str) -> dict:
+    """Times the fp32 RMSNorm + SwiGLU entry at the reference benchmark's
+    three shapes and the recurrence + out-projection entry at the decode
+    layer's shape (64 sequences, 32 v-heads, head_dim 128, hidden 4096, one
+    token), all through li_launch_* with the same arguments: impl "ours" calls
+    this library, impl "reference" the reference's kernels built from its
+    sources (oracle/_ref/libliref_gpu.so). Timing as the reference benchmark
+    (cuda/benchmark_fused.cu:126-137: warm-up, then back-to-back launches), but
+    with CUDA events; weight copies rotate so that the working set of
+    consecutive launches exceeds 3x the L2."""
+    import ctypes
+
+    import torch
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    if impl == "reference":
+        from oracle import oracle
+        if not oracle.REF_GPU.exists():
+            return {"impl": "reference", "unavailable": "the reference's kernels were not built (oracle/_ref)"}
+        lib = ctypes.CDLL(str(oracle.REF_GPU))
+    else:
+        from leaninfer_b200 import _lib
+        lib = _lib.load()
+    c_p, c_i, c_f, c_64, c_sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_int64, ctypes.c_size_t
+    sw = lib.li_launch_fused_rms_norm_swiglu_f32
+    sw.argtypes = [c_p] * 5 + [c_i, c_i, c_f, c_p]
+    sw.restype = None
+    rec = lib.li_launch_fused_deltanet_recurrent_out_f32
+    rec.argtypes = [c_p] * 9 + [c_64] * 4 + [c_i, c_64, c_64, c_sz, c_sz, c_sz, c_p]
+    rec.restype = None
+    stream = torch.cuda.current_stream()
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    peaks = measured_peaks()
+    cases = {}
+    g = torch.Generator(device=dev)
+    g.manual_seed(31)
+
+    def timed(fn, n_copies, iters):
+        for i in range(3):
+            fn(i % n_copies)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(iters):
+            fn(i % n_copies)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / iters * 1e3     # us per launch
+
+    for name, K, N in REF_SWIGLU_SHAPES:
+        wbytes = 2 * N * K * 4
+        n_copies = max(1, math.ceil(3 * l2 / wbytes) + 1) if wbytes < 3 * l2 else 1
+        Ws = [(0.02 * torch.randn(N, K, device=dev, generator=g), 0.02 * torch.randn(N, K, device=dev, generator=g))
+              for _ in range(n_copies)]
+        x = torch.randn(K, device=dev, generator=g)
+        gamma = torch.rand(K, device=dev, generator=g) + 0.5
+        h = torch.empty(N, device=dev)
+        fn = lambda i: sw(x.data_ptr(), gamma.data_ptr(), Ws[i][0].data_ptr(), Ws[i][1].data_ptr(), h.data_ptr(),
+                          K, N, 1e-5, stream.cuda_stream)
+        us = timed(fn, n_copies, 50)
+        by = wbytes + 2 * K * 4 + N * 4
+        cases[f"swiglu_f32 {name} K={K} N={N}"] = {"us": round(us, 2), "GB/s": round(by / us / 1e3, 1),
+                                                   "frac": round(by / us / 1e3 / peaks["hbm_gbs"], 4)}
+        del Ws
+    # recurrence + out-projection, decode layer shape, one token
+    B, H, gqa, D, hidden = 64, 32, 2, 128, 4096
+    q = torch.randn(B, H // gqa, 1, D, device=dev, generator=g)
+    k = torch.nn.functional.normalize(torch.randn(B, H // gqa, 1, D, device=dev, generator=g), dim=-1)
+    v = torch.randn(B, H, 1, D, device=dev, generator=g)
+    gg = -torch.rand(B, 1, H, device=dev, generator=g)
+    beta = torch.randn(B, 1, H, device=dev, generator=g)
+    states = [0.02 * torch.randn(B, H, D, D, device=dev, generator=g) for _ in range(2)]
+    W = 0.02 * torch.randn(hidden, H * D, device=dev, generator=g)
+    dsts = [torch.empty(B * H * D + B * H * D * D, device=dev) for _ in range(2)]
+    proj = torch.empty(hidden, device=dev)
+    fn = lambda i: rec(q.data_ptr(), k.data_ptr(), v.data_ptr(), gg.data_ptr(), beta.data_ptr(), states[i].data_ptr(),
+                       W.data_ptr(), dsts[i].data_ptr(), proj.data_ptr(), D, 1, H, gqa, 0, B, hidden, D, D, D * H,
+                       stream.cuda_stream)
+    us = timed(fn, 2, 50)
+    by = 2 * B * H * D * D * 4 + hidden * H * D * 4 + B * H * D * 4 * 3 + B * H * D * 4
+    cases[f"recurrent_out_f32 B={B} H={H} D={D} hidden={hidden}"] = {
+        "us": round(us, 2), "GB/s": round(by / us / 1e3, 1), "frac": round(by / us / 1e3 / peaks["hbm_gbs"], 4)}
+    big = cases[f"swiglu_f32 Qwen3-14B K=5120 N=17408"]
+    line = {"metric": "fp32 RMSNorm+SwiGLU GB/s (Qwen3-14B shape)", "value": big["GB/s"], "unit": "GB/s",
+            "n_gpus": 1, "steps": 50, "warmup": 3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "reference_kernel_shapes", "cases": cases,
+                       "l2": "weight copies rotate: consecutive launches touch more than 3x the L2"},
+            "roofline": {"bound": "hbm", "kernel": "li_launch_fused_rms_norm_swiglu_f32 at K=5120 N=17408",
+                         "achieved": big["GB/s"], "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": big["frac"],
+                         "peak_source": peaks["source"], "traffic": None},
+            "e2e": {"value": big["GB/s"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "gpu_launches": 50 * 4 if impl == "ours" else 0}
+    if impl == "reference":
+        line["impl"] = "reference"
+        line["note"] = "the reference's CUDA kernels (cuda/leaninfer-fused-{ffn,deltanet}.cu) built unchanged " \
+                       "for sm_100a; its recurrence's projection sums D/32 of the terms per head (less work)"
+    return line
+
+
 def run_reference(args, rank: int) -> dict | None:
     """The reference's CPU path for the workload (the oracle port: ggml's CPU
     ops are not vendored), on the host cores with all threads; rank 0 only."""
     if rank != 0:
         return None
+    if args.workload == "refgpu":
+        return run_refgpu(args, "reference")
     if args.workload != "decode":
         if args.workload == "stack":
             cb = cpu_baseline_stack(args.layers, args.ctx)
@@ -999,7 +1136,7 @@ def main():
     ap.add_argument("--layers", type=int, default=64, help="stack: layers (3 DeltaNet : 1 attention)")
     ap.add_argument("--ctx", type=int, default=4096, help="stack: attention context (KV cache length)")
     ap.add_argument("--tp-ffn", action="store_true", help="stack: shard the FFN weights across the GPUs (NCCL)")
-    ap.add_argument("--workload", choices=["decode", "prefill", "qkv", "ffn", "stack"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "qkv", "ffn", "stack", "refgpu"], default="decode",
                     help="decode: the fused DeltaNet layer decode step (the headline); prefill: one 8192-token "
                          "chunked prefill + gated norm + bf16 out-projection; qkv: RMSNorm + Q/K/V Q8_0 GEMV "
                          "(K=2048, one token); ffn: RMSNorm + SwiGLU FFN 4096 -> 12288 -> 4096 (--batch rows, "
@@ -1044,6 +1181,8 @@ def main():
             line = run_prefill(args, rank, world, dist)
         elif args.workload == "stack":
             line = run_stack(args, rank, world, dist)
+        elif args.workload == "refgpu":
+            line = run_refgpu(args, "ours") if rank == 0 else None
         elif args.workload in ("qkv", "ffn"):
             line = run_gemv(args, rank, world, dist)
         else:

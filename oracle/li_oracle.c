@@ -654,17 +654,37 @@ static void layer_head_body(void *cp, int64_t idx) {
  * a_softplus, g_in, delta_net_fused_raw, attn_out_norm, linear_attn_out);
  * the recurrence is gdr_token (reference kernel arithmetic), the gated norm
  * lio_silu_gate's, the projections lio_rms_norm_matmul's. */
+typedef int (*lio_matmul_fn)(int, const float *, const float *, const void *, float *, int, int, int, float);
+
+static int layer_decode_impl(const lio_deltanet_layer *L, const float *x,
+                             float *y, float *conv_state, float *state,
+                             int n_seqs, float *taps, lio_matmul_fn mm);
+
 int lio_deltanet_layer_decode(const lio_deltanet_layer *L, const float *x,
                               float *y, float *conv_state, float *state,
                               int n_seqs, float *taps) {
+    return layer_decode_impl(L, x, y, conv_state, state, n_seqs, taps, lio_rms_norm_matmul);
+}
+
+/* The same step with both projections in ggml's CPU arithmetic (activations
+ * quantized to q8_K / q8_0, integer dots: lio_rms_norm_matmul_q8act), the
+ * form ggml's CPU backend runs; UNPINNED, for the timed CPU baseline only. */
+int lio_deltanet_layer_decode_q8act(const lio_deltanet_layer *L, const float *x,
+                                    float *y, float *conv_state, float *state,
+                                    int n_seqs) {
+    return layer_decode_impl(L, x, y, conv_state, state, n_seqs, NULL, lio_rms_norm_matmul_q8act);
+}
+
+static int layer_decode_impl(const lio_deltanet_layer *L, const float *x,
+                             float *y, float *conv_state, float *state,
+                             int n_seqs, float *taps, lio_matmul_fn mm) {
     const int D = L->head_dim, Hk = L->n_k_heads, Hv = L->n_v_heads;
     const int K = L->conv_kernel, hid = L->hidden;
     if (Hk <= 0 || Hv % Hk) return -1;
     const int C = 2 * Hk * D + Hv * D;                 /* conv channels   */
     const int NI = C + Hv * D + 2 * Hv;                /* in-proj rows    */
     float *p = (float *)malloc(sizeof(float) * (size_t)NI * n_seqs);
-    int rc = lio_rms_norm_matmul(L->w_in_type, x, L->in_norm_w, L->w_in, p, hid, NI,
-                                 n_seqs, L->in_norm_eps);
+    int rc = mm(L->w_in_type, x, L->in_norm_w, L->w_in, p, hid, NI, n_seqs, L->in_norm_eps);
     if (rc) { free(p); return rc; }
     float *og = (float *)malloc(sizeof(float) * (size_t)Hv * D * n_seqs);
     double *act = (double *)malloc(sizeof(double) * (size_t)C * n_seqs);
@@ -703,7 +723,7 @@ int lio_deltanet_layer_decode(const lio_deltanet_layer *L, const float *x,
     }
     layer_ctx lc = {L, p, act, qkn, state, og, taps, C, NI, tps};
     parallel_for((int64_t)n_seqs * Hv, 1, layer_head_body, &lc);
-    rc = lio_rms_norm_matmul(L->w_out_type, og, NULL, L->w_out, y, Hv * D, hid, n_seqs, 0.f);
+    rc = mm(L->w_out_type, og, NULL, L->w_out, y, Hv * D, hid, n_seqs, 0.f);
     free(qkn);
     free(act);
     free(og);

@@ -81,6 +81,12 @@ int lio_deltanet_layer_decode(const lio_deltanet_layer *L, const float *x,
                               float *y, float *conv_state, float *state,
                               int n_seqs, float *taps);
 
+/* The same step with the projections in ggml's CPU arithmetic (quantized
+ * activations, integer dots); UNPINNED, the timed CPU baseline's form. */
+int lio_deltanet_layer_decode_q8act(const lio_deltanet_layer *L, const float *x,
+                                    float *y, float *conv_state, float *state,
+                                    int n_seqs);
+
 /* Sequential gated delta rule over T tokens, one sequence, in the token-major
  * layout of the prefill entry: q, k bf16 (as uint16) [T, Hk, D]; v bf16
  * [T, Hv, D]; g, beta fp32 [T, Hv] (beta already a probability, g the

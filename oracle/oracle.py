@@ -106,6 +106,7 @@ def _load(path: Path) -> None:
     L.lio_deltanet_taps_per_seq.restype = c_size_t
     L.lio_deltanet_layer_decode.argtypes = [POINTER(Layer), c_void_p, c_void_p, c_void_p, c_void_p, c_int,
                                             c_void_p]
+    L.lio_deltanet_layer_decode_q8act.argtypes = [POINTER(Layer), c_void_p, c_void_p, c_void_p, c_void_p, c_int]
     L.lio_gdr_prefill.argtypes = [c_void_p] * 7 + [c_int, c_int, c_int, c_int, c_float]
     L.lio_fp16_to_fp32.argtypes = [c_uint16]
     L.lio_fp16_to_fp32.restype = c_float
@@ -261,6 +262,26 @@ def attn_layer_decode(layer, keep, x, k_cache, v_cache, pos):
     assert lib().lio_attn_layer_decode(ctypes.byref(layer), _ptr(x), _ptr(y), _ptr(k_cache), _ptr(v_cache),
                                        _ptr(pos), n, max_ctx) == 0
     return y
+
+
+def deltanet_layer_decode_q8act(layer, keep, x, conv_state, state):
+    """One step with ggml-style quantized-activation projections (the CPU
+    baseline's arithmetic; unpinned); states updated in place."""
+    x = _f32(np.atleast_2d(x))
+    n = x.shape[0]
+    y = np.empty((n, layer.hidden), np.float32)
+    assert lib().lio_deltanet_layer_decode_q8act(ctypes.byref(layer), _ptr(x), _ptr(y), _ptr(conv_state),
+                                                 _ptr(state), n) == 0
+    return y
+
+
+def ffn_q8act(wtype, x, gamma, Wg, Wu, Wd, N, eps=1e-6):
+    """The SwiGLU FFN with ggml-style quantized-activation matmuls (the CPU
+    baseline's arithmetic; unpinned)."""
+    g = rms_norm_matmul_q8act(wtype, x, gamma, Wg, N, eps)
+    u = rms_norm_matmul_q8act(wtype, x, gamma, Wu, N, eps)
+    h = (g / (1.0 + np.exp(-g.astype(np.float64))) * u).astype(np.float32)
+    return rms_norm_matmul_q8act(wtype, h, None, Wd, np.atleast_2d(x).shape[1])
 
 
 def gdr_prefill(q_bf16, k_bf16, v_bf16, g, beta, state, scale):

@@ -27,3 +27,19 @@ def test_reference_arm_prints_one_contract_line(args):
     assert d["cpu_baseline"]["value"] == d["value"] and d["cpu_baseline"]["sample"]
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     assert "workload" in d["config"]
+
+
+def test_traffic_constant_matches_the_committed_capture():
+    """roofline.traffic of the default line is the per-step DRAM traffic of
+    the committed ncu summary (its table's per-launch bytes, summed per step
+    and averaged), so the number can be recomputed from profiles/."""
+    import re
+    import bench
+    text = (ROOT / "profiles" / "layer_decode_q4k_b64_traffic.md").read_text()
+    rows = re.findall(r"^\| (\d) \| [^|]+ \| ([\d,]+) \| ([\d,]+) \|", text, flags=re.M)
+    assert len(rows) == 8
+    per = [int(a.replace(",", "")) + int(b.replace(",", "")) for _, a, b in rows]
+    steps = [sum(per[0:4]), sum(per[4:8])]
+    mean = sum(steps) // 2
+    assert f"traffic_bytes_per_step_mean: {mean}" in text
+    assert bench.NCU_TRAFFIC[64] == mean
