@@ -988,6 +988,8 @@ def run_refgpu(args, impl: str) -> dict:
     import ctypes
 
     import torch
+    if not torch.cuda.is_available():
+        return {"impl": impl, "unavailable": "no CUDA device: the reference's kernels need a GPU"}
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
     if impl == "reference":

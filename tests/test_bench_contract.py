@@ -12,7 +12,8 @@ import pytest
 from conftest import ROOT
 
 
-@pytest.mark.parametrize("args", [["--batch", "2"], ["--workload", "qkv"], ["--workload", "ffn", "--batch", "1"]])
+@pytest.mark.parametrize("args", [["--batch", "2"], ["--workload", "qkv"], ["--workload", "ffn", "--batch", "1"],
+                                  ["--workload", "stack", "--layers", "4", "--ctx", "512"]])
 def test_reference_arm_prints_one_contract_line(args):
     r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1",
                         "--warmup", "3", *args], capture_output=True, text=True, timeout=600, cwd=ROOT)
@@ -43,3 +44,22 @@ def test_traffic_constant_matches_the_committed_capture():
     mean = sum(steps) // 2
     assert f"traffic_bytes_per_step_mean: {mean}" in text
     assert bench.NCU_TRAFFIC[64] == mean
+
+
+def test_reference_gpu_arm_without_gpu_reports_unavailable():
+    r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--workload", "refgpu",
+                        "--steps", "1", "--warmup", "3"], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [json.loads(ln) for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1 and lines[0]["impl"] == "reference" and "unavailable" in lines[0]
+
+
+def test_stack_launch_count_and_bytes():
+    """The stack's kernel count per step and algorithmic bytes (64 layers,
+    256 sequences, context 4096 on one GPU: about 162 GB, the figure the
+    workload's definition gives)."""
+    import bench
+    by = bench.stack_bytes(64, 256, 4096, 1)
+    assert 150e9 < by["total"] < 170e9
+    assert bench.stack_bytes(64, 32, 4096, 8)["weights"] < by["weights"]
+    assert bench.stack_launches(64, 256, 1) == 48 * (4 + 4 + 2) + 16 * (2 + 3 + 2 + 4 + 2)
