@@ -166,6 +166,12 @@ __device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gsrc, uint3
         : "memory");
 }
 
+// Hint: bring `bytes` (a multiple of 16, 16-byte aligned) of global memory into
+// L2 ahead of use (bulk async, nothing to wait for).
+__device__ __forceinline__ void bulk_prefetch_l2(const void *gsrc, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gsrc), "r"(bytes) : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // Programmatic dependent launch (sm_90+): a kernel launched with the
 // programmatic-serialization attribute may start while its predecessor in

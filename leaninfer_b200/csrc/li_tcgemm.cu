@@ -304,6 +304,17 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
             }
             for (int j = issued - p.XS < 0 ? 0 : issued - p.XS; j < issued; ++j)
                 mbar_wait(&x_full[j % p.XS], (uint32_t)((j / p.XS) & 1));
+        } else if (lane == 2 && EPI == kTcConv && row0 < a.conv_channels && a.conv_channels % 4 == 0 &&
+                   ((uintptr_t)a.conv_state & 15u) == 0) {
+            // the epilogue's conv-state rows into L2 while the tile runs: they
+            // were last written by the previous step (finished before this
+            // step's first, non-dependent launch), and come from DRAM otherwise
+            // (measured: the conv epilogue is 7 of the 27 us of this kernel at
+            // 64 sequences and hidden 4096). A bulk prefetch needs 16-byte
+            // aligned rows of a multiple of 16 bytes: 4k channels of 12 bytes.
+            const int nrow = a.conv_channels - row0 < kBM ? a.conv_channels - row0 : kBM;
+            for (int b = 0; b < a.B; ++b)
+                bulk_prefetch_l2(a.conv_state + ((size_t)b * a.conv_channels + row0) * 3, (uint32_t)nrow * 12u);
         }
     } else if (warp >= issuer0) {
         // ------------- MMA issuer of group grp (lane 0) -------------
