@@ -65,7 +65,7 @@ def kernels_per_step(batch: int) -> int:
         return 3      # in-projection GEMV, recurrence, out-projection GEMV
     if batch <= TCX_MAX_ROWS:
         return 6      # x prep, in-projection GEMM + reduce, recurrence, out-projection GEMM + reduce
-    return 4          # x prep, in-projection GEMM, recurrence, out-projection GEMM
+    return 5          # x prep, in-projection GEMM (K split) + conv finish, recurrence, out-projection GEMM
 
 
 def algorithmic_bytes(batch: int, state_bytes: int = 4) -> int:
@@ -329,7 +329,8 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
                    "parallelism": f"sequence-sharded x{world}, no collectives",
                    "l2": f"inputs larger than L2: rotating {n_inst} layer instances of {per_inst / 1e6:.1f} MB"},
         "roofline": {"bound": "hbm", "kernel": "deltanet layer decode step: " + (
-                         "x prep + tcgen05 in-projection + recurrence + tcgen05 out-projection" if B >= TC_MIN_ROWS else
+                         "x prep + tcgen05 in-projection (+ conv finish) + recurrence + tcgen05 out-projection"
+                         if B >= TC_MIN_ROWS else
                          "in-projection GEMV + recurrence + out-projection GEMV") + " (PDL-chained)",
                      "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],

@@ -600,6 +600,12 @@ static int layer_decode(const li_deltanet_layer *L, const float *x, float *y, fl
     in.conv_w = L->conv_w; in.conv_state = conv_state; in.conv_channels = C;
     in.partials = partials;
     in.x_npad = tc_gemm_x_npad(in);
+    if (tc_gemm_splits_k(in)) {
+        // the K-split in-projection adds its partial sums into proj (the conv
+        // epilogue follows in its own kernel)
+        const cudaError_t e = cudaMemsetAsync(proj, 0, (size_t)NI * n * sizeof(float), s);
+        if (e != cudaSuccess) return (int)e;
+    }
     if ((rc = tc_prep_launch(x, L->hidden, L->in_norm_w, L->in_norm_eps, n_seqs, L->hidden, x16, xscale, s,
                              false, in.x_npad)))
         return rc;

