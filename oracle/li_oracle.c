@@ -315,53 +315,84 @@ typedef struct {
     size_t rb;
     const int8_t *q;
     const float *d;
+    const int32_t *bs;   /* per activation row: sums of its 32-value groups (ggml's q8_K bsums) */
     float *dst;
     int K, N, n_rows;
 } q8_ctx;
 
+/* One weight row against every activation row. The row is unpacked once
+ * (4-bit codes to int8, scales and mins to ints), then each row's dot is a
+ * plain int8 x int8 -> int32 loop per 32-value group, which the compiler
+ * vectorises (the integer dots of ggml's vec_dot kernels); the integer sums
+ * and their float combination are the same as before, so the result is
+ * unchanged bit for bit. */
 static void q8_body(void *cp, int64_t n) {
     q8_ctx *c = (q8_ctx *)cp;
     const uint8_t *row = c->W + c->rb * n;
-    for (int r = 0; r < c->n_rows; ++r) {
-        const int8_t *q = c->q + (size_t)r * c->K;
-        const float *d = c->d + (size_t)r * (c->K / (c->wtype == 12 ? 256 : 32));
-        double acc = 0;
-        if (c->wtype == 12) {
-            for (int b = 0; b < c->K / 256; ++b) {
-                const uint8_t *blk = row + 144 * (size_t)b;
-                uint16_t dh, mh;
-                memcpy(&dh, blk, 2);
-                memcpy(&mh, blk + 2, 2);
-                int64_t s_sc = 0, s_mn = 0;
-                for (int j = 0; j < 8; ++j) {
-                    int sc, mn;
-                    q4k_scale_min(blk + 4, j, &sc, &mn);
-                    const uint8_t *src = blk + 16 + 32 * (j / 2);
-                    const int8_t *qj = q + 256 * b + 32 * j;
-                    int64_t dot = 0, sum = 0;
-                    for (int i = 0; i < 32; ++i) {
-                        dot += (int64_t)((src[i] >> ((j & 1) ? 4 : 0)) & 0x0f) * qj[i];
-                        sum += qj[i];
-                    }
-                    s_sc += sc * dot;
-                    s_mn += mn * sum;
-                }
-                acc += (double)lio_fp16_to_fp32(dh) * d[b] * (double)s_sc -
-                       (double)lio_fp16_to_fp32(mh) * d[b] * (double)s_mn;
-            }
-        } else {
-            for (int b = 0; b < c->K / 32; ++b) {
-                const uint8_t *blk = row + 34 * (size_t)b;
-                uint16_t dh;
-                memcpy(&dh, blk, 2);
-                const int8_t *w = (const int8_t *)(blk + 2);
-                int64_t dot = 0;
-                for (int i = 0; i < 32; ++i) dot += (int64_t)w[i] * q[32 * b + i];
-                acc += (double)lio_fp16_to_fp32(dh) * d[b] * (double)dot;
+    const int K = c->K;
+    int8_t *wq = (int8_t *)malloc((size_t)K);
+    if (c->wtype == 12) {
+        const int nb = K / 256;
+        int *sc = (int *)malloc(sizeof(int) * 16 * (size_t)nb);
+        int *mn = sc + 8 * nb;
+        double *dd = (double *)malloc(sizeof(double) * 2 * (size_t)nb);
+        for (int b = 0; b < nb; ++b) {
+            const uint8_t *blk = row + 144 * (size_t)b;
+            uint16_t dh, mh;
+            memcpy(&dh, blk, 2);
+            memcpy(&mh, blk + 2, 2);
+            dd[2 * b] = lio_fp16_to_fp32(dh);
+            dd[2 * b + 1] = lio_fp16_to_fp32(mh);
+            for (int j = 0; j < 8; ++j) {
+                q4k_scale_min(blk + 4, j, &sc[8 * b + j], &mn[8 * b + j]);
+                const uint8_t *src = blk + 16 + 32 * (j / 2);
+                for (int i = 0; i < 32; ++i) wq[256 * b + 32 * j + i] = (int8_t)((src[i] >> ((j & 1) ? 4 : 0)) & 0x0f);
             }
         }
-        c->dst[(size_t)r * c->N + n] = (float)acc;
+        for (int r = 0; r < c->n_rows; ++r) {
+            const int8_t *q = c->q + (size_t)r * K;
+            const float *d = c->d + (size_t)r * nb;
+            const int32_t *bs = c->bs + (size_t)r * (K / 32);
+            double acc = 0;
+            for (int b = 0; b < nb; ++b) {
+                int32_t s_sc = 0, s_mn = 0;
+                for (int j = 0; j < 8; ++j) {
+                    const int8_t *wj = wq + 256 * b + 32 * j, *qj = q + 256 * b + 32 * j;
+                    int32_t dot = 0;
+                    for (int i = 0; i < 32; ++i) dot += (int32_t)wj[i] * (int32_t)qj[i];
+                    s_sc += sc[8 * b + j] * dot;
+                    s_mn += mn[8 * b + j] * bs[8 * b + j];
+                }
+                acc += dd[2 * b] * d[b] * (double)s_sc - dd[2 * b + 1] * d[b] * (double)s_mn;
+            }
+            c->dst[(size_t)r * c->N + n] = (float)acc;
+        }
+        free(dd);
+        free(sc);
+    } else {
+        const int nb = K / 32;
+        double *dd = (double *)malloc(sizeof(double) * (size_t)nb);
+        for (int b = 0; b < nb; ++b) {
+            const uint8_t *blk = row + 34 * (size_t)b;
+            uint16_t dh;
+            memcpy(&dh, blk, 2);
+            dd[b] = lio_fp16_to_fp32(dh);
+            memcpy(wq + 32 * b, blk + 2, 32);
+        }
+        for (int r = 0; r < c->n_rows; ++r) {
+            const int8_t *q = c->q + (size_t)r * K;
+            const float *d = c->d + (size_t)r * nb;
+            double acc = 0;
+            for (int b = 0; b < nb; ++b) {
+                int32_t dot = 0;
+                for (int i = 0; i < 32; ++i) dot += (int32_t)wq[32 * b + i] * (int32_t)q[32 * b + i];
+                acc += dd[b] * d[b] * (double)dot;
+            }
+            c->dst[(size_t)r * c->N + n] = (float)acc;
+        }
+        free(dd);
     }
+    free(wq);
 }
 
 int lio_rms_norm_matmul_q8act(int wtype, const float *x, const float *gamma,
@@ -385,8 +416,15 @@ int lio_rms_norm_matmul_q8act(int wtype, const float *x, const float *gamma,
         }
         q8act_row(xn, K, qk, q + (size_t)r * K, d + (size_t)r * (K / qk));
     }
-    q8_ctx c = {wtype, (const uint8_t *)W, rb, q, d, dst, K, N, n_rows};
+    int32_t *bs = (int32_t *)malloc(sizeof(int32_t) * (size_t)(K / 32) * n_rows);
+    for (int64_t g = 0; g < (int64_t)(K / 32) * n_rows; ++g) {
+        int32_t t = 0;
+        for (int i = 0; i < 32; ++i) t += q[32 * g + i];
+        bs[g] = t;
+    }
+    q8_ctx c = {wtype, (const uint8_t *)W, rb, q, d, bs, dst, K, N, n_rows};
     parallel_for(N, 16, q8_body, &c);
+    free(bs);
     free(xn);
     free(q);
     free(d);
