@@ -29,6 +29,8 @@
 #include "li_qgemv.cuh"
 #include "li_tcgemm.cuh"
 
+#include <mutex>
+
 LI_DEFINE_TU_STATUS(attn)
 
 namespace li {
@@ -116,13 +118,6 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(AttnArgs a, int B) {
     }
 }
 
-__device__ __forceinline__ uint4 ld_nc_u4(const void *p) {
-    uint4 r;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
-    return r;
-}
-
 __device__ __forceinline__ void h8_to_f(const uint4 u, float (&f)[8]) {
     const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -133,16 +128,39 @@ __device__ __forceinline__ void h8_to_f(const uint4 u, float (&f)[8]) {
     }
 }
 
+// 16 bytes global -> shared, asynchronous (zero-filled when !valid: a cache
+// slot past the context may hold anything).
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(smem_dst)), "l"(gsrc),
+                 "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Per warp and stage: the K and V rows of one sub-chunk, [K, V][kSub tokens][256 B].
+constexpr int kStageBytes = 2 * kSub * kD * 2;
+constexpr size_t kDecSmem = (size_t)4 * 2 * kStageBytes;   // 4 warps x 2 stages = 64 KB
+
 // ---------------------------------------------------------------------------
 // attn_decode: CTA (chunk, kv head j, sequence s), 4 warps. In a warp, lane
 // l works on token (l / 16) of each pair of tokens and on dims 8*(l % 16) ..
 // +7 of it; every q head of the group is held in registers for those dims.
+// Each warp streams its tokens through two shared-memory stages with
+// cp.async: the next sub-chunk's K and V rows are in flight while the current
+// one is computed. A lane copies exactly the 16-byte pieces it reads later, so
+// its own cp.async.wait_group is all the ordering it needs.
 // ---------------------------------------------------------------------------
 template <int G>
 __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(AttnArgs a) {
+    extern __shared__ __align__(16) uint8_t kv_smem[];   // [warp][stage][K, V][kSub][256 B]
     __shared__ float sc[4][G][kSub];                 // scores, then probabilities
     __shared__ float wm[4][G], wl[4][G];
-    __shared__ __align__(16) float wo[4][G][kD];
+    // each warp's partial o[G][D] for the merge, in its own staging area once
+    // its loop is done (keeps the CTA at 65 KB of shared memory: 3 per SM)
+    auto wo = [&](int w, int g) -> float * {
+        return reinterpret_cast<float *>(kv_smem + (size_t)w * 2 * kStageBytes) + (size_t)g * kD;
+    };
     grid_dep_wait();
     grid_dep_launch_dependents();
     const int chunk = blockIdx.x, j = blockIdx.y, s = blockIdx.z;
@@ -175,19 +193,38 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(AttnArgs a) {
     const size_t row_stride = (size_t)a.Hkv * kD;   // halves between consecutive tokens
     const __half *kbase = a.k_cache + ((size_t)s * a.max_ctx * a.Hkv + j) * kD + 8 * c;
     const __half *vbase = a.v_cache + ((size_t)s * a.max_ctx * a.Hkv + j) * kD + 8 * c;
-
-    for (int tb = wb; tb < we; tb += kSub) {
-        // scores of kSub tokens (kSub/2 iterations of one token per half-warp)
-        uint4 kr[kSub / 2];
+    uint8_t *wbuf = kv_smem + (size_t)warp * 2 * kStageBytes;
+    // this lane's 16-byte piece of row r of stage st: K at +0, V at +kSub*256
+    auto piece = [&](int st, int r, int kv) -> uint8_t * {
+        return wbuf + (size_t)st * kStageBytes + (size_t)kv * kSub * kD * 2 + (size_t)r * kD * 2 + 16 * c;
+    };
+    auto issue = [&](int tb, int st) {
 #pragma unroll
         for (int it = 0; it < kSub / 2; ++it) {
-            const int t = tb + 2 * it + hw;
-            kr[it] = t < we ? ld_nc_u4(kbase + (size_t)t * row_stride) : make_uint4(0u, 0u, 0u, 0u);
+            const int r = 2 * it + hw, t = tb + r;
+            const bool ok = t < we;
+            const size_t off = (size_t)(ok ? t : wb) * row_stride;
+            cp_async16(piece(st, r, 0), kbase + off, ok);
+            cp_async16(piece(st, r, 1), vbase + off, ok);
         }
+        cp_async_commit();
+    };
+    if (wb < we) issue(wb, 0);
+
+    int st = 0;
+    for (int tb = wb; tb < we; tb += kSub, st ^= 1) {
+        // the next sub-chunk goes in flight, then this one must have landed
+        if (tb + kSub < we) {
+            issue(tb + kSub, st ^ 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        // scores of kSub tokens (kSub/2 iterations of one token per half-warp)
 #pragma unroll
         for (int it = 0; it < kSub / 2; ++it) {
             float kf[8];
-            h8_to_f(kr[it], kf);
+            h8_to_f(*reinterpret_cast<const uint4 *>(piece(st, 2 * it + hw, 0)), kf);
             const int t = tb + 2 * it + hw;
 #pragma unroll
             for (int g = 0; g < G; ++g) {
@@ -221,17 +258,11 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(AttnArgs a) {
             if (lane < kSub) sc[warp][g][lane] = pv;
         }
         __syncwarp();
-        // weighted V rows
-        uint4 vr[kSub / 2];
-#pragma unroll
-        for (int it = 0; it < kSub / 2; ++it) {
-            const int t = tb + 2 * it + hw;
-            vr[it] = t < we ? ld_nc_u4(vbase + (size_t)t * row_stride) : make_uint4(0u, 0u, 0u, 0u);
-        }
+        // weighted V rows (zero-filled past the warp's range)
 #pragma unroll
         for (int it = 0; it < kSub / 2; ++it) {
             float vf[8];
-            h8_to_f(vr[it], vf);
+            h8_to_f(*reinterpret_cast<const uint4 *>(piece(st, 2 * it + hw, 1)), vf);
 #pragma unroll
             for (int g = 0; g < G; ++g) {
                 const float pw = sc[warp][g][2 * it + hw];
@@ -246,11 +277,12 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(AttnArgs a) {
     for (int g = 0; g < G; ++g)
 #pragma unroll
         for (int d = 0; d < 8; ++d) o[g][d] += __shfl_xor_sync(0xffffffffu, o[g][d], 16);
+    __syncwarp();   // every lane of this warp is past its last read of the staging area
     if (lane < 16) {
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            *reinterpret_cast<float4 *>(&wo[warp][g][8 * c]) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
-            *reinterpret_cast<float4 *>(&wo[warp][g][8 * c + 4]) = make_float4(o[g][4], o[g][5], o[g][6], o[g][7]);
+            *reinterpret_cast<float4 *>(wo(warp, g) + 8 * c) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
+            *reinterpret_cast<float4 *>(wo(warp, g) + 8 * c + 4) = make_float4(o[g][4], o[g][5], o[g][6], o[g][7]);
         }
     }
     if (lane == 0) {
@@ -270,7 +302,7 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(AttnArgs a) {
         for (int w = 0; w < 4; ++w) {
             const float f = wm[w][g] == -INFINITY ? 0.f : __expf(wm[w][g] - M);
             L = fmaf(wl[w][g], f, L);
-            O = fmaf(wo[w][g][d], f, O);
+            O = fmaf(wo(w, g)[d], f, O);
         }
         float *rec = a.part + (((size_t)s * a.Hq + (size_t)j * G + g) * a.n_chunk + chunk) * kPartStride;
         rec[4 + d] = O;
@@ -302,8 +334,15 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(AttnArgs a) {
 
 template <int G>
 int launch_decode(const AttnArgs &a, int B, cudaStream_t s) {
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [] {
+        attr_err = cudaFuncSetAttribute(attn_decode_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)kDecSmem);
+    });
+    if (attr_err != cudaSuccess) return (int)attr_err;
     return (int)launch_pdl(attn_decode_kernel<G>, dim3((unsigned)a.n_chunk, (unsigned)a.Hkv, (unsigned)B),
-                           dim3(kDecThreads), 0, s, true, a);
+                           dim3(kDecThreads), kDecSmem, s, true, a);
 }
 
 int launch_decode_any(int G, const AttnArgs &a, int B, cudaStream_t s) {
