@@ -18,10 +18,13 @@ than 3x the L2 capacity of traffic.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl reference]
 
-Other workloads (`--workload`): `prefill` (one 8192-token chunked prefill +
-gated norm + bf16 out-projection), `qkv` (RMSNorm + Q/K/V Q8_0 GEMV, K = 2048,
-one token) and `ffn` (RMSNorm + SwiGLU FFN 4096 -> 12288 -> 4096, `--batch`
-rows, `--wtype` 12 = Q4_K or 8 = Q8_0).
+Other workloads (`--workload`): `layerffn` (the same layer followed by the
+SwiGLU FFN 4096 -> 12288 -> 4096, a residual add after each), `prefill` (one
+8192-token chunked prefill + gated norm + bf16 out-projection), `qkv`
+(RMSNorm + Q/K/V Q8_0 GEMV, K = 2048, one token), `ffn` (RMSNorm + SwiGLU FFN
+4096 -> 12288 -> 4096, `--batch` rows, `--wtype` 12 = Q4_K or 8 = Q8_0),
+`stack` (the 64-layer hybrid decode stack) and `refgpu` (the reference's own
+kernels next to this library's entries).
 """
 from __future__ import annotations
 
@@ -65,7 +68,9 @@ def kernels_per_step(batch: int) -> int:
         return 3      # in-projection GEMV, recurrence, out-projection GEMV
     if batch <= TCX_MAX_ROWS:
         return 6      # x prep, in-projection GEMM + reduce, recurrence, out-projection GEMM + reduce
-    return 5          # x prep, in-projection GEMM (K split) + conv finish, recurrence, out-projection GEMM
+    # x prep, in-projection GEMM (one CTA per 128-row tile: 97 tiles, no K
+    # split, the conv epilogue inside), recurrence, out-projection GEMM
+    return 4
 
 
 def algorithmic_bytes(batch: int, state_bytes: int = 4) -> int:
@@ -956,6 +961,192 @@ def cpu_baseline_stack(n_layers: int, ctx: int) -> dict:
                       f"for {n_layers} layers", "seconds": round(t_dn + t_at + t_ffn, 3)}
 
 
+# --------------------------------------------------------------------------
+# DeltaNet + FFN decode layer: the headline's Gated DeltaNet layer followed by
+# the SwiGLU FFN 4096 -> 12288 -> 4096 (Q4_K), a residual add after each, one
+# li_launch_stack_decode call per step
+# --------------------------------------------------------------------------
+LF_METRIC = "deltanet+ffn layer decode tokens/s"
+
+
+def layerffn_bytes(batch: int) -> int:
+    """Algorithmic bytes of one DeltaNet+FFN layer step: the DeltaNet layer's
+    (algorithmic_bytes: weights, states, x in and y out), the FFN's Q4_K
+    weights and norm weights once, and per sequence the residual stream into
+    and out of the FFN sub-layer."""
+    ffn_w = 2 * q4k_bytes(FFN_N, FFN_K) + q4k_bytes(FFN_K, FFN_N) + FFN_K * 4
+    return algorithmic_bytes(batch) + ffn_w + batch * HIDDEN * 4 * 2
+
+
+def layerffn_launches(batch: int) -> int:
+    """Kernels of the library per step: the DeltaNet layer's, the FFN's and
+    the two residual adds."""
+    return kernels_per_step(batch) + gemv_launches("ffn", batch) + 2
+
+
+def build_layerffn(dev, batch: int, n_inst: int, seed: int) -> list:
+    """Independent one-layer stacks (weights drawn on the device with the
+    synth distributions: random-code Q4_K blocks; states N(0, 0.02))."""
+    import torch
+    from leaninfer_b200.stack import HybridStackDecode, random_q4_k_device
+    insts = []
+    for i in range(n_inst):
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed * 1000 + i)
+        u = lambda *shape: torch.rand(*shape, device=dev, generator=g)
+        q4 = lambda n, k: random_q4_k_device(n, k, dev, g)
+        l = dict(kind="deltanet", hidden=HIDDEN, n_k_heads=HK, n_v_heads=HV, head_dim=D, wtype=12,
+                 w_in=q4(N_IN, HIDDEN), w_out=q4(HIDDEN, HV * D),
+                 conv_w=0.1 * torch.randn(CONV_CH, 4, device=dev, generator=g),
+                 a_log=0.5 * torch.randn(HV, device=dev, generator=g), dt_bias=torch.zeros(HV, device=dev),
+                 norm_w=u(D) + 0.5, in_norm_w=(u(HIDDEN) + 0.5) / 128.0,
+                 conv_state=0.1 * torch.randn(batch, CONV_CH, 3, device=dev, generator=g),
+                 state=0.02 * torch.randn(batch, HV, D, D, device=dev, generator=g))
+        l["ffn"] = dict(wtype=12, hidden=HIDDEN, n_inner=FFN_N, norm_w=(u(HIDDEN) + 0.5) / 128.0,
+                        w_gate=q4(FFN_N, HIDDEN), w_up=q4(FFN_N, HIDDEN), w_down=q4(HIDDEN, FFN_N))
+        stack = HybridStackDecode([l], n_seqs=batch, max_ctx=1)
+        insts.append(dict(layer=l, stack=stack, x=torch.randn(batch, HIDDEN, device=dev, generator=g),
+                          pos=torch.zeros(batch, dtype=torch.int32, device=dev)))
+    return insts
+
+
+def run_layerffn(args, rank: int, world: int, dist) -> dict | None:
+    """One step = one token for each of the B sequences of this rank through
+    the DeltaNet+FFN layer (x += deltanet(x); x += ffn(x)). Sequences shard
+    across ranks with no data-path communication (weak scaling); steps rotate
+    over layer instances so that consecutive uses of one are separated by more
+    than 3x the L2 capacity of traffic."""
+    import torch
+    from leaninfer_b200 import ops
+    from leaninfer_b200.shard import max_over_ranks, shard_bounds
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    _, B = shard_bounds(args.batch * world, world, rank)
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    per_inst = layerffn_bytes(B)
+    n_inst = max(2, math.ceil(3 * l2 / per_inst) + 1)
+    insts = build_layerffn(dev, B, n_inst, seed=rank + 1)
+    stream = torch.cuda.current_stream()
+
+    def launch(it):
+        it["stack"].step(it["x"], it["pos"])
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for it in insts:
+            launch(it)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    for it in insts:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            launch(it)
+        it["graph"] = g
+    torch.cuda.synchronize()
+    timed = chained_graphs(insts, launch, args.steps)
+    for i in range(args.warmup):
+        insts[i % n_inst]["graph"].replay()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    sampler = ClockSampler(dev.index)
+    sampler.start()
+    time.sleep(0.3)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t_wall0 = time.time()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    timed()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    ms = e0.elapsed_time(e1)
+    sampler.stop()
+    clocks = sampler.summary(t_wall0, t_wall1)
+    status = ops.device_status()
+    if status:
+        raise RuntimeError(f"device status {status} after the timed region")
+    # e2e: each step's x from pinned host memory in and the residual stream out
+    hx = [it["x"].cpu().pin_memory() for it in insts]
+    hy = [torch.empty_like(h).pin_memory() for h in hx]
+    e_steps = max(1, min(args.steps, 200))
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0.record(stream)
+    for i in range(e_steps):
+        it = insts[i % n_inst]
+        it["x"].copy_(hx[i % n_inst], non_blocking=True)
+        it["graph"].replay()
+        hy[i % n_inst].copy_(it["x"], non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if dist:
+        dist.barrier()
+    ms, e2e_ms = max_over_ranks([ms, e2e_ms], dist, device=dev)
+    if rank != 0:
+        return None
+    peaks = measured_peaks()
+    step_s = ms / 1e3 / args.steps
+    achieved = layerffn_bytes(B) / step_s / 1e9
+    line = {
+        "metric": LF_METRIC, "value": round(world * B * args.steps / (ms / 1e3), 1), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (Q4_K weights)",
+        "data": "synthetic",
+        "config": {"workload": "deltanet_ffn_layer_decode_q4k", "batch_per_gpu": B, "global_batch": B * world,
+                   "hidden": HIDDEN, "k_heads": HK, "v_heads": HV, "head_dim": D, "ffn": FFN_N, "weights": "Q4_K",
+                   "parallelism": f"sequence-sharded x{world}, no collectives",
+                   "l2": f"inputs larger than L2: rotating {n_inst} layer instances of {per_inst / 1e6:.1f} MB"},
+        "roofline": {"bound": "hbm", "kernel": "DeltaNet layer (prep, in-projection, recurrence, out-projection) "
+                                                "+ residual add + SwiGLU FFN (prep, gate/up, prep, down) + "
+                                                "residual add, one li_launch_stack_decode call",
+                     "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
+                     "algorithmic_bytes_per_step": layerffn_bytes(B), "traffic": None},
+        "e2e": {"value": round(world * B * e_steps / (e2e_ms / 1e3), 1), "unit": UNIT,
+                "h2d_bytes_per_step": B * HIDDEN * 4, "d2h_bytes_per_step": B * HIDDEN * 4},
+        "gpu_launches": layerffn_launches(B) * args.steps,
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline and world == 1:
+        line["cpu_baseline"] = cpu_baseline_layerffn(B, args.cpu_steps)
+    return line
+
+
+def cpu_baseline_layerffn(batch: int, steps: int) -> dict:
+    """The DeltaNet+FFN layer on the host cores in ggml's CPU arithmetic
+    (q8_K activations and integer dots for every Q4_K projection, the
+    recurrence in double), all threads, `steps` steps at `batch` sequences."""
+    from leaninfer_b200 import synth
+    oracle, flags = cpu_oracle()
+    r = np.random.Generator(np.random.PCG64(11))
+    w = synth.deltanet_layer(r, hidden=HIDDEN, n_k_heads=HK, n_v_heads=HV, head_dim=D, wtype=synth.Q4_K)
+    L, keep = oracle.make_layer(w)
+    inp = synth.deltanet_inputs(r, batch, w)
+    Wg, Wu = synth.random_q4_k(r, FFN_N, HIDDEN), synth.random_q4_k(r, FFN_N, HIDDEN)
+    Wd = synth.random_q4_k(r, HIDDEN, FFN_N)
+    gamma = r.uniform(0.5, 1.5, HIDDEN).astype(np.float32) / 128.0
+    cs, st = inp["conv_state"], inp["state"]
+
+    def step(x):
+        x = x + oracle.deltanet_layer_decode_q8act(L, keep, x, cs, st)
+        return (x + oracle.ffn_q8act(12, x, gamma, Wg, Wu, Wd, FFN_N)).astype(np.float32)
+    x = step(inp["x"])                   # warm-up
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        x = step(x)
+    dt = time.perf_counter() - t0
+    return {"value": round(batch * steps / dt, 2), "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"{steps} steps of the DeltaNet+FFN layer at batch {batch} (oracle/li_oracle.c built {flags}: "
+                      f"projections with ggml-style q8_K activations and integer dots, recurrence in double; "
+                      f"{oracle.num_threads()} host threads)", "seconds": round(dt, 3)}
+
+
 def stack_launches(n_layers: int, batch: int, tp: int) -> int:
     """Kernels of the library per stack step (NCCL's own kernels not counted):
     per layer the mixer's, the FFN's and two residual adds."""
@@ -1098,6 +1289,18 @@ def run_reference(args, rank: int) -> dict | None:
                     "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
                     "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
                             "d2h_bytes_per_step": 0}}
+        if args.workload == "layerffn":
+            cb = cpu_baseline_layerffn(args.batch, max(1, min(args.steps, 4)))
+            return {"impl": "reference", "metric": LF_METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": 0,
+                    "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                    "vs_baseline": None, "dtype": "f64 accumulation (Q4_K weights)", "data": "synthetic",
+                    "config": {"workload": "deltanet_ffn_layer_decode_q4k", "batch_per_gpu": args.batch,
+                               "hidden": HIDDEN, "k_heads": HK, "v_heads": HV, "head_dim": D, "ffn": FFN_N,
+                               "weights": "Q4_K",
+                               "note": "the reference's ggml CPU ops are not vendored; its CPU path is the C "
+                                       "oracle port"},
+                    "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                    "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         if args.workload == "prefill":
             cb, metric, cfg = cpu_baseline_prefill(), "chunked prefill tokens/s", {
                 "workload": "deltanet_chunk_prefill_bf16", "tokens_per_sequence": PF_T, "chunk": 64}
@@ -1139,11 +1342,13 @@ def main():
     ap.add_argument("--layers", type=int, default=64, help="stack: layers (3 DeltaNet : 1 attention)")
     ap.add_argument("--ctx", type=int, default=4096, help="stack: attention context (KV cache length)")
     ap.add_argument("--tp-ffn", action="store_true", help="stack: shard the FFN weights across the GPUs (NCCL)")
-    ap.add_argument("--workload", choices=["decode", "prefill", "qkv", "ffn", "stack", "refgpu"], default="decode",
-                    help="decode: the fused DeltaNet layer decode step (the headline); prefill: one 8192-token "
-                         "chunked prefill + gated norm + bf16 out-projection; qkv: RMSNorm + Q/K/V Q8_0 GEMV "
-                         "(K=2048, one token); ffn: RMSNorm + SwiGLU FFN 4096 -> 12288 -> 4096 (--batch rows, "
-                         "--wtype)")
+    ap.add_argument("--workload", choices=["decode", "layerffn", "prefill", "qkv", "ffn", "stack", "refgpu"],
+                    default="decode",
+                    help="decode: the fused DeltaNet layer decode step (the headline); layerffn: that layer "
+                         "followed by the SwiGLU FFN 4096 -> 12288 -> 4096, residual adds after each; prefill: one "
+                         "8192-token chunked prefill + gated norm + bf16 out-projection; qkv: RMSNorm + Q/K/V Q8_0 "
+                         "GEMV (K=2048, one token); ffn: RMSNorm + SwiGLU FFN 4096 -> 12288 -> 4096 (--batch "
+                         "rows, --wtype)")
     ap.add_argument("--wtype", type=int, choices=[8, 12], default=12, help="ffn weights: 12 = Q4_K, 8 = Q8_0")
     ap.add_argument("--state", choices=["f32", "f16"], default="f32",
                     help="decode: recurrent state storage (f16 = li_launch_deltanet_layer_decode_f16state)")
@@ -1184,6 +1389,8 @@ def main():
             line = run_prefill(args, rank, world, dist)
         elif args.workload == "stack":
             line = run_stack(args, rank, world, dist)
+        elif args.workload == "layerffn":
+            line = run_layerffn(args, rank, world, dist)
         elif args.workload == "refgpu":
             line = run_refgpu(args, "ours") if rank == 0 else None
         elif args.workload in ("qkv", "ffn"):
