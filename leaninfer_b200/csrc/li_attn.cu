@@ -27,8 +27,12 @@
 // HBM-bound: a step reads each cached token's K and V row once per kv head.
 #include "li_common.cuh"
 #include "li_qgemv.cuh"
+#include "li_tc.cuh"
 #include "li_tcgemm.cuh"
 
+#include <cuda.h>   // CUtensorMap and its enums; the encoder is fetched at run time
+
+#include <cstring>
 #include <mutex>
 
 LI_DEFINE_TU_STATUS(attn)
@@ -311,6 +315,331 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(AttnArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// attn_decode on the tensor cores: a persistent CTA per SM walks the (chunk,
+// kv head, sequence) items c, c + grid, ... with one continuous stream of
+// 128-token K and V tiles (TMA, 32 KB each, a ring of four), so the copies of
+// the next item are in flight while this one finishes. Per tile:
+//   S^T[t][n] = K[t][:] . Qcat[n][:]   tcgen05, M = 128 tokens, N = 32, K = D:
+//       Qcat rows 0..15 are the group's q heads rounded to f16 (hi), rows
+//       16..31 the f16 remainders (lo), so hi + lo carries q to ~22 bits;
+//   online softmax per head over the tile (warps 0-3, one token row each);
+//   O^T[d][n] += V[:][d] . Pcat[n][:]  tcgen05, M = 128 dims (V read MN-major),
+//       N = 32, K = 128 tokens, with Pcat = probabilities as f16 hi | lo;
+// O is rescaled in tensor memory when a head's running max grows. Rows of the
+// last tile past the sequence's position are masked (score -inf, V row zeroed
+// in shared memory: a cache slot past the context may hold anything). The
+// item's (max, sum, o[D]) per q head goes to the same records as the SIMT
+// kernel's, merged by attn_combine.
+// Warps: 0-3 softmax and epilogue, 4 TMA producer, 5 MMA issuer (and TMEM).
+// ---------------------------------------------------------------------------
+constexpr int kTcTok = 128;                        // tokens per K / V tile
+constexpr int kTcRing = 4;                         // K and V tiles in flight
+constexpr uint32_t kTcTileBytes = kTcTok * kD * 2; // 32 KB
+constexpr uint32_t kTcOpBytes = 32 * kD * 2;       // Qcat / Pcat operand: 32 rows x 128 (8 KB)
+constexpr uint32_t kTcOffQ = kTcRing * kTcTileBytes, kTcOffP = kTcOffQ + kTcOpBytes, kTcOffBar = kTcOffP + kTcOpBytes;
+constexpr size_t kTcSmem = kTcOffBar + 256 + 1024;  // barriers, then slack for the 1 KB alignment
+constexpr int kTcAttnThreads = 192;
+constexpr uint32_t kIdescAMajorMN = 1u << 15;
+
+__device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *map, int x, int y, int z,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];"
+        ::"r"(smem_addr(smem_dst)), "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Named barrier 1 over the four softmax warps, returning whether any of them
+// passed `v` (a timed-out wait), so that all four leave their loops together.
+__device__ __forceinline__ bool softmax_bar_any(bool v) {
+    uint32_t r;
+    asm volatile("{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\t"
+                 "bar.red.or.pred po, 1, 128, pi;\n\tselp.u32 %0, 1, 0, po;\n\t}"
+                 : "=r"(r) : "r"((uint32_t)v) : "memory");
+    return r != 0;
+}
+
+__device__ __forceinline__ bool attn_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (!mbar_wait(bar, parity)) {
+        *abort_flag = 1;
+        return false;
+    }
+    return true;
+}
+
+// Tokens [t0, t1) of an item and its tile count (0: past the context).
+__device__ __forceinline__ int attn_item(const AttnArgs &a, int it, int &s, int &j, int &chunk, int &t0, int &t1) {
+    chunk = it % a.n_chunk;
+    j = (it / a.n_chunk) % a.Hkv;
+    s = it / (a.n_chunk * a.Hkv);
+    t0 = chunk * a.chunk;
+    t1 = min(t0 + a.chunk, a.pos[s] + 1);
+    return t0 < t1 ? (t1 - t0 + kTcTok - 1) / kTcTok : 0;
+}
+
+// byte offset of element (row, k) in a [32 rows][128] f16 operand (two 64-wide 128B-swizzled blocks)
+__device__ __forceinline__ uint32_t op_off(int row, int k) {
+    return (uint32_t)(k >> 6) * 4096u + sw128_off(row, (k & 63) >> 3) + (uint32_t)(k & 7) * 2u;
+}
+
+template <int G>
+__global__ void __launch_bounds__(kTcAttnThreads, 1)
+attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, AttnArgs a,
+                      int n_items) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    uint8_t *ring = smem, *qbuf = smem + kTcOffQ, *pbuf = smem + kTcOffP;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kTcOffBar);
+    uint64_t *full = bars, *empty = bars + kTcRing;
+    uint64_t *q_full = empty + kTcRing, *s_full = q_full + 1, *s_empty = s_full + 2, *p_full = s_empty + 2;
+    uint64_t *pv_done = p_full + 1, *fin = pv_done + 1;
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(fin + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+    __shared__ float red_m[4][16], red_s[4][16];
+    const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp, tid = threadIdx.x;
+
+    if (tid == 0) {
+        for (int i = 0; i < kTcRing; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
+        mbar_init(q_full, 4);
+        for (int i = 0; i < 2; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_empty[i], 4); }
+        mbar_init(p_full, 4);
+        mbar_init(pv_done, 1);
+        mbar_init(fin, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 5) tmem_alloc(tmem_holder, 128);
+    if (warp < 4) {
+        // the operands' padding rows (heads G..15 of each half) stay zero
+        for (int i = tid; i < 2 * (int)kTcOpBytes / 16; i += 128)
+            reinterpret_cast<uint4 *>(qbuf)[i] = make_uint4(0u, 0u, 0u, 0u);   // qbuf and pbuf are adjacent
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+    grid_dep_wait();                 // q and the caches come from the previous kernels
+    grid_dep_launch_dependents();
+
+    if (warp == 4) {
+        // ------------- producer: K_i, V_i of every item, in order -------------
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&tmK) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&tmV) : "memory");
+            int n = 0;
+            for (int it = blockIdx.x; it < n_items && !*abort_flag; it += gridDim.x) {
+                int s, j, chunk, t0, t1;
+                const int nt = attn_item(a, it, s, j, chunk, t0, t1);
+                for (int i = 0; i < nt; ++i) {
+                    const int z = s * a.max_ctx + t0 + i * kTcTok;
+                    for (int kv = 0; kv < 2; ++kv, ++n) {
+                        const int slot = n % kTcRing;
+                        if (n >= kTcRing && !attn_wait(&empty[slot], (uint32_t)((n / kTcRing - 1) & 1), abort_flag))
+                            break;
+                        mbar_arrive_expect_tx(&full[slot], kTcTileBytes);
+                        uint8_t *dst = ring + (size_t)slot * kTcTileBytes;
+                        const CUtensorMap *m = kv ? &tmV : &tmK;
+                        tma_load_3d(dst, m, 0, j, z, &full[slot]);
+                        tma_load_3d(dst + kTcTileBytes / 2, m, 64, j, z, &full[slot]);
+                    }
+                }
+            }
+            // every copy issued has landed before the CTA exits
+            for (int k = n - kTcRing < 0 ? 0 : n - kTcRing; k < n; ++k)
+                mbar_wait(&full[k % kTcRing], (uint32_t)((k / kTcRing) & 1));
+        }
+    } else if (warp == 5) {
+        // ------------- MMA issuer -------------
+        if (lane == 0) {
+            const uint32_t id_s = idesc_kf16(128, 32, false);
+            const uint32_t id_pv = idesc_kf16(128, 32, false) | kIdescAMajorMN;
+            int gt = 0, items = 0;
+            bool ok = true;
+            for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
+                int s, j, chunk, t0, t1;
+                const int nt = attn_item(a, it, s, j, chunk, t0, t1);
+                if (nt == 0) continue;
+                if (!(ok = attn_wait(q_full, (uint32_t)(items & 1), abort_flag))) break;
+                ++items;
+                // S for tile gt (ring slot of its K tile: 2*gt)
+                auto issue_s = [&](int g) -> bool {
+                    const int n = 2 * g, slot = n % kTcRing, b = g & 1;
+                    if (!attn_wait(&full[slot], (uint32_t)((n / kTcRing) & 1), abort_flag)) return false;
+                    if (g >= 2 && !attn_wait(&s_empty[b], (uint32_t)(((g >> 1) - 1) & 1), abort_flag)) return false;
+                    tc_fence_after();
+                    const uint32_t kb = smem_addr(ring + (size_t)slot * kTcTileBytes);
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint64_t ad = sw128_desc(kb + (uint32_t)(kk >> 2) * 16384u) + 2 * (kk & 3);
+                        const uint64_t bd = sw128_desc(smem_addr(qbuf) + (uint32_t)(kk >> 2) * 4096u) + 2 * (kk & 3);
+                        umma_f16(tmem + 32u * b, ad, bd, id_s, kk ? 1u : 0u);
+                    }
+                    umma_commit(&s_full[b]);
+                    umma_commit(&empty[slot]);
+                    return true;
+                };
+                if (!(ok = issue_s(gt))) break;
+                for (int i = 0; i < nt; ++i) {
+                    if (i + 1 < nt && !(ok = issue_s(gt + 1))) break;
+                    // O^T += V^T Pcat for tile gt (ring slot of its V tile: 2*gt+1)
+                    const int n = 2 * gt + 1, slot = n % kTcRing;
+                    if (!(ok = attn_wait(&full[slot], (uint32_t)((n / kTcRing) & 1), abort_flag))) break;
+                    if (!(ok = attn_wait(p_full, (uint32_t)(gt & 1), abort_flag))) break;
+                    tc_fence_after();
+                    const uint32_t vb = smem_addr(ring + (size_t)slot * kTcTileBytes);
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint64_t ad = sw128_mn_desc(vb + (uint32_t)kk * 2048u, 16384u);
+                        const uint64_t bd = sw128_desc(smem_addr(pbuf) + (uint32_t)(kk >> 2) * 4096u) + 2 * (kk & 3);
+                        umma_f16(tmem + 64u, ad, bd, id_pv, (i | kk) ? 1u : 0u);
+                    }
+                    umma_commit(pv_done);
+                    umma_commit(&empty[slot]);
+                    ++gt;
+                }
+            }
+            // every MMA issued has completed before the tensor memory is freed
+            umma_commit(fin);
+            mbar_wait(fin, 0u);
+        }
+    } else {
+        // ------------- softmax (thread = token row of S^T, dim row of O^T) -------------
+        // A timed-out wait never leaves a loop by itself: the warp carries on
+        // (its later waits return at once) to the next named barrier, which
+        // tells all four warps to stop.
+        const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
+        int gt = 0;
+        bool stop = false;
+        for (int it = blockIdx.x; !stop && it < n_items; it += gridDim.x) {
+            int s, j, chunk, t0, t1;
+            const int nt = attn_item(a, it, s, j, chunk, t0, t1);
+            if (nt == 0) continue;
+            // Qcat for this item (the previous item's S products have completed: their results were read)
+            {
+                const float *qs = a.proj + (size_t)s * a.NP + (size_t)j * G * kD + tid;
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                    const float q = qs[(size_t)h * kD] * a.scale;
+                    const __half hi = __float2half_rn(q);
+                    *reinterpret_cast<__half *>(qbuf + op_off(h, tid)) = hi;
+                    *reinterpret_cast<__half *>(qbuf + op_off(16 + h, tid)) = __float2half_rn(q - __half2float(hi));
+                }
+            }
+            fence_proxy_async_shared();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(q_full);
+            float m[G], l[G];
+#pragma unroll
+            for (int h = 0; h < G; ++h) { m[h] = -INFINITY; l[h] = 0.f; }
+            for (int i = 0; i < nt; ++i, ++gt) {
+                const int b = gt & 1;
+                const bool w_ok = __all_sync(0xffffffffu, attn_wait(&s_full[b], (uint32_t)((gt >> 1) & 1), abort_flag));
+                uint32_t sv[32];
+                if (w_ok) {
+                    tc_fence_after();
+                    tmem_ld32_nowait(lane_base + 32u * b, sv);
+                    tmem_wait_ld();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&s_empty[b]);
+                }
+                const bool valid = w_ok && t0 + i * kTcTok + tid < t1;
+                float sc[G], p[G];
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                    sc[h] = valid ? __uint_as_float(sv[h]) + __uint_as_float(sv[16 + h]) : -INFINITY;
+                    float mx = sc[h];
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                    if (lane == 0) red_m[warp][h] = mx;
+                }
+                if ((stop = softmax_bar_any(!w_ok))) break;
+                float alpha[G];
+                bool grow = false;
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                    const float tm = fmaxf(fmaxf(red_m[0][h], red_m[1][h]), fmaxf(red_m[2][h], red_m[3][h]));
+                    const float mn = fmaxf(m[h], tm);          // finite: the tile holds a valid token
+                    alpha[h] = m[h] == -INFINITY ? 0.f : __expf(m[h] - mn);
+                    grow |= m[h] != mn;
+                    m[h] = mn;
+                    p[h] = valid ? __expf(sc[h] - mn) : 0.f;
+                    float ps = p[h];
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+                    if (lane == 0) red_s[warp][h] = ps;
+                }
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+#pragma unroll
+                for (int h = 0; h < G; ++h)
+                    l[h] = l[h] * alpha[h] + ((red_s[0][h] + red_s[1][h]) + (red_s[2][h] + red_s[3][h]));
+                // the previous tile's O product has finished: Pcat may be rewritten, O rescaled
+                bool ok2 = i == 0 || __all_sync(0xffffffffu, attn_wait(pv_done, (uint32_t)((gt - 1) & 1), abort_flag));
+                // this tile's V has landed: rows past the context are zeroed (their products with p = 0 must be 0)
+                const int n = 2 * gt + 1, slot = n % kTcRing;
+                ok2 = ok2 && __all_sync(0xffffffffu, attn_wait(&full[slot], (uint32_t)((n / kTcRing) & 1), abort_flag));
+                if (!ok2) continue;                   // the next tile's barrier stops every warp
+                tc_fence_after();
+                if (i > 0 && grow) {
+                    uint32_t ov[32];
+                    tmem_ld32_nowait(lane_base + 64u, ov);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int h = 0; h < G; ++h) {
+                        ov[h] = __float_as_uint(__uint_as_float(ov[h]) * alpha[h]);
+                        ov[16 + h] = __float_as_uint(__uint_as_float(ov[16 + h]) * alpha[h]);
+                    }
+                    tmem_st32(lane_base + 64u, ov);
+                    tmem_wait_st();
+                }
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                    const __half hi = __float2half_rn(p[h]);
+                    *reinterpret_cast<__half *>(pbuf + op_off(h, tid)) = hi;
+                    *reinterpret_cast<__half *>(pbuf + op_off(16 + h, tid)) = __float2half_rn(p[h] - __half2float(hi));
+                }
+                if (t0 + i * kTcTok + tid >= t1) {
+                    uint8_t *vrow = ring + (size_t)slot * kTcTileBytes + (size_t)tid * 128;
+#pragma unroll
+                    for (int q16 = 0; q16 < 8; ++q16) {
+                        reinterpret_cast<uint4 *>(vrow)[q16] = make_uint4(0u, 0u, 0u, 0u);
+                        reinterpret_cast<uint4 *>(vrow + kTcTileBytes / 2)[q16] = make_uint4(0u, 0u, 0u, 0u);
+                    }
+                }
+                fence_proxy_async_shared();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(p_full);
+            }
+            if (stop) break;
+            // the item's last O product, then its records
+            if (!__all_sync(0xffffffffu, attn_wait(pv_done, (uint32_t)((gt - 1) & 1), abort_flag))) continue;
+            tc_fence_after();
+            uint32_t ov[32];
+            tmem_ld32_nowait(lane_base + 64u, ov);
+            tmem_wait_ld();
+            tc_fence_before();
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+                float *rec = a.part + (((size_t)s * a.Hq + (size_t)j * G + h) * a.n_chunk + chunk) * kPartStride;
+                rec[4 + tid] = __uint_as_float(ov[h]) + __uint_as_float(ov[16 + h]);
+                if (tid == 0) { rec[0] = m[h]; rec[1] = l[h]; }
+            }
+        }
+    }
+
+    if (*abort_flag && tid == 0) atomicExch(&g_device_error, LI_ERR_TIMEOUT);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, 128);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // attn_combine: CTA per (sequence, head), thread per dim.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kD) attn_combine_kernel(AttnArgs a) {
@@ -354,6 +683,78 @@ int launch_decode_any(int G, const AttnArgs &a, int B, cudaStream_t s) {
     case 5: return launch_decode<5>(a, B, s);
     case 6: return launch_decode<6>(a, B, s);
     case 8: return launch_decode<8>(a, B, s);
+    default: return LI_ERR_UNSUPPORTED;
+    }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encoder() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// A cache [B][max_ctx][Hkv][128] f16 as a 3-D tensor (d, kv head, B*max_ctx
+// token rows) with a [128 tokens][1][64 d] box, 128-byte swizzle (rows past
+// the last sequence's slots come in as zeros).
+int encode_cache(CUtensorMap *m, void *base, int Hkv, long long rows) {
+    EncodeTiledFn fn = encoder();
+    if (!fn) return LI_ERR_UNSUPPORTED;
+    const cuuint64_t dims[3] = {(cuuint64_t)kD, (cuuint64_t)Hkv, (cuuint64_t)rows};
+    const cuuint64_t strides[2] = {(cuuint64_t)kD * 2, (cuuint64_t)Hkv * kD * 2};
+    const cuuint32_t box[3] = {64, 1, (cuuint32_t)kTcTok};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, base, dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : LI_ERR_BAD_SHAPE;
+}
+
+// The tensor-core decode kernel where it applies: whole 128-token tiles per
+// chunk, and the group's q heads in one half of the 32 MMA columns.
+bool attn_tc(int G, int chunk) { return chunk % kTcTok == 0 && G >= 1 && G <= 16; }
+
+template <int G>
+int launch_decode_tc(const AttnArgs &a, int B, cudaStream_t s) {
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [] {
+        attr_err = cudaFuncSetAttribute(attn_decode_tc_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)kTcSmem);
+    });
+    if (attr_err != cudaSuccess) return (int)attr_err;
+    CUtensorMap mk, mv;
+    memset(&mk, 0, sizeof(mk));
+    memset(&mv, 0, sizeof(mv));
+    const long long rows = (long long)B * a.max_ctx;
+    if (rows + kTcTok >= (1ll << 31)) return LI_ERR_BAD_SHAPE;
+    int rc;
+    if ((rc = encode_cache(&mk, a.k_cache, a.Hkv, rows)) || (rc = encode_cache(&mv, a.v_cache, a.Hkv, rows))) return rc;
+    const int items = a.n_chunk * a.Hkv * B;
+    const int grid = items < num_sms() ? items : num_sms();
+    return (int)launch_pdl(attn_decode_tc_kernel<G>, dim3((unsigned)grid), dim3(kTcAttnThreads), kTcSmem, s, true,
+                           mk, mv, a, items);
+}
+
+int launch_decode_tc_any(int G, const AttnArgs &a, int B, cudaStream_t s) {
+    switch (G) {
+    case 1: return launch_decode_tc<1>(a, B, s);
+    case 2: return launch_decode_tc<2>(a, B, s);
+    case 3: return launch_decode_tc<3>(a, B, s);
+    case 4: return launch_decode_tc<4>(a, B, s);
+    case 5: return launch_decode_tc<5>(a, B, s);
+    case 6: return launch_decode_tc<6>(a, B, s);
+    case 8: return launch_decode_tc<8>(a, B, s);
     default: return LI_ERR_UNSUPPORTED;
     }
 }
@@ -499,8 +900,9 @@ int li_launch_attn_layer_decode(const li_attn_layer *L, const float *x, float *y
     if ((rc = (int)launch_pdl(attn_prep_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, s, true, a,
                               n_seqs)))
         return rc;
-    // 3. split-K attention, 4. merge + output gate
-    if ((rc = launch_decode_any(G, a, n_seqs, s))) return rc;
+    // 3. split-K attention (tensor cores for whole 128-token tiles), 4. merge + output gate
+    if ((rc = attn_tc(G, a.chunk) ? launch_decode_tc_any(G, a, n_seqs, s) : launch_decode_any(G, a, n_seqs, s)))
+        return rc;
     if ((rc = (int)launch_pdl(attn_combine_kernel, dim3((unsigned)(n_seqs * Hq)), dim3(kD), 0, s, true, a)))
         return rc;
     // 5. output projection

@@ -8,7 +8,9 @@ several steps with the position advancing.
 Tolerances (normwise, max|got - ref| / max|ref|): 1e-3 for y when the
 projections are SIMT GEMVs (up to 3 sequences), 3e-3 when they run on the
 tensor cores (f16 operands in both projections, the scores' softmax between
-them); the cache rows written by the step within 1e-3 (one f16 rounding).
+them); the cache rows written by the step within 1e-3 (one f16 rounding) with
+the SIMT projections and 2e-3 with the tensor-core in-projection (its f16
+operands, then the rounding; measured up to 1.12e-3 at 24 sequences).
 """
 from __future__ import annotations
 
@@ -57,9 +59,10 @@ def _check_step(cuda, oracle_mod, layer, L, keep, x, kc, vc, kc_d, vc_d, pos, to
     # the device caches changed
     kg = kc_d.cpu().numpy().view(np.uint16)
     vg = vc_d.cpu().numpy().view(np.uint16)
+    tol_row = 1e-3 if n <= 2 else 2e-3
     for s in range(n):
-        assert_close(_f16(kg[s, pos[s]]), _f16(kc[s, pos[s]]), 1e-3, f"{what}: k row s={s}")
-        assert_close(_f16(vg[s, pos[s]]), _f16(vc[s, pos[s]]), 1e-3, f"{what}: v row s={s}")
+        assert_close(_f16(kg[s, pos[s]]), _f16(kc[s, pos[s]]), tol_row, f"{what}: k row s={s}")
+        assert_close(_f16(vg[s, pos[s]]), _f16(vc[s, pos[s]]), tol_row, f"{what}: v row s={s}")
     mask = np.ones(kc.shape[:2], bool)
     mask[np.arange(n), pos] = False
     assert np.array_equal(kg[mask], kg0[mask]) and np.array_equal(vg[mask], vg0[mask])
@@ -85,11 +88,14 @@ def test_attn_layer_decode_ctx4096(cuda, oracle_mod, B, wtype):
     assert ops.device_status() == 0
 
 
-@pytest.mark.parametrize("B,G", [(3, 5), (6, 4), (4, 1)])
-def test_attn_layer_ragged_positions_and_steps(cuda, oracle_mod, B, G):
+@pytest.mark.parametrize("B,G,max_ctx", [(3, 5, 700), (6, 4, 700), (4, 1, 700), (24, 5, 6000), (40, 8, 4000)])
+def test_attn_layer_ragged_positions_and_steps(cuda, oracle_mod, B, G, max_ctx):
     """Ragged contexts (a sequence at its first token, others mid-cache) and
     three steps with every position advancing by one, at hidden 1024 with
-    Hq/Hkv = G; rope over 32 dims."""
+    Hq/Hkv = G; rope over 32 dims. The first three cases split the context
+    into 64-token chunks (the CUDA-core attention kernel); the last two into
+    256-token chunks (the tensor-core kernel: 128-token tiles, the last tile
+    of each sequence partly past its position, chunks past it skipped)."""
     import torch
     from leaninfer_b200 import synth
     r = rng(6100 + 10 * B + G)
@@ -97,7 +103,6 @@ def test_attn_layer_ragged_positions_and_steps(cuda, oracle_mod, B, G):
     w = synth.attn_layer(r, hidden=1024, n_q_heads=Hkv * G, n_kv_heads=Hkv, rope_dim=32, wtype=12)
     layer = _layer(cuda, w)
     L, keep = oracle_mod.make_attn_layer(w)
-    max_ctx = 700
     pos = np.array([0] + list(r.integers(1, max_ctx - 3, size=B - 1)), np.int32)
     inp = synth.attn_inputs(r, B, w, max_ctx, pos)
     kc, vc = inp["k_cache"], inp["v_cache"]
