@@ -606,8 +606,9 @@ static int layer_decode(const li_deltanet_layer *L, const float *x, float *y, fl
         const cudaError_t e = cudaMemsetAsync(proj, 0, (size_t)NI * n * sizeof(float), s);
         if (e != cudaSuccess) return (int)e;
     }
+    // a dependent launch: the prep waits for the previous kernel before it reads x
     if ((rc = tc_prep_launch(x, L->hidden, L->in_norm_w, L->in_norm_eps, n_seqs, L->hidden, x16, xscale, s,
-                             false, in.x_npad)))
+                             true, in.x_npad)))
         return rc;
     if ((rc = tc_gemm_launch(in, s, true))) return rc;
     TcArgs out = {};
