@@ -369,7 +369,10 @@ int li_launch_deltanet_layer_decode_noalloc(const li_deltanet_layer * L,
  * v_cache are __half [n_seqs][max_ctx][Hkv][D] (token-major, as ggml's KV
  * cache rows); pos [n_seqs] int32 in device memory, 0 <= pos[s] < max_ctx:
  * the step writes the new token's k and v at pos[s] and attends over tokens
- * 0..pos[s]; the caller advances pos between steps. No counterpart among the
+ * 0..pos[s]; the caller advances pos between steps. A position outside
+ * [0, max_ctx) (the host cannot see device memory to check it) writes and
+ * reads no cache row: that sequence's output is the out-projection of zeros
+ * and li_device_status() reports LI_ERR_BAD_ARG. No counterpart among the
  * reference's kernels. */
 size_t li_attn_layer_workspace_size(const li_attn_layer * L, int n_seqs, int max_ctx);
 int li_launch_attn_layer_decode(const li_attn_layer * L,

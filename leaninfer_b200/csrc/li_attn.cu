@@ -74,6 +74,11 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(AttnArgs a, int B) {
     if (gw >= B * slots) return;
     const int s = gw / slots, hs = gw % slots;
     const int pos = a.pos[s];
+    if (pos < 0 || pos >= a.max_ctx) {
+        // no cache slot for this token: nothing is written, the device flag is raised
+        if (hs == 0 && lane == 0) atomicExch(&g_device_error, LI_ERR_BAD_ARG);
+        return;
+    }
     float *ps = a.proj + (size_t)s * a.NP;
     const bool is_q = hs < a.Hq;
     const int j = hs - a.Hq;
@@ -172,8 +177,8 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(AttnArgs a) {
     const int hw = lane >> 4, c = lane & 15;
     const int pos = a.pos[s];
     const int t0 = chunk * a.chunk;
-    const int t1 = min(t0 + a.chunk, pos + 1);
-    if (t0 >= t1) return;                            // beyond this sequence's context
+    const int t1 = min(min(t0 + a.chunk, pos + 1), a.max_ctx);   // a position past the cache reads none of it
+    if (t0 >= t1 || pos < 0) return;                 // beyond this sequence's context
     // this warp's tokens: a contiguous quarter of the chunk's range
     const int per = (t1 - t0 + 3) / 4;
     const int wb = t0 + warp * per, we = min(wb + per, t1);
@@ -376,8 +381,9 @@ __device__ __forceinline__ int attn_item(const AttnArgs &a, int it, int &s, int 
     j = (it / a.n_chunk) % a.Hkv;
     s = it / (a.n_chunk * a.Hkv);
     t0 = chunk * a.chunk;
-    t1 = min(t0 + a.chunk, a.pos[s] + 1);
-    return t0 < t1 ? (t1 - t0 + kTcTok - 1) / kTcTok : 0;
+    const int pos = a.pos[s];
+    t1 = min(min(t0 + a.chunk, pos + 1), a.max_ctx);   // a position past the cache reads none of it
+    return t0 < t1 && pos >= 0 ? (t1 - t0 + kTcTok - 1) / kTcTok : 0;
 }
 
 // byte offset of element (row, k) in a [32 rows][128] f16 operand (two 64-wide 128B-swizzled blocks)
@@ -646,7 +652,12 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(AttnArgs a) {
     grid_dep_wait();
     grid_dep_launch_dependents();
     const int s = blockIdx.x / a.Hq, h = blockIdx.x % a.Hq, d = threadIdx.x;
-    const int nch = (a.pos[s] + a.chunk) / a.chunk;   // chunks holding tokens 0..pos
+    const int pos = a.pos[s];
+    if (pos < 0 || pos >= a.max_ctx) {                 // no context (the prep raised the device flag)
+        a.og[(size_t)s * a.Hq * kD + (size_t)h * kD + d] = 0.f;
+        return;
+    }
+    const int nch = (pos + a.chunk) / a.chunk;         // chunks holding tokens 0..pos
     const float *rec = a.part + ((size_t)s * a.Hq + h) * a.n_chunk * kPartStride;
     float M = -INFINITY;
     for (int c = 0; c < nch; ++c) M = fmaxf(M, rec[(size_t)c * kPartStride]);

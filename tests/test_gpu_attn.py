@@ -113,3 +113,37 @@ def test_attn_layer_ragged_positions_and_steps(cuda, oracle_mod, B, G, max_ctx):
         x = r.standard_normal((B, 1024)).astype(np.float32)
         p = pos + step
         _check_step(cuda, oracle_mod, layer, L, keep, x, kc, vc, kc_d, vc_d, p, tol, f"attn ragged step {step}")
+
+
+@pytest.mark.parametrize("B,max_ctx", [(3, 300), (24, 6000)])
+def test_attn_position_outside_the_cache_raises_the_device_flag(cuda, oracle_mod, B, max_ctx):
+    """A position at max_ctx (one past the last slot) and one at -1: the
+    kernels' bounds checks write and read no cache row for those sequences,
+    li_device_status() reports LI_ERR_BAD_ARG, the other sequences' outputs
+    are the oracle's and their cache rows are written. 3 sequences (64-token
+    chunks, the CUDA-core attention kernel) and 24 (256-token chunks, the
+    tensor-core kernel)."""
+    import torch
+    from leaninfer_b200 import ops, synth
+    r = rng(6300 + B)
+    w = synth.attn_layer(r, hidden=1024, n_q_heads=8, n_kv_heads=2, rope_dim=32, wtype=12)
+    layer = _layer(cuda, w)
+    L, keep = oracle_mod.make_attn_layer(w)
+    pos = np.array([max_ctx // 2, max_ctx] + [max_ctx // 3] * (B - 3) + [-1], np.int32)
+    inp = synth.attn_inputs(r, B, w, max_ctx, np.clip(pos, 0, max_ctx - 1))
+    kc, vc = inp["k_cache"], inp["v_cache"]
+    kc_d, vc_d = T(kc, cuda).view(torch.float16), T(vc, cuda).view(torch.float16)
+    x = r.standard_normal((B, 1024)).astype(np.float32)
+    y = torch.empty(B, 1024, device=cuda)
+    layer.step(T(x, cuda), y, kc_d, vc_d, T(pos, cuda))
+    assert ops.device_status() == 2001                       # LI_ERR_BAD_ARG
+    got = y.cpu().numpy()
+    assert np.all(np.isfinite(got))
+    bad = [1, B - 1]
+    kg, vg = kc_d.cpu().numpy().view(np.uint16), vc_d.cpu().numpy().view(np.uint16)
+    for s in bad:                                            # nothing written for the bad positions
+        assert np.array_equal(kg[s], kc[s]) and np.array_equal(vg[s], vc[s])
+    good = [s for s in range(B) if s not in bad]
+    y_ref = oracle_mod.attn_layer_decode(L, keep, x[good], kc[good].copy(), vc[good].copy(), pos[good])
+    assert_close(got[good], y_ref, 1e-3 if B <= 2 else 3e-3, "valid sequences")
+    assert ops.device_status() == 0
