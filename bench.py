@@ -19,7 +19,7 @@ than 3x the L2 capacity of traffic.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl reference]
 
 Other workloads (`--workload`): `layerffn` (the same layer followed by the
-SwiGLU FFN 4096 -> 12288 -> 4096, a residual add after each), `prefill` (one
+SwiGLU FFN 4096 -> 12288 -> 4096, each adding into the residual stream), `prefill` (one
 8192-token chunked prefill + gated norm + bf16 out-projection), `qkv`
 (RMSNorm + Q/K/V Q8_0 GEMV, K = 2048, one token), `ffn` (RMSNorm + SwiGLU FFN
 4096 -> 12288 -> 4096, `--batch` rows, `--wtype` 12 = Q4_K or 8 = Q8_0),
@@ -979,9 +979,9 @@ def layerffn_bytes(batch: int) -> int:
 
 
 def layerffn_launches(batch: int) -> int:
-    """Kernels of the library per step: the DeltaNet layer's, the FFN's and
-    the two residual adds."""
-    return kernels_per_step(batch) + gemv_launches("ffn", batch) + 2
+    """Kernels of the library per step: the DeltaNet layer's and the FFN's
+    (the residual adds ride on their output projections)."""
+    return kernels_per_step(batch) + gemv_launches("ffn", batch)
 
 
 def build_layerffn(dev, batch: int, n_inst: int, seed: int) -> list:
@@ -1102,9 +1102,10 @@ def run_layerffn(args, rank: int, world: int, dist) -> dict | None:
                    "hidden": HIDDEN, "k_heads": HK, "v_heads": HV, "head_dim": D, "ffn": FFN_N, "weights": "Q4_K",
                    "parallelism": f"sequence-sharded x{world}, no collectives",
                    "l2": f"inputs larger than L2: rotating {n_inst} layer instances of {per_inst / 1e6:.1f} MB"},
-        "roofline": {"bound": "hbm", "kernel": "DeltaNet layer (prep, in-projection, recurrence, out-projection) "
-                                                "+ residual add + SwiGLU FFN (prep, gate/up, prep, down) + "
-                                                "residual add, one li_launch_stack_decode call",
+        "roofline": {"bound": "hbm", "kernel": "DeltaNet layer (prep, in-projection, recurrence, out-projection "
+                                                "adding into the residual stream) + SwiGLU FFN (prep, gate/up, prep, "
+                                                "down adding into the residual stream), one li_launch_stack_decode "
+                                                "call",
                      "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
                      "algorithmic_bytes_per_step": layerffn_bytes(B), "traffic": None},
@@ -1149,14 +1150,16 @@ def cpu_baseline_layerffn(batch: int, steps: int) -> dict:
 
 def stack_launches(n_layers: int, batch: int, tp: int) -> int:
     """Kernels of the library per stack step (NCCL's own kernels not counted):
-    per layer the mixer's, the FFN's and two residual adds."""
+    per layer the mixer's and the FFN's; the residual adds ride on their
+    output projections, except after a sharded FFN (one add kernel)."""
     def proj(rows):   # one projection: SIMT GEMV, or prep + GEMM (+ reduce for the X-stationary kernel)
         return 1 if rows < TC_MIN_ROWS else (3 if rows <= TCX_MAX_ROWS else 2)
     n_attn = n_layers // 4
     dn = kernels_per_step(batch)
     at = proj(batch) + 3 + proj(batch)
     ffn = gemv_launches("ffn", batch * tp)
-    return (n_layers - n_attn) * (dn + ffn + 2) + n_attn * (at + ffn + 2)
+    add = 1 if tp > 1 else 0
+    return (n_layers - n_attn) * (dn + ffn + add) + n_attn * (at + ffn + add)
 
 
 # --------------------------------------------------------------------------

@@ -818,9 +818,11 @@ AttnWs attn_ws_layout(const li_attn_layer *L, int n, int max_ctx) {
     return w;
 }
 
-// One projection y[b] = W . (rmsnorm?(x[b])): SIMT GEMV or prep + tcgen05 GEMM.
+// One projection y[b] = W . (rmsnorm?(x[b])): SIMT GEMV or prep + tcgen05 GEMM;
+// accumulate: y[b] += W . x[b] (a residual update of dst).
 int project(bool simt, int wtype, const void *W, int K, int N, const float *x, const float *gamma, float eps,
-            float *dst, int B, char *ws, const AttnWs &lay, bool first, bool out, cudaStream_t s) {
+            float *dst, int B, char *ws, const AttnWs &lay, bool first, bool out, cudaStream_t s,
+            bool accumulate = false) {
     int rc;
     if (simt) {
         QGemvArgs g = {};
@@ -828,6 +830,7 @@ int project(bool simt, int wtype, const void *W, int K, int N, const float *x, c
         if ((rc = qgemv_plan(wtype, K, N, kEpiStore, &g.plan))) return rc;
         g.x = x; g.x_stride = K; g.gamma = gamma; g.K = K; g.eps = eps;
         g.n_seg = 1; g.W[0] = W; g.seg_rows[0] = N; g.dst[0] = dst; g.dst_stride[0] = N;
+        g.accumulate = accumulate;
         return qgemv_launch(g, B, s, !first);
     }
     TcArgs t = {};
@@ -836,12 +839,13 @@ int project(bool simt, int wtype, const void *W, int K, int N, const float *x, c
     t.X16 = reinterpret_cast<const __half *>(ws + (out ? lay.og16 : lay.x16));
     t.xscale = reinterpret_cast<const float *>(ws + (out ? lay.oscale : lay.xscale));
     t.partials = lay.partials ? reinterpret_cast<float *>(ws + lay.partials) : nullptr;
+    t.accumulate = accumulate;
     t.x_npad = tc_gemm_x_npad(t);
     // a dependent launch also as the layer's first kernel: the prep waits for the previous kernel before it reads x
     if ((rc = tc_prep_launch(x, K, gamma, eps, B, K, const_cast<__half *>(t.X16), const_cast<float *>(t.xscale), s,
                              true, t.x_npad)))
         return rc;
-    if (tc_gemm_splits_k(t)) {
+    if (tc_gemm_splits_k(t) && !accumulate) {
         // the K-split CTAs add into dst; ordered after the prep by the stream
         cudaError_t e = cudaMemsetAsync(dst, 0, (size_t)B * N * sizeof(float), s);
         if (e != cudaSuccess) return (int)e;
@@ -862,9 +866,12 @@ size_t li_attn_layer_workspace_size(const li_attn_layer *L, int n_seqs, int max_
     return attn_ws_layout(L, n_seqs, max_ctx).total;
 }
 
-int li_launch_attn_layer_decode(const li_attn_layer *L, const float *x, float *y, void *k_cache, void *v_cache,
-                                const int32_t *pos, int n_seqs, int max_ctx, void *workspace,
-                                size_t workspace_bytes, void *stream) {
+}  // extern "C"
+
+// accumulate: y += the layer's output (the output projection adds into y).
+static int attn_layer_decode(const li_attn_layer *L, const float *x, float *y, void *k_cache, void *v_cache,
+                             const int32_t *pos, int n_seqs, int max_ctx, void *workspace, size_t workspace_bytes,
+                             void *stream, bool accumulate) {
     if (!L || !x || !y || !k_cache || !v_cache || !pos || n_seqs < 0 || max_ctx <= 0) return LI_ERR_BAD_ARG;
     if (n_seqs == 0) return 0;
     if (!L->w_in || !L->w_out) return LI_ERR_BAD_ARG;
@@ -919,7 +926,19 @@ int li_launch_attn_layer_decode(const li_attn_layer *L, const float *x, float *y
         return rc;
     // 5. output projection
     return project(simt, L->w_out_type, L->w_out, Hq * D, L->hidden, a.og, nullptr, 0.f, y, n_seqs, ws, lay, false,
-                   true, s);
+                   true, s, accumulate);
 }
 
-}  // extern "C"
+extern "C" int li_launch_attn_layer_decode(const li_attn_layer *L, const float *x, float *y, void *k_cache,
+                                           void *v_cache, const int32_t *pos, int n_seqs, int max_ctx,
+                                           void *workspace, size_t workspace_bytes, void *stream) {
+    return attn_layer_decode(L, x, y, k_cache, v_cache, pos, n_seqs, max_ctx, workspace, workspace_bytes, stream,
+                             false);
+}
+
+int li::attn_layer_decode_residual(const li_attn_layer *L, const float *x, float *y, void *k_cache, void *v_cache,
+                                   const int32_t *pos, int n_seqs, int max_ctx, void *workspace,
+                                   size_t workspace_bytes, void *stream) {
+    return attn_layer_decode(L, x, y, k_cache, v_cache, pos, n_seqs, max_ctx, workspace, workspace_bytes, stream,
+                             true);
+}

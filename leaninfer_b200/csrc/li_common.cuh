@@ -28,6 +28,20 @@ void set_last_error(int code);                 // legacy void entries
 int  num_sms();                                // SMs of the current device
 int  launch_status();                          // cudaGetLastError as int
 
+// Residual forms of the layer entries, for the layer stack: y += layer(x),
+// where y may be x itself (every read of x precedes the first write of y in
+// stream order). The output projection adds its result to y instead of
+// storing it (a K-split projection adds its partial sums onto y instead of
+// a zeroed output), so the stack needs no separate residual-add kernel.
+int deltanet_layer_decode_residual(const li_deltanet_layer *L, const float *x, float *y, float *conv_state,
+                                   float *state, int n_seqs, void *workspace, size_t workspace_bytes, void *stream);
+int attn_layer_decode_residual(const li_attn_layer *L, const float *x, float *y, void *k_cache, void *v_cache,
+                               const int32_t *pos, int n_seqs, int max_ctx, void *workspace, size_t workspace_bytes,
+                               void *stream);
+int fused_ffn_q_residual(int wtype, const float *x, const float *gamma, const void *Wg, const void *Wu,
+                         const void *Wd, float *y, int K, int N, int n_rows, float eps, void *workspace,
+                         size_t workspace_bytes, void *stream);
+
 // Device-side failure flag (a bounded wait that gave up). Each translation
 // unit has its own copy (internal linkage, no relocatable device code); each
 // defines a host reader with LI_DEFINE_TU_STATUS, and li_device_status()

@@ -524,8 +524,10 @@ size_t li_deltanet_layer_workspace_size(const li_deltanet_layer *L, int n_seqs) 
 }  // extern "C"
 
 // The layer step; the state is fp32 (`state`) or fp16 (`state16`).
+// accumulate: y += the layer's output (the out-projection adds into y).
 static int layer_decode(const li_deltanet_layer *L, const float *x, float *y, float *conv_state, float *state,
-                        __half *state16, int n_seqs, void *workspace, size_t workspace_bytes, void *stream) {
+                        __half *state16, int n_seqs, void *workspace, size_t workspace_bytes, void *stream,
+                        bool accumulate = false) {
     if (!L || !x || !y || !conv_state || (!state && !state16) || n_seqs < 0) return LI_ERR_BAD_ARG;
     if (!state) state = reinterpret_cast<float *>(state16);   // alignment check below covers both
     if (n_seqs == 0) return 0;
@@ -579,6 +581,7 @@ static int layer_decode(const li_deltanet_layer *L, const float *x, float *y, fl
         out.x = og; out.x_stride = Hv * D; out.gamma = nullptr; out.K = Hv * D; out.eps = 0.f;
         out.n_seg = 1; out.W[0] = L->w_out; out.seg_rows[0] = L->hidden;
         out.dst[0] = y; out.dst_stride[0] = L->hidden;
+        out.accumulate = accumulate;
         return qgemv_launch(out, n_seqs, s, true);
     }
 
@@ -616,10 +619,11 @@ static int layer_decode(const li_deltanet_layer *L, const float *x, float *y, fl
     out.W[0] = L->w_out; out.n_seg = 1; out.seg_rows[0] = L->hidden; out.dst[0] = y;
     out.dst_stride[0] = L->hidden; out.X16 = og16; out.xscale = nullptr;
     out.partials = partials;
+    out.accumulate = accumulate;
     out.x_npad = tc_gemm_x_npad(out);
     a.o_gated16 = og16;
     a.og16_npad = out.x_npad;
-    if (tc_gemm_splits_k(out)) {
+    if (tc_gemm_splits_k(out) && !accumulate) {
         a.zero_out = y;
         a.zero_len = (int64_t)n_seqs * L->hidden;
     }
@@ -646,6 +650,13 @@ int li_launch_deltanet_layer_decode_f16state(const li_deltanet_layer *L, const f
 }
 
 }  // extern "C"
+
+int li::deltanet_layer_decode_residual(const li_deltanet_layer *L, const float *x, float *y, float *conv_state,
+                                       float *state, int n_seqs, void *workspace, size_t workspace_bytes,
+                                       void *stream) {
+    if (!state) return LI_ERR_BAD_ARG;
+    return layer_decode(L, x, y, conv_state, state, nullptr, n_seqs, workspace, workspace_bytes, stream, true);
+}
 
 // ---------------------------------------------------------------------------
 // Layer decode with scratch in this library's own device memory.

@@ -354,7 +354,8 @@ qgemv_kernel(QGemvArgs a) {
                 while (m < a.n_seg - 1 && lr >= a.seg_rows[m]) lr -= a.seg_rows[m++];
                 float *d = m == 0 ? a.dst[0] : (m == 1 ? a.dst[1] : a.dst[2]);
                 const int ds = m == 0 ? a.dst_stride[0] : (m == 1 ? a.dst_stride[1] : a.dst_stride[2]);
-                d[(size_t)b * ds + lr] = s0;
+                float *o = d + (size_t)b * ds + lr;
+                *o = a.accumulate ? *o + s0 : s0;
             } else {  // kEpiConv: DeltaNet in-projection epilogue
                 float out = s0;
                 if (row < a.conv_channels) {
@@ -639,7 +640,8 @@ __global__ void __launch_bounds__(kRowThreads, 1) qgemv_row_kernel(QGemvArgs a, 
                 while (m < a.n_seg - 1 && lr >= a.seg_rows[m]) lr -= a.seg_rows[m++];
                 float *d = m == 0 ? a.dst[0] : (m == 1 ? a.dst[1] : a.dst[2]);
                 const int ds = m == 0 ? a.dst_stride[0] : (m == 1 ? a.dst_stride[1] : a.dst_stride[2]);
-                d[(size_t)my_b * ds + lr] = s0;
+                float *o = d + (size_t)my_b * ds + lr;
+                *o = a.accumulate ? *o + s0 : s0;
             } else {   // kEpiConv: DeltaNet in-projection epilogue
                 float out = s0;
                 if (row < a.conv_channels) {
@@ -1034,9 +1036,12 @@ size_t li_fused_ffn_workspace_size(int K, int N, int n_rows) {
     return b;
 }
 
-int li_launch_fused_ffn_q(int wtype, const float *x, const float *gamma, const void *Wg,
-                          const void *Wu, const void *Wd, float *y, int K, int N, int n_rows,
-                          float eps, void *workspace, size_t workspace_bytes, void *stream) {
+}  // extern "C"
+
+// accumulate: y += ffn(x) (the down projection adds into y).
+static int fused_ffn(int wtype, const float *x, const float *gamma, const void *Wg, const void *Wu, const void *Wd,
+                     float *y, int K, int N, int n_rows, float eps, void *workspace, size_t workspace_bytes,
+                     void *stream, bool accumulate) {
     int rc = common_q_checks(wtype, x, Wg, y, K, N, n_rows);
     if (!rc) rc = common_q_checks(wtype, x, Wu, y, K, N, n_rows);
     if (!rc) rc = common_q_checks(wtype, x, Wd, y, N, K, n_rows);
@@ -1061,8 +1066,9 @@ int li_launch_fused_ffn_q(int wtype, const float *x, const float *gamma, const v
         d.wtype = wtype; d.epi = kTcStore; d.K = N; d.total_rows = K; d.B = n_rows;
         d.W[0] = Wd; d.n_seg = 1; d.seg_rows[0] = K; d.dst[0] = y; d.dst_stride[0] = K;
         d.X16 = h16; d.xscale = hs; d.partials = partials;
+        d.accumulate = accumulate;
         d.x_npad = tc_gemm_x_npad(d);
-        if (tc_gemm_splits_k(d)) {   // the down projection adds K-split partials into y
+        if (tc_gemm_splits_k(d) && !accumulate) {   // the down projection adds K-split partials into y
             const cudaError_t e = cudaMemsetAsync(y, 0, (size_t)n_rows * K * sizeof(float), s);
             if (e != cudaSuccess) return (int)e;
         }
@@ -1088,7 +1094,18 @@ int li_launch_fused_ffn_q(int wtype, const float *x, const float *gamma, const v
     if ((rc = qgemv_plan(wtype, N, K, kEpiStore, &dn.plan))) return rc;
     dn.x = h; dn.x_stride = N; dn.gamma = nullptr; dn.K = N; dn.eps = 0.f;
     dn.n_seg = 1; dn.W[0] = Wd; dn.seg_rows[0] = K; dn.dst[0] = y; dn.dst_stride[0] = K;
+    dn.accumulate = accumulate;
     return qgemv_launch(dn, n_rows, s, true);
 }
 
-}  // extern "C"
+extern "C" int li_launch_fused_ffn_q(int wtype, const float *x, const float *gamma, const void *Wg,
+                                     const void *Wu, const void *Wd, float *y, int K, int N, int n_rows,
+                                     float eps, void *workspace, size_t workspace_bytes, void *stream) {
+    return fused_ffn(wtype, x, gamma, Wg, Wu, Wd, y, K, N, n_rows, eps, workspace, workspace_bytes, stream, false);
+}
+
+int li::fused_ffn_q_residual(int wtype, const float *x, const float *gamma, const void *Wg, const void *Wu,
+                             const void *Wd, float *y, int K, int N, int n_rows, float eps, void *workspace,
+                             size_t workspace_bytes, void *stream) {
+    return fused_ffn(wtype, x, gamma, Wg, Wu, Wd, y, K, N, n_rows, eps, workspace, workspace_bytes, stream, true);
+}

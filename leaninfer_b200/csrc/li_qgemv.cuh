@@ -35,6 +35,9 @@ struct QGemvArgs {
     const float *conv_w;     // [conv_channels][4]
     float *conv_state;       // [n_rows][conv_channels][3]
     int conv_channels;
+    // kEpiStore: 1 adds the result to what dst holds (a residual update,
+    // dst[b][row] += acc) instead of overwriting it
+    int accumulate;
 };
 
 int qgemv_plan(int wtype, int K, int total_rows, int epi, QGemvPlan *p);

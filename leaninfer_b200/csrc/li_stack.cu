@@ -10,6 +10,9 @@
 //     x += ffn(x)            li_launch_fused_ffn_q (RMSNorm + SwiGLU + down),
 //                            or li_launch_ffn_q_tp over a communicator when the
 //                            FFN weights are sharded across GPUs
+// The mixers and the unsharded FFN run in their residual forms: their output
+// projection adds its result into x, so no residual-add kernel runs between
+// them (the sharded FFN's result is added by li_launch_add_f32).
 // Every launch goes to the caller's stream; the host loop only issues them
 // (nothing synchronises), so a whole step can be captured into one CUDA graph.
 // Embeddings and the output head are not part of the stack.
@@ -93,24 +96,26 @@ int li_launch_stack_decode(const li_stack_layer *layers, int n_layers, float *x,
     char *ws = reinterpret_cast<char *>(workspace) + al256((size_t)n * 4);
     const size_t ws_bytes = workspace_bytes - al256((size_t)n * 4);
     int rc;
+    // The residual adds ride on the output projections: each mixer and each
+    // unsharded FFN adds its result into x (x += f(x)); the sharded FFN's
+    // reduce-scatter lands in t, added by a kernel of its own.
     for (int i = 0; i < n_layers; ++i) {
         const li_stack_layer &l = layers[i];
         if (l.kind == LI_LAYER_DELTANET)
-            rc = li_launch_deltanet_layer_decode(l.deltanet, x, t, l.conv_state, l.state, n_seqs, ws, ws_bytes,
-                                                 stream);
+            rc = deltanet_layer_decode_residual(l.deltanet, x, x, l.conv_state, l.state, n_seqs, ws, ws_bytes, stream);
         else
-            rc = li_launch_attn_layer_decode(l.attn, x, t, l.k_cache, l.v_cache, pos, n_seqs, max_ctx, ws, ws_bytes,
-                                             stream);
+            rc = attn_layer_decode_residual(l.attn, x, x, l.k_cache, l.v_cache, pos, n_seqs, max_ctx, ws, ws_bytes,
+                                            stream);
         if (rc) return rc;
-        if ((rc = li_launch_add_f32(x, x, t, n, stream))) return rc;
-        if (tp_nranks > 1)
+        if (tp_nranks > 1) {
             rc = li_launch_ffn_q_tp(l.ffn.wtype, x, l.ffn.norm_w, l.ffn.w_gate, l.ffn.w_up, l.ffn.w_down, t, hidden,
                                     l.ffn.n_inner, n_seqs, l.ffn.eps, tp_comm, tp_nranks, ws, ws_bytes, stream);
-        else
-            rc = li_launch_fused_ffn_q(l.ffn.wtype, x, l.ffn.norm_w, l.ffn.w_gate, l.ffn.w_up, l.ffn.w_down, t, hidden,
-                                       l.ffn.n_inner, n_seqs, l.ffn.eps, ws, ws_bytes, stream);
+            if (!rc) rc = li_launch_add_f32(x, x, t, n, stream);
+        } else {
+            rc = fused_ffn_q_residual(l.ffn.wtype, x, l.ffn.norm_w, l.ffn.w_gate, l.ffn.w_up, l.ffn.w_down, x, hidden,
+                                      l.ffn.n_inner, n_seqs, l.ffn.eps, ws, ws_bytes, stream);
+        }
         if (rc) return rc;
-        if ((rc = li_launch_add_f32(x, x, t, n, stream))) return rc;
     }
     return 0;
 }

@@ -657,7 +657,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__
                     a.dst[0][(size_t)b * a.dst_stride[0] + row] = silu(v) * u;
                 } else if (EPI == kTcStore || split_k) {
                     float *d = dseg + (size_t)b * dstride + row;
-                    if (split_k) atomicAdd(d, v); else *d = v;
+                    if (split_k) atomicAdd(d, v); else *d = a.accumulate ? *d + v : v;
                 } else {
                     float out = v;
                     if (conv_row) {
@@ -1006,6 +1006,10 @@ __global__ void __launch_bounds__(256) tcx_reduce_kernel(TcArgs a, int nchunk, i
         for (int e = 0; e < 3; ++e)
             reinterpret_cast<float4 *>(cs)[e] = make_float4(ns[4 * e], ns[4 * e + 1], ns[4 * e + 2], ns[4 * e + 3]);
     }
+    if (EPI == kTcStore && a.accumulate) {
+        const float4 o = *reinterpret_cast<const float4 *>(dst);
+        r[0] = o.x + r[0]; r[1] = o.y + r[1]; r[2] = o.z + r[2]; r[3] = o.w + r[3];
+    }
     *reinterpret_cast<float4 *>(dst) = make_float4(r[0], r[1], r[2], r[3]);
 }
 
@@ -1035,20 +1039,42 @@ __global__ void __launch_bounds__(256) tc_conv_finish_kernel(TcArgs a) {
 // ---------------------------------------------------------------------------
 // x -> f16 with optional RMSNorm and a per-row power-of-two scale
 // ---------------------------------------------------------------------------
+// NV > 0: the row's K/4 float4 words (at most 256*NV) are loaded once, all
+// before the first reduction, and kept in registers for the conversion (one
+// memory round trip per row instead of two dependent passes); NV = 0 re-reads
+// x in a second pass for longer rows. Both give the same bits: every thread
+// visits its words in the same order either way.
+template <int NV>
 __global__ void __launch_bounds__(256)
 tc_prep_kernel(const float *__restrict__ x, int x_stride, const float *__restrict__ gamma, float eps, int K,
                __half *__restrict__ X16, float *__restrict__ xscale, int x_npad) {
     __shared__ float s_sq[8], s_mx[8];
-    const int b = blockIdx.x, t = threadIdx.x;
+    const int b = blockIdx.x, t = threadIdx.x, n4 = K / 4;
     grid_dep_wait();
     const float4 *x4 = reinterpret_cast<const float4 *>(x + (size_t)b * x_stride);
     const float4 *g4 = reinterpret_cast<const float4 *>(gamma);
     float sq = 0.f, mx = 0.f;
-    for (int i = t; i < K / 4; i += 256) {
-        const float4 v = x4[i];
-        sq = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, sq))));
-        float4 g = gamma ? g4[i] : make_float4(1.f, 1.f, 1.f, 1.f);
-        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x * g.x), fabsf(v.y * g.y)), fmaxf(fabsf(v.z * g.z), fabsf(v.w * g.w))));
+    float4 vg[NV > 0 ? NV : 1];           // x * gamma of this thread's words
+    if constexpr (NV > 0) {
+        float4 v[NV];
+#pragma unroll
+        for (int j = 0; j < NV; ++j)
+            if (t + 256 * j < n4) v[j] = x4[t + 256 * j];
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            if (t + 256 * j >= n4) break;
+            sq = fmaf(v[j].x, v[j].x, fmaf(v[j].y, v[j].y, fmaf(v[j].z, v[j].z, fmaf(v[j].w, v[j].w, sq))));
+            const float4 g = gamma ? g4[t + 256 * j] : make_float4(1.f, 1.f, 1.f, 1.f);
+            vg[j] = make_float4(v[j].x * g.x, v[j].y * g.y, v[j].z * g.z, v[j].w * g.w);
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(vg[j].x), fabsf(vg[j].y)), fmaxf(fabsf(vg[j].z), fabsf(vg[j].w))));
+        }
+    } else {
+        for (int i = t; i < n4; i += 256) {
+            const float4 v = x4[i];
+            sq = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, sq))));
+            float4 g = gamma ? g4[i] : make_float4(1.f, 1.f, 1.f, 1.f);
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x * g.x), fabsf(v.y * g.y)), fmaxf(fabsf(v.z * g.z), fabsf(v.w * g.w))));
+        }
     }
     sq = warp_sum(sq);
 #pragma unroll
@@ -1064,15 +1090,24 @@ tc_prep_kernel(const float *__restrict__ x, int x_stride, const float *__restric
     if (m > 0.f) { frexpf(m, &e); e -= 14; }
     const float s = ldexpf(1.0f, e), inv = ldexpf(1.0f, -e) * r;
     if (t == 0) xscale[b] = s;
-    for (int i = t; i < K / 4; i += 256) {
-        const float4 v = x4[i];
-        const float4 g = gamma ? g4[i] : make_float4(1.f, 1.f, 1.f, 1.f);
-        const __half2 lo = __floats2half2_rn(v.x * g.x * inv, v.y * g.y * inv);
-        const __half2 hi = __floats2half2_rn(v.z * g.z * inv, v.w * g.w * inv);
+    auto put = [&](int i, float4 w) {
+        const __half2 lo = __floats2half2_rn(w.x * inv, w.y * inv);
+        const __half2 hi = __floats2half2_rn(w.z * inv, w.w * inv);
         // four consecutive k stay together in either layout (8 bytes)
         __half *dst = X16 + (x_npad ? tiled_x_offset(b, 4 * i, x_npad) : (size_t)b * K + 4 * i);
         *reinterpret_cast<uint2 *>(dst) = make_uint2(*reinterpret_cast<const uint32_t *>(&lo),
                                                      *reinterpret_cast<const uint32_t *>(&hi));
+    };
+    if constexpr (NV > 0) {
+#pragma unroll
+        for (int j = 0; j < NV; ++j)
+            if (t + 256 * j < n4) put(t + 256 * j, vg[j]);
+    } else {
+        for (int i = t; i < n4; i += 256) {
+            const float4 v = x4[i];
+            const float4 g = gamma ? g4[i] : make_float4(1.f, 1.f, 1.f, 1.f);
+            put(i, make_float4(v.x * g.x, v.y * g.y, v.z * g.z, v.w * g.w));
+        }
     }
 }
 
@@ -1375,8 +1410,22 @@ int tc_prep_launch(const float *x, int x_stride, const float *gamma, float eps, 
                    float *xscale, cudaStream_t stream, bool pdl, int x_npad) {
     if (K % 8 || !aligned16(x) || (gamma && !aligned16(gamma)) || !aligned16(X16)) return LI_ERR_MISALIGNED;
     if (x_npad && (x_npad < B || x_npad % 8 || K % 64)) return LI_ERR_BAD_SHAPE;
-    return (int)launch_pdl(tc_prep_kernel, dim3((unsigned)B), dim3(256), 0, stream, pdl, x, x_stride, gamma, eps,
-                           K, X16, xscale, x_npad);
+    const int nv = (K / 4 + 255) / 256;   // float4 words per thread
+    const dim3 grid((unsigned)B), block(256);
+    if (nv <= 4)
+        return (int)launch_pdl(tc_prep_kernel<4>, grid, block, 0, stream, pdl, x, x_stride, gamma, eps, K, X16, xscale,
+                               x_npad);
+    if (nv <= 8)
+        return (int)launch_pdl(tc_prep_kernel<8>, grid, block, 0, stream, pdl, x, x_stride, gamma, eps, K, X16, xscale,
+                               x_npad);
+    if (nv <= 12)
+        return (int)launch_pdl(tc_prep_kernel<12>, grid, block, 0, stream, pdl, x, x_stride, gamma, eps, K, X16,
+                               xscale, x_npad);
+    if (nv <= 20)
+        return (int)launch_pdl(tc_prep_kernel<20>, grid, block, 0, stream, pdl, x, x_stride, gamma, eps, K, X16,
+                               xscale, x_npad);
+    return (int)launch_pdl(tc_prep_kernel<0>, grid, block, 0, stream, pdl, x, x_stride, gamma, eps, K, X16, xscale,
+                           x_npad);
 }
 
 bool tc_gemm_splits_k(const TcArgs &a) {

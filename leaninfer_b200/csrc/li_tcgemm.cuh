@@ -36,6 +36,10 @@ struct TcArgs {
     // fp32 scratch of tc_gemm_partials_bytes() for the X-stationary kernel
     // (batch <= 64); nullptr keeps the one-tile-per-CTA kernel
     float *partials;
+    // kTcStore: 1 adds the result to what dst holds (a residual update); a
+    // K-split GEMM then adds its partial sums onto dst instead of a zeroed
+    // output
+    int accumulate;
 };
 
 // Tiled X for the X-stationary kernel: [K/64][npad rows][64 k] f16, each
