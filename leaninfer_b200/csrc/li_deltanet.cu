@@ -189,6 +189,14 @@ recurrent_kernel(RecArgs a) {
             for (int64_t i = z0 + threadIdx.x; i < z1; i += blockDim.x) a.zero_out[i] = 0.f;
         }
     }
+    // Layer mode (one token): this thread's projected v and z are loaded now,
+    // next to q and k, so the token's phases wait for no further global load.
+    float v_pre = 0.f, z_pre = 0.f;
+    if (LAYER && threadIdx.x < RB) {
+        const float *pr = a.proj + (size_t)seq * a.NI + h * D + row0 + threadIdx.x;
+        v_pre = pr[2 * a.Hk * D];
+        z_pre = pr[a.C];
+    }
 
     for (int64_t t = 0; t < a.n_tokens; ++t) {
         float beta_s, decay;
@@ -268,7 +276,7 @@ recurrent_kernel(RecArgs a) {
             if (!LAYER)
                 vv = a.v[seq * a.vnb3 + h * a.vnb2 + t * a.vnb1 + row0 + r];
             else
-                vv = a.proj[(size_t)seq * a.NI + 2 * a.Hk * D + h * D + row0 + r];
+                vv = v_pre;
             const float vn = beta_s * (vv - u * decay);
             o = w * decay + vn * attn;
             s_vp[r] = vn;
@@ -303,7 +311,7 @@ recurrent_kernel(RecArgs a) {
             if (threadIdx.x < RB) {
                 const int r = threadIdx.x;
                 const float rs = rsqrtf(tot / (float)D + a.norm_eps);
-                const float z = a.proj[(size_t)seq * a.NI + a.C + h * D + row0 + r];
+                const float z = z_pre;
                 const float og = silu(z) * (o * a.norm_w[row0 + r] * rs);
                 const size_t oi = ((size_t)seq * a.n_heads + h) * D + row0 + r;
                 if (a.o_gated16)
