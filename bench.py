@@ -172,6 +172,54 @@ def chained_graphs(insts: list, launch, steps: int):
     return run
 
 
+def pipelined_e2e(n_inst: int, steps: int, copy_in, replay, copy_out) -> float:
+    """End-to-end milliseconds of `steps` steps over the rotating instances,
+    each step copying its input in from pinned host memory (copy_in(j)),
+    running (replay(j)) and copying its result out (copy_out(j)), as a serving
+    loop double-buffers them: host-to-device copies on one stream,
+    device-to-host copies on another, the steps on the current stream, so the
+    copies of one step overlap the computation of its neighbours. Instance j's
+    input goes in once its previous result is out (the result may live in the
+    input buffer), the step waits for its input, its result goes out after
+    it. The CUDA-event interval covers every copy."""
+    import torch
+    stream = torch.cuda.current_stream()
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    ready = [torch.cuda.Event() for _ in range(n_inst)]     # input j copied in
+    done = [torch.cuda.Event() for _ in range(n_inst)]      # step on instance j finished
+    out = [torch.cuda.Event() for _ in range(n_inst)]       # result j copied out
+
+    def one(i: int):
+        j = i % n_inst
+        with torch.cuda.stream(h2d):
+            if i >= n_inst:
+                h2d.wait_event(out[j])
+            copy_in(j)
+            ready[j].record(h2d)
+        stream.wait_event(ready[j])
+        replay(j)
+        done[j].record(stream)
+        with torch.cuda.stream(d2h):
+            d2h.wait_event(done[j])
+            copy_out(j)
+            out[j].record(d2h)
+
+    for i in range(min(3, steps)):
+        one(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    h2d.wait_event(e0)
+    d2h.wait_event(e0)
+    for i in range(steps):
+        one(i)
+    stream.wait_stream(h2d)
+    stream.wait_stream(d2h)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1)
+
+
 # --------------------------------------------------------------------------
 # our arm
 # --------------------------------------------------------------------------
@@ -272,46 +320,12 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
     for i in range(n_inst):
         hx[i].copy_(insts[i]["x"].cpu())
     e_steps = max(1, min(args.steps, 200))
-    # Copies run on their own stream, overlapped with the neighbouring steps'
-    # compute as a serving loop would: x of instance j goes in once j's
-    # previous step has finished, the step waits for its x and for the
-    # previous read-out of its y, and y comes out after the step.
-    copy = torch.cuda.Stream()
-    ready = [torch.cuda.Event() for _ in range(n_inst)]     # x_j copied in
-    done = [torch.cuda.Event() for _ in range(n_inst)]      # step on instance j finished
-    out = [torch.cuda.Event() for _ in range(n_inst)]       # y_j copied out
-
-    def e2e_step(i: int):
-        j = i % n_inst
-        it = insts[j]
-        with torch.cuda.stream(copy):
-            if i >= n_inst:
-                copy.wait_event(done[j])
-            it["x"].copy_(hx[j], non_blocking=True)
-            ready[j].record(copy)
-        stream.wait_event(ready[j])
-        if i >= n_inst:
-            stream.wait_event(out[j])
-        it["graph"].replay()
-        done[j].record(stream)
-        with torch.cuda.stream(copy):
-            copy.wait_event(done[j])
-            hy[j].copy_(it["y"], non_blocking=True)
-            out[j].record(copy)
-
-    for i in range(3):
-        e2e_step(i)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
-    e0.record(stream)
-    copy.wait_event(e0)
-    for i in range(e_steps):
-        e2e_step(i)
-    stream.wait_stream(copy)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
+    e2e_ms = pipelined_e2e(n_inst, e_steps, lambda j: insts[j]["x"].copy_(hx[j], non_blocking=True),
+                           lambda j: insts[j]["graph"].replay(),
+                           lambda j: hy[j].copy_(insts[j]["y"], non_blocking=True))
     if dist:
         dist.barrier()
 
@@ -641,22 +655,13 @@ def run_gemv(args, rank: int, world: int, dist) -> dict | None:
     ho = [[o.cpu().pin_memory() for o in outs(it)] for it in insts]
     e_steps = max(1, min(args.steps, 200))
 
-    def e2e_step(i: int):
-        it = insts[i % n_inst]
-        it["x"].copy_(hx[i % n_inst], non_blocking=True)
-        it["graph"].replay()
-        for h, o in zip(ho[i % n_inst], outs(it)):
+    def copy_out(j: int):
+        for h, o in zip(ho[j], outs(insts[j])):
             h.copy_(o, non_blocking=True)
 
-    for i in range(3):
-        e2e_step(i)
     torch.cuda.synchronize()
-    e0.record(stream)
-    for i in range(e_steps):
-        e2e_step(i)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
+    e2e_ms = pipelined_e2e(n_inst, e_steps, lambda j: insts[j]["x"].copy_(hx[j], non_blocking=True),
+                           lambda j: insts[j]["graph"].replay(), copy_out)
     status = ops.device_status()
     if status:
         raise RuntimeError(f"device status {status} after the timed region")
@@ -1076,15 +1081,9 @@ def run_layerffn(args, rank: int, world: int, dist) -> dict | None:
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
-    e0.record(stream)
-    for i in range(e_steps):
-        it = insts[i % n_inst]
-        it["x"].copy_(hx[i % n_inst], non_blocking=True)
-        it["graph"].replay()
-        hy[i % n_inst].copy_(it["x"], non_blocking=True)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
+    e2e_ms = pipelined_e2e(n_inst, e_steps, lambda j: insts[j]["x"].copy_(hx[j], non_blocking=True),
+                           lambda j: insts[j]["graph"].replay(),
+                           lambda j: hy[j].copy_(insts[j]["x"], non_blocking=True))
     if dist:
         dist.barrier()
     ms, e2e_ms = max_over_ranks([ms, e2e_ms], dist, device=dev)
