@@ -843,7 +843,7 @@ int project(bool simt, int wtype, const void *W, int K, int N, const float *x, c
     t.x_npad = tc_gemm_x_npad(t);
     // a dependent launch also as the layer's first kernel: the prep waits for the previous kernel before it reads x
     if ((rc = tc_prep_launch(x, K, gamma, eps, B, K, const_cast<__half *>(t.X16), const_cast<float *>(t.xscale), s,
-                             true, t.x_npad)))
+                             true, t.x_npad, tc_gemm_x_stationary(t))))
         return rc;
     if (tc_gemm_splits_k(t) && !accumulate) {
         // the K-split CTAs add into dst; ordered after the prep by the stream

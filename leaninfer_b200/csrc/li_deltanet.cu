@@ -619,7 +619,7 @@ static int layer_decode(const li_deltanet_layer *L, const float *x, float *y, fl
     }
     // a dependent launch: the prep waits for the previous kernel before it reads x
     if ((rc = tc_prep_launch(x, L->hidden, L->in_norm_w, L->in_norm_eps, n_seqs, L->hidden, x16, xscale, s,
-                             true, in.x_npad)))
+                             true, in.x_npad, tc_gemm_x_stationary(in))))
         return rc;
     if ((rc = tc_gemm_launch(in, s, true))) return rc;
     TcArgs out = {};

@@ -1077,9 +1077,11 @@ static int fused_ffn(int wtype, const float *x, const float *gamma, const void *
         g.W[0] = Wg; g.W[1] = Wu; g.n_seg = 1; g.seg_rows[0] = N; g.dst[0] = h; g.dst_stride[0] = N;
         g.X16 = x16; g.xscale = xs; g.partials = partials;
         g.x_npad = tc_gemm_x_npad(g);
-        if ((rc = tc_prep_launch(x, K, gamma, eps, n_rows, K, x16, xs, s, true, g.x_npad))) return rc;
+        if ((rc = tc_prep_launch(x, K, gamma, eps, n_rows, K, x16, xs, s, true, g.x_npad, tc_gemm_x_stationary(g))))
+            return rc;
         if ((rc = tc_gemm_launch(g, s, true))) return rc;
-        if ((rc = tc_prep_launch(h, N, nullptr, 0.f, n_rows, N, h16, hs, s, true, d.x_npad))) return rc;
+        if ((rc = tc_prep_launch(h, N, nullptr, 0.f, n_rows, N, h16, hs, s, true, d.x_npad, tc_gemm_x_stationary(d))))
+            return rc;
         return tc_gemm_launch(d, s, true);
     }
     QGemvArgs a = {};

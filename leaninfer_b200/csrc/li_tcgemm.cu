@@ -1047,9 +1047,12 @@ __global__ void __launch_bounds__(256) tc_conv_finish_kernel(TcArgs a) {
 template <int NV>
 __global__ void __launch_bounds__(256)
 tc_prep_kernel(const float *__restrict__ x, int x_stride, const float *__restrict__ gamma, float eps, int K,
-               __half *__restrict__ X16, float *__restrict__ xscale, int x_npad) {
+               __half *__restrict__ X16, float *__restrict__ xscale, int x_npad, int early_dependents) {
     __shared__ float s_sq[8], s_mx[8];
     const int b = blockIdx.x, t = threadIdx.x, n4 = K / 4;
+    // An X-stationary GEMM after this kernel may launch at once: it streams
+    // its weights meanwhile and waits for this kernel before it reads X16.
+    if (early_dependents) grid_dep_launch_dependents();
     grid_dep_wait();
     const float4 *x4 = reinterpret_cast<const float4 *>(x + (size_t)b * x_stride);
     const float4 *g4 = reinterpret_cast<const float4 *>(gamma);
@@ -1407,25 +1410,25 @@ int launch_kernel(const CUtensorMap *maps, const TcArgs &a, const TcPlan &p, cud
 }  // namespace
 
 int tc_prep_launch(const float *x, int x_stride, const float *gamma, float eps, int B, int K, __half *X16,
-                   float *xscale, cudaStream_t stream, bool pdl, int x_npad) {
+                   float *xscale, cudaStream_t stream, bool pdl, int x_npad, bool early_dependents) {
     if (K % 8 || !aligned16(x) || (gamma && !aligned16(gamma)) || !aligned16(X16)) return LI_ERR_MISALIGNED;
     if (x_npad && (x_npad < B || x_npad % 8 || K % 64)) return LI_ERR_BAD_SHAPE;
     const int nv = (K / 4 + 255) / 256;   // float4 words per thread
     const dim3 grid((unsigned)B), block(256);
     if (nv <= 4)
         return (int)launch_pdl(tc_prep_kernel<4>, grid, block, 0, stream, pdl, x, x_stride, gamma, eps, K, X16, xscale,
-                               x_npad);
+                               x_npad, (int)early_dependents);
     if (nv <= 8)
         return (int)launch_pdl(tc_prep_kernel<8>, grid, block, 0, stream, pdl, x, x_stride, gamma, eps, K, X16, xscale,
-                               x_npad);
+                               x_npad, (int)early_dependents);
     if (nv <= 12)
         return (int)launch_pdl(tc_prep_kernel<12>, grid, block, 0, stream, pdl, x, x_stride, gamma, eps, K, X16,
-                               xscale, x_npad);
+                               xscale, x_npad, (int)early_dependents);
     if (nv <= 20)
         return (int)launch_pdl(tc_prep_kernel<20>, grid, block, 0, stream, pdl, x, x_stride, gamma, eps, K, X16,
-                               xscale, x_npad);
+                               xscale, x_npad, (int)early_dependents);
     return (int)launch_pdl(tc_prep_kernel<0>, grid, block, 0, stream, pdl, x, x_stride, gamma, eps, K, X16, xscale,
-                           x_npad);
+                           x_npad, (int)early_dependents);
 }
 
 bool tc_gemm_splits_k(const TcArgs &a) {
@@ -1435,6 +1438,13 @@ bool tc_gemm_splits_k(const TcArgs &a) {
     if (planx(c, &px, false) == 0) return false;   // the X-stationary kernel stores whole sums
     TcPlan p;
     return plan(a, &p) == 0 && p.ks > 1;
+}
+
+bool tc_gemm_x_stationary(const TcArgs &a) {
+    TcArgs c = a;
+    if (!c.X16) c.X16 = reinterpret_cast<const __half *>(c.partials);
+    TcxPlan px;
+    return planx(c, &px, false) == 0;
 }
 
 int tc_gemm_x_npad(const TcArgs &a) {

@@ -55,8 +55,13 @@ __host__ __device__ inline size_t tiled_x_offset(int b, int k, int npad) {
 // x[b] (fp32) -> X16[b] = f16(rmsnorm?(x[b]) / s_b), xscale[b] = s_b (a power
 // of two that keeps the row inside f16 range). gamma == nullptr: no norm.
 // x_npad > 0 writes X16 tiled (tiled_x_offset), else row-major [B][K].
+// early_dependents: the kernel lets its dependent launch at entry, for the
+// X-stationary GEMM only (tc_gemm_x_stationary), which then streams and
+// dequantizes its weights while the prep runs; its reduce kernel waits for it
+// before letting anything after it launch.
 int tc_prep_launch(const float *x, int x_stride, const float *gamma, float eps, int B, int K,
-                   __half *X16, float *xscale, cudaStream_t stream, bool pdl, int x_npad = 0);
+                   __half *X16, float *xscale, cudaStream_t stream, bool pdl, int x_npad = 0,
+                   bool early_dependents = false);
 
 // One launch covers all batch rows (up to 256); returns LI_ERR_* / cudaError_t.
 // kTcStore and kTcConv launches may split K over several CTAs per tile and
@@ -73,5 +78,7 @@ size_t tc_gemm_partials_bytes(int wtype, int epi, int K, int rows_total, int B);
 // Rows of the tiled X (x_npad) the launch with these arguments (X16 and
 // x_npad aside) will use the X-stationary kernel with, or 0 when it will not.
 int tc_gemm_x_npad(const TcArgs &a);
+// True when this GEMM runs on the X-stationary kernel (K chunks + reduce).
+bool tc_gemm_x_stationary(const TcArgs &a);
 
 }  // namespace li
