@@ -21,8 +21,8 @@
 // kernel (cuda/leaninfer-fused-deltanet.cu:217-288): q~ = q*D^-1/2,
 // beta = sigmoid, decay = exp(min(g,50)), clamp to +-1e6.
 //
-// Layer decode = three stream-ordered kernels, the 2nd and 3rd launched as
-// programmatic dependents so they start while their predecessor drains:
+// Layer decode = three stream-ordered kernels, each launched as a
+// programmatic dependent so it starts while its predecessor drains:
 //   1. in-projection GEMV (li_qgemv.cu) with the causal-conv1d + SiLU
 //      epilogue that also shifts the conv state;
 //   2. this file's recurrence in layer mode: q/k L2 norm, beta, g from the
@@ -30,8 +30,11 @@
 //      (reference cuda/leaninfer-fused-gate.cu:39-85) into the workspace;
 //   3. out-projection GEMV (li_qgemv.cu) of the gated heads.
 // Kernel 2 reads its state before griddepcontrol.wait; this is safe because
-// kernel 1 is launched without the programmatic attribute, so by the time
-// kernel 2 runs the previous step's kernels have all completed.
+// the GEMV kernels let their dependents launch only after their own
+// griddepcontrol.wait: kernel 2 starts once kernel 1's predecessor (the
+// previous step's last kernel, which itself waited for the previous
+// recurrence) has completed. (The tensor-core path gets the same order from
+// its x prep, which lets the GEMM after it launch only when it completes.)
 #include "li_common.cuh"
 #include "li_qgemv.cuh"
 #include "li_tcgemm.cuh"
@@ -569,7 +572,8 @@ static int layer_decode(const li_deltanet_layer *L, const float *x, float *y, fl
 
     if (!tc) {
         float *og = (float *)(ws + al256((size_t)NI * n * 4));
-        // 1. in-projection + conv1d/SiLU epilogue (not a dependent launch)
+        // 1. in-projection + conv1d/SiLU epilogue (dependent launch: weights
+        //    and the conv state are read before its wait, x after it)
         QGemvArgs in = {};
         in.wtype = L->w_in_type; in.epi = kEpiConv;
         if ((rc = qgemv_plan(L->w_in_type, L->hidden, NI, kEpiConv, &in.plan))) return rc;
@@ -577,7 +581,7 @@ static int layer_decode(const li_deltanet_layer *L, const float *x, float *y, fl
         in.eps = L->in_norm_eps; in.n_seg = 1; in.W[0] = L->w_in; in.seg_rows[0] = NI;
         in.dst[0] = proj; in.dst_stride[0] = NI;
         in.conv_w = L->conv_w; in.conv_state = conv_state; in.conv_channels = C;
-        if ((rc = qgemv_launch(in, n_seqs, s, false))) return rc;
+        if ((rc = qgemv_launch(in, n_seqs, s, true))) return rc;
         // 2. recurrence + L2 norm + gated RMSNorm (dependent launch)
         a.o_gated = og;
         rc = launch_layer_rec_any(a, rb, state16 != nullptr, s);

@@ -237,10 +237,12 @@ qgemv_kernel(QGemvArgs a) {
         for (int v = XB; v < p.S; ++v)
             if (stage_of(v) < n_stages) issue(v);
     }
-    // Let a dependent launch start its own weight-independent prologue.
-    grid_dep_launch_dependents();
-    // x depends on the previous kernel in the stream; weights do not.
+    // x depends on the previous kernel in the stream; weights do not. A
+    // dependent launch may start its own prologue once this kernel's
+    // predecessor has completed (the recurrence after a layer's first GEMV
+    // reads its state before its own wait).
     grid_dep_wait();
+    grid_dep_launch_dependents();
 
     // -- x (times gamma) into buffers 0..XB-1, coalesced, padded by one
     //    float per unit so the per-unit reads below are conflict free --
@@ -512,8 +514,13 @@ __global__ void __launch_bounds__(kRowThreads, 1) qgemv_row_kernel(QGemvArgs a, 
     };
 
     if (base < total) load_rows(base);
+    // x may be written by the previous kernel; a dependent launch may start
+    // once that kernel has completed (the recurrence after a layer's first
+    // GEMV reads its state before its own wait). The conv state read above
+    // was last written by this layer's previous step, which had completed
+    // before this kernel's predecessor could trigger it.
+    grid_dep_wait();
     grid_dep_launch_dependents();
-    grid_dep_wait();   // x and the conv state may be written by earlier kernels
     {
         const float4 *g4 = reinterpret_cast<const float4 *>(a.gamma);
         float sq[NB];
@@ -1090,6 +1097,8 @@ static int fused_ffn(int wtype, const float *x, const float *gamma, const void *
     a.x = x; a.x_stride = K; a.gamma = gamma; a.K = K; a.eps = eps;
     a.n_seg = 1; a.W[0] = Wg; a.W[1] = Wu; a.seg_rows[0] = N;
     a.dst[0] = h; a.dst_stride[0] = N;
+    // a plain launch: as a dependent launch (resident during the previous
+    // down projection) the one-row FFN step measured 38.8 us against 30.7
     if ((rc = qgemv_launch(a, n_rows, s, false))) return rc;
     QGemvArgs dn = {};
     dn.wtype = wtype; dn.epi = kEpiStore;
