@@ -910,7 +910,9 @@ static int attn_layer_decode(const li_attn_layer *L, const float *x, float *y, v
     a.og = reinterpret_cast<float *>(ws + lay.og);
     a.scale = 1.0f / sqrtf((float)D);
 
-    // 1. input projection (RMSNorm fused); the first kernel is not a dependent launch
+    // 1. input projection (RMSNorm fused): a plain launch on the few-row path;
+    //    on the tensor-core path its x prep is a dependent launch that waits
+    //    for the previous kernel before it reads x
     if ((rc = project(simt, L->w_in_type, L->w_in, L->hidden, NP, x, L->in_norm_w, L->in_norm_eps, a.proj, n_seqs,
                       ws, lay, true, false, s)))
         return rc;
