@@ -17,8 +17,9 @@
  *   - every pointer is device memory owned by the caller (ggml tensors);
  *     no entry allocates or frees device memory;
  *   - every launch is stream-ordered on `stream` (a cudaStream_t passed as
- *     void*, as in the reference), performs no synchronisation and no host
- *     allocation, and may be captured into a CUDA graph;
+ *     void*, as in the reference) and performs no synchronisation and no
+ *     host allocation; the entries that take their scratch from the caller
+ *     may be captured into a CUDA graph;
  *   - quantized weights are raw ggml blocks, one matrix row after another
  *     (row r of a [N, K] matrix starts at r * li_row_bytes(type, K));
  *   - activations are fp32, row-major [n_rows, K].
